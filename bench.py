@@ -1,0 +1,535 @@
+"""Benchmark of the FP32 operator path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload chain|gemm|layernorm|affine|add]
+                    [--impl ours|reference]
+
+Workloads (synthetic seeded inputs with the shapes and distributions of the
+benchmark configurations; one "step" is one pass of the path over one batch):
+  chain      Y = LayerNorm(X W), X[65536 x 4096] ~ N(0,1), W[4096 x 4096] ~ N(0,1/4096),
+             gamma = 1, beta = 0, eps 1e-5, seed 4; rows sharded over the ranks (the
+             default: the configuration that drives GEMM TFLOP/s, LayerNorm and scaling)
+  gemm       C = A B, M = N = K = 4096, A, B ~ U[-1,1), seed 3; rows sharded
+  layernorm  X[16384 x 4096] ~ N(0,1), gamma ~ N(1,.02), beta ~ N(0,.02), seed 2; rows sharded
+  affine     y = 1.5 x - 0.25, n = 2^26, x ~ U[-4,4), seed 1 (replica per rank)
+  add        c = a + b, n = 2^20, a, b ~ U[-1,1), seed 0 (replica per rank, 16 rotating sets)
+`value` is device time (CUDA events on the library's context stream between two
+queue markers, max over ranks); `e2e` times the same steps through the public API
+with pinned host inputs copied in and results copied out every step. Under
+torchrun every rank drives cuda:LOCAL_RANK; a gloo process group carries only the
+barrier and the max-over-ranks reduction (the path itself has no exchange).
+`--impl reference` times the reference's CPU computation of the path (the
+oracle's restatement of its verifier, all host threads) on a bounded sample.
+"""
+import argparse
+import json
+import math
+import os
+from pathlib import Path
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP32 GEMM TFLOP/s; LayerNorm & affine HBM GB/s at 1/2/4/8 B200"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="chain", choices=("chain", "gemm", "layernorm", "affine", "add"))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+DEFAULT_STEPS = {"chain": 2, "gemm": 20, "layernorm": 50, "affine": 100, "add": 200}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+class Group:
+    def __init__(self, world):
+        self.world = world
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", str(self.rank)))
+        self.dist = None
+        if world > 1 or (int(os.environ.get("WORLD_SIZE", "1")) > 1 and world != 1):
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+            self.dist = dist
+            self.world = dist.get_world_size()
+            self.rank = dist.get_rank()
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def max(self, value):
+        if not self.dist:
+            return value
+        import torch
+        t = torch.tensor([float(value)], dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t.item()
+
+    def close(self):
+        if self.dist:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- clocks during the timed region
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device, self.lines, self.proc = device, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *_):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        mhz, max_mhz, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                max_mhz = float(f[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": max_mhz, "reasons": sorted(reasons), "samples": 0}
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max_mhz, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------- workloads (our implementation)
+class Workload:
+    """Holds device inputs/outputs for one rank and runs steps through the public API."""
+
+    def __init__(self, name, ctx, group):
+        import numpy as np
+        import importlib
+        import paralyn_b200 as p
+        from paralyn_b200 import b200, shard, synthetic
+        self.p, self.np, self.b200, self.shard = p, np, b200, shard
+        self.T = importlib.import_module("paralyn_b200.tensor")
+        self.name, self.ctx, self.group = name, ctx, group
+        self.res = self.T.operators_of(ctx)
+        self.queue = self.res.queue
+        world, rank = group.world, group.rank
+        if name == "chain":
+            self.rows, self.k, self.n = 65536, 4096, 4096
+            self.chain = shard.ChainShard(ctx, self.rows, self.k, self.n, world, rank, seed=4, w_std=1.0 / 64.0)
+            self.chain.fill_synthetic()
+            self.units_total = 2 * self.rows * self.n * self.k
+            self.units_local = self.chain.flops()
+            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "strong"
+            self.metric = "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)"
+            self.config = {"workload": "chain: Y = LayerNorm(X W), X[65536x4096] ~ N(0,1), W[4096x4096] ~ N(0,1/4096), "
+                                       "gamma=1, beta=0, eps=1e-5, seed 4",
+                           "rows": self.rows, "k": self.k, "n": self.n, "rows_per_gpu": self.chain.local_rows,
+                           "parallelism": f"rows{world}", "l2": "inputs larger than L2 (X shard >= 128 MiB)"}
+            self.h2d = 4 * self.chain.local_rows * self.k
+            self.d2h = 4 * self.chain.local_rows * self.n
+        elif name == "gemm":
+            m = n = k = 4096
+            r0, r1 = shard.row_range(m, world, rank)
+            self.m_local, self.n, self.k = r1 - r0, n, k
+            self.a = ctx.buffer(4 * self.m_local * k)
+            self.b = ctx.buffer(4 * k * n)
+            self.c = ctx.buffer(4 * self.m_local * n)
+            fill = b200.fill_synthetic_into
+            for e in (fill(self.queue, self.T.TensorDescriptor(self.a, (self.m_local, k)), seed=3, first_draw=r0 * k),
+                      fill(self.queue, self.T.TensorDescriptor(self.b, (k, n)), seed=3, first_draw=m * k)):
+                e.wait()
+                e.close()
+            self.units_total, self.units_local = 2 * m * n * k, 2 * self.m_local * n * k
+            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "strong"
+            self.metric = "FP32 GEMM TFLOP/s (4096^3, rows sharded)"
+            self.config = {"workload": "gemm: C = A B, M=N=K=4096, A,B ~ U[-1,1), seed 3", "m": m, "n": n, "k": k,
+                           "rows_per_gpu": self.m_local, "parallelism": f"rows{world}",
+                           "l2": "operands are 64 MiB each; A/B re-reads are part of the GEMM"}
+            self.h2d, self.d2h = 4 * self.m_local * k, 4 * self.m_local * n
+        elif name == "layernorm":
+            rows, cols = 16384, 4096
+            r0, r1 = shard.row_range(rows, world, rank)
+            self.rows_local, self.cols = r1 - r0, cols
+            self.x = ctx.buffer(4 * self.rows_local * cols)
+            self.g, self.bt = ctx.buffer(4 * cols), ctx.buffer(4 * cols)
+            self.y = ctx.buffer(4 * self.rows_local * cols)
+            fill = b200.fill_synthetic_into
+            D = self.T.TensorDescriptor
+            for e in (fill(self.queue, D(self.x, (self.rows_local, cols)), seed=2, first_draw=2 * r0 * cols,
+                           distribution=b200.NORMAL, p0=0.0, p1=1.0),
+                      fill(self.queue, D(self.g, (cols,)), seed=2, first_draw=2 * rows * cols,
+                           distribution=b200.NORMAL, p0=1.0, p1=0.02),
+                      fill(self.queue, D(self.bt, (cols,)), seed=2, first_draw=2 * rows * cols + 2 * cols,
+                           distribution=b200.NORMAL, p0=0.0, p1=0.02)):
+                e.wait()
+                e.close()
+            self.units_total = 2 * rows * cols * 4 + 2 * cols * 4 * world
+            self.units_local = 2 * self.rows_local * cols * 4 + 2 * cols * 4
+            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "strong"
+            self.metric = "FP32 row LayerNorm HBM GB/s (16384x4096, rows sharded)"
+            self.config = {"workload": "layernorm: X[16384x4096] ~ N(0,1), gamma ~ N(1,.02), beta ~ N(0,.02), eps 1e-5, seed 2",
+                           "rows_per_gpu": self.rows_local, "cols": cols, "parallelism": f"rows{world}",
+                           "l2": "inputs larger than L2 (256 MiB)"}
+            self.h2d = self.d2h = 4 * self.rows_local * cols
+        elif name == "affine":
+            self.count = 1 << 26
+            self.x = ctx.buffer(4 * self.count)
+            self.y = ctx.buffer(4 * self.count)
+            e = b200.fill_synthetic_into(self.queue, self.T.TensorDescriptor(self.x, (self.count,)), seed=1, p0=4.0)
+            e.wait()
+            e.close()
+            self.module = p.Module.load_file(ctx, p.array.operators_path())
+            self.kernel = self.module.kernel("array_affine_scalar")
+            self.xv, self.yv = self.x.view(access=p.Access.READ), self.y.view(access=p.Access.WRITE)
+            self.units_local = 8 * self.count
+            self.units_total = self.units_local * world
+            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
+            self.metric = "FP32 affine y = 1.5x - 0.25 HBM GB/s (n = 2^26)"
+            self.config = {"workload": "affine: y = alpha x + beta, n = 2^26, x ~ U[-4,4), alpha 1.5, beta -0.25, seed 1",
+                           "bytes_per_element": 8, "parallelism": f"replica{world}",
+                           "l2": "inputs larger than L2 (256 MiB)"}
+            self.h2d = self.d2h = 4 * self.count
+        elif name == "add":
+            self.count, self.sets = 1 << 20, 16
+            self.module = p.Module.load_file(ctx, p.array.operators_path())
+            self.kernel = self.module.kernel("array_add")
+            self.bufs = []
+            for s in range(self.sets):
+                a, b, c = (ctx.buffer(4 * self.count) for _ in range(3))
+                for buf, first in ((a, 0), (b, self.count)):
+                    e = b200.fill_synthetic_into(self.queue, self.T.TensorDescriptor(buf, (self.count,)), seed=0,
+                                                 first_draw=first)
+                    e.wait()
+                    e.close()
+                self.bufs.append((a, b, c, a.view(access=p.Access.READ), b.view(access=p.Access.READ),
+                                  c.view(access=p.Access.WRITE)))
+            self.units_local = 12 * self.count
+            self.units_total = self.units_local * world
+            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
+            self.metric = "FP32 vector add HBM GB/s (n = 2^20)"
+            self.config = {"workload": "add: c = a + b, n = 1,048,576, a,b ~ U[-1,1), seed 0", "bytes_per_element": 12,
+                           "parallelism": f"replica{world}",
+                           "l2": "16 rotating buffer sets (192 MiB) exceed L2"}
+            self.h2d, self.d2h = 8 * self.count, 4 * self.count
+            self.turn = 0
+        self.ctx.synchronize()
+
+    def step(self):
+        """Enqueue one step; returns (events, dominant-kernel event)."""
+        p = self.p
+        if self.name == "chain":
+            mm, ln = self.chain.step()
+            return [mm, ln], mm
+        if self.name == "gemm":
+            D = self.T.TensorDescriptor
+            e = self.T.matmul_into(self.queue, self.res.module, D(self.a, (self.m_local, self.k)), D(self.b, (self.k, self.n)),
+                                   D(self.c, (self.m_local, self.n)), m=self.m_local, n=self.n, k=self.k)
+            return [e], e
+        if self.name == "layernorm":
+            D = self.T.TensorDescriptor
+            e = self.T.layer_norm_into(self.queue, self.res.module, D(self.x, (self.rows_local, self.cols)),
+                                       D(self.g, (self.cols,)), D(self.bt, (self.cols,)),
+                                       D(self.y, (self.rows_local, self.cols)), epsilon=1e-5)
+            return [e], e
+        if self.name == "affine":
+            e = self.queue.launch(self.kernel, [self.xv, self.yv, p.u32(self.count), p.f32(1.5), p.f32(-0.25)],
+                                  grid=((self.count + 255) // 256, 1, 1), block=(256, 1, 1))
+            return [e], e
+        a, b, c, av, bv, cv = self.bufs[self.turn % self.sets]
+        self.turn += 1
+        e = self.queue.launch(self.kernel, [av, bv, cv, p.u32(self.count)], grid=((self.count + 255) // 256, 1, 1),
+                              block=(256, 1, 1))
+        return [e], e
+
+    def io_buffers(self):
+        """(device buffer written from host, device buffer read back) for the e2e leg."""
+        if self.name == "chain":
+            return [(self.chain.x, self.h2d)], (self.chain.y, self.d2h)
+        if self.name == "gemm":
+            return [(self.a, self.h2d)], (self.c, self.d2h)
+        if self.name == "layernorm":
+            return [(self.x, self.h2d)], (self.y, self.d2h)
+        if self.name == "affine":
+            return [(self.x, self.h2d)], (self.y, self.d2h)
+        a, b, c = self.bufs[0][:3]
+        return [(a, 4 * self.count), (b, 4 * self.count)], (c, self.d2h)
+
+
+def run_ours(args, group):
+    import numpy as np
+    import paralyn_b200 as p
+    from paralyn_b200 import b200
+    world = group.world
+    ctx = p.Context(f"cuda:{group.local_rank}")
+    w = Workload(args.workload, ctx, group)
+    steps = args.steps or DEFAULT_STEPS[args.workload]
+    warm = []
+    for _ in range(args.warmup):
+        warm += w.step()[0]
+    ctx.synchronize()
+    for e in warm:
+        e.close()
+    kernels_before = p.device_kernel_count(ctx)
+    group.barrier()
+    ctx.synchronize()
+    timed, dominant = [], []
+    with Clocks(group.local_rank) as clocks:
+        start = b200.marker(w.queue)
+        for _ in range(steps):
+            events, main = w.step()
+            timed += events
+            dominant.append(main)
+        stop = b200.marker(w.queue)
+        seconds = b200.elapsed(start, stop)
+    ctx.synchronize()
+    group.barrier()
+    kernels = p.device_kernel_count(ctx) - kernels_before - 2
+    durations = [e.timing().duration_seconds for e in dominant]
+    variant = last_variant(ctx)
+    for e in timed + [start, stop]:
+        e.close()
+    worst = group.max(seconds)
+    value = w.units_total * steps / worst * w.scale
+    ms = worst / steps * 1e3
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(w, ctx, group, steps=1 if args.workload == "chain" else steps)
+
+    dom = sum(durations) / len(durations)
+    roofline = roofline_for(w, dom, variant)
+    line = {"metric": w.metric, "value": round(value, 3), "unit": w.unit, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": w.scaling,
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded SplitMix64 stream generated on device)",
+            "config": w.config, "e2e": e2e, "gpu_launches": int(group.max(kernels)), "roofline": roofline,
+            "clocks": clocks.summary(), "dominant_kernel_variant": variant, "headline_metric": METRIC}
+    if group.rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload)
+    ctx.close()
+    return line
+
+
+def last_variant(ctx):
+    import tempfile
+    d = Path(tempfile.mkdtemp(prefix="paralyn_evidence_")) / "e"
+    ctx.write_evidence(str(d))
+    launches = json.loads((d / "execution.json").read_text())["launches"]
+    for launch in reversed(launches):
+        if launch["kernel"] not in ("b200_marker", "b200_synthetic_f32"):
+            if launch["kernel"] == "paralyn_layer_norm_f32":
+                continue
+            return launch["variant"]
+    return None
+
+
+def end_to_end(w, ctx, group, steps):
+    """Same steps with host buffers: pinned inputs copied in, result copied out, every step."""
+    import torch
+    ins, (out_buf, out_bytes) = w.io_buffers()
+    pinned_in = [(buf, torch.empty(nbytes, dtype=torch.uint8, pin_memory=True), nbytes) for buf, nbytes in ins]
+    for buf, host, nbytes in pinned_in:  # the device's current inputs become the host copy
+        buf.read_into(host.data_ptr(), nbytes)
+    pinned_out = torch.empty(out_bytes, dtype=torch.uint8, pin_memory=True)
+    ctx.synchronize()
+    group.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for buf, host, nbytes in pinned_in:
+            buf.write_from(host.data_ptr(), nbytes)
+        events, _ = w.step()
+        out_buf.read_into(pinned_out.data_ptr(), out_bytes)
+        for e in events:
+            e.close()
+    ctx.synchronize()
+    seconds = time.perf_counter() - t0
+    group.barrier()
+    worst = group.max(seconds)
+    return {"value": round(w.units_total * steps / worst * w.scale, 3), "unit": w.unit,
+            "h2d_bytes_per_step": sum(n for _, _, n in pinned_in), "d2h_bytes_per_step": out_bytes,
+            "timing": "host wall clock around blocking pr_buffer_write / launches / pr_buffer_read, max over ranks",
+            "steps": steps}
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}, "fallback"
+
+
+def roofline_for(w, seconds, variant):
+    peaks, basis = measured_peaks()
+    traffic = load_traffic().get(w.name)
+    if w.name in ("layernorm", "affine", "add"):
+        per_launch = w.units_local
+        achieved = per_launch / seconds / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "peak_basis": f"{basis} STREAM-style copy"}
+    flops = 2 * (w.chain.local_rows if w.name == "chain" else w.m_local) * w.n * w.k
+    achieved = flops / seconds / 1e12
+    if variant and "tf32x3" in variant:
+        peak = peaks["bf16_tflops"] / 2 / 3
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_basis": f"{basis} bf16 cuBLAS burst / 2 (TF32 rate) / 3 (three TF32 products per FP32 product)"}
+    sms = 148
+    peak = sms * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    return {"bound": "fp32_ffma", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "peak_basis": f"148 SMs x 128 FP32 lanes x 2 flop x {basis} max SM clock"}
+
+
+def load_traffic():
+    path = ROOT / "profiles" / "traffic.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+# ---------------------------------------------------------------- CPU side (oracle)
+def cpu_sample(workload, budget_seconds):
+    """Runs the oracle (all host threads) on a bounded sample; returns (units/s, sample text)."""
+    import numpy as np
+    import oracle
+    from paralyn_b200 import synthetic
+    if workload in ("chain", "gemm"):
+        k = n = 4096
+        b = synthetic.normal(4, 0, k * n, 0.0, 1.0 / 64) if workload == "chain" else synthetic.uniform(3, 0, k * n)
+        rows = max(8, oracle.threads())
+        block = synthetic.uniform(3, 1, 64 * k)  # timing does not depend on the values
+        a = np.tile(block, (rows + 63) // 64)[:rows * k]
+        t0 = time.perf_counter()
+        z = oracle.matmul(a, b, rows, n, k, threaded=True)
+        if workload == "chain":
+            oracle.layer_norm(z, np.ones(n, np.float32), np.zeros(n, np.float32), 1e-5, threaded=True)
+        t = time.perf_counter() - t0
+        scale = max(1, int(budget_seconds / max(t, 1e-3)))
+        rows2 = min(rows * scale, 65536)
+        a = np.tile(block, (rows2 + 63) // 64)[:rows2 * k]
+        t0 = time.perf_counter()
+        z = oracle.matmul(a, b, rows2, n, k, threaded=True)
+        if workload == "chain":
+            oracle.layer_norm(z, np.ones(n, np.float32), np.zeros(n, np.float32), 1e-5, threaded=True)
+        t = time.perf_counter() - t0
+        return 2 * rows2 * n * k / t * 1e-12, "TFLOP/s", f"{rows2} of the rows x 4096 x 4096 (reference-order sequential GEMM" + (
+            " + reference-order LayerNorm)" if workload == "chain" else ")")
+    if workload == "layernorm":
+        cols = 4096
+        rows = 4096
+        x = synthetic.normal(2, 0, rows * cols).reshape(rows, cols)
+        g, bt = np.ones(cols, np.float32), np.zeros(cols, np.float32)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < budget_seconds or reps == 0:
+            oracle.layer_norm(x, g, bt, 1e-5, threaded=True)
+            reps += 1
+        t = time.perf_counter() - t0
+        return reps * (2 * rows * cols * 4 + 2 * cols * 4) / t * 1e-9, "GB/s", f"{reps} x 4096 rows x 4096"
+    count = 1 << 26 if workload == "affine" else 1 << 20
+    x = synthetic.uniform(1, 0, count, 4.0)
+    y = synthetic.uniform(0, count, count)
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < budget_seconds or reps == 0:
+        if workload == "affine":
+            oracle.affine_scalar(x, np.float32(1.5), np.float32(-0.25), threaded=True)
+        else:
+            oracle.add(x, y, threaded=True)
+        reps += 1
+    t = time.perf_counter() - t0
+    per = 8 * count if workload == "affine" else 12 * count
+    return reps * per / t * 1e-9, "GB/s", f"{reps} passes over n = {count}"
+
+
+def cpu_baseline(workload, budget=10.0):
+    import oracle
+    value, unit, sample = cpu_sample(workload, budget)
+    return {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
+            "sample": sample + "; oracle restatement of the reference's CPU verifier, -O2 -ffp-contract=off, OpenMP"}
+
+
+def run_reference(args, group):
+    """The reference's CPU computation of the path (oracle port), rank 0 only."""
+    if group.rank != 0:
+        return None
+    import oracle
+    steps = args.steps or 2
+    budget = 8.0
+    for _ in range(args.warmup):
+        cpu_sample(args.workload, 0.5)
+    values = []
+    unit = sample = None
+    for _ in range(steps):
+        v, unit, sample = cpu_sample(args.workload, budget)
+        values.append(v)
+    value = sorted(values)[len(values) // 2]
+    names = {"chain": "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)",
+             "gemm": "FP32 GEMM TFLOP/s (4096^3, rows sharded)",
+             "layernorm": "FP32 row LayerNorm HBM GB/s (16384x4096, rows sharded)",
+             "affine": "FP32 affine y = 1.5x - 0.25 HBM GB/s (n = 2^26)",
+             "add": "FP32 vector add HBM GB/s (n = 2^20)"}
+    return {"impl": "reference", "metric": names[args.workload], "value": round(value, 4), "unit": unit,
+            "n_gpus": group.world, "steps": steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload, "sample": sample},
+            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
+        return  # the CPU reference runs on rank 0 alone
+    group = Group(1) if args.impl == "reference" else Group(args.gpus)
+    try:
+        line = run_reference(args, group) if args.impl == "reference" else run_ours(args, group)
+        if group.rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        group.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,50 @@
+// Thin C entry points over the reference's OWN sources, compiled in place from
+// the reference checkout by oracle/Makefile (target `ref`) into oracle/_ref/.
+// Test infrastructure only: used to pin the oracle and the .prk writer against
+// the reference itself; nothing in the product links or loads it.
+//
+//   ref_prk_emit_cuda   deserialize_module (compiler/ir/artifact.cpp:275-313) +
+//                       emit_cuda (compiler/codegen/cuda.cpp:84-107) for every
+//                       kernel of a .prk; returns the generated CUDA text
+//   ref_tree_sum_f32    tree_sum_f32 (examples/native/transformer_reference.hpp:172-181)
+//   ref_layer_norm_row  layer_norm_row float64 bound (same header :133-147)
+#include "paralyn/artifact.hpp"
+#include "paralyn/cuda_codegen.hpp"
+#include "transformer_reference.hpp"
+#include <cstring>
+#include <string>
+#include <vector>
+
+extern "C" {
+// Returns 0 and writes the concatenated CUDA sources (NUL-terminated) on success;
+// returns 1 and writes the exception text when the reference rejects the bytes.
+int ref_prk_emit_cuda(const void *data, size_t size, char *out, size_t capacity) {
+  std::string text;
+  int status = 0;
+  try {
+    for (const auto &kernel : paralyn::deserialize_module(data, size))
+      text += paralyn::emit_cuda(kernel);
+  } catch (const std::exception &e) {
+    text = e.what();
+    status = 1;
+  }
+  if (capacity) {
+    const size_t n = text.size() < capacity - 1 ? text.size() : capacity - 1;
+    std::memcpy(out, text.data(), n);
+    out[n] = 0;
+  }
+  return status;
+}
+float ref_tree_sum_f32(const float *x, size_t n) { return paralyn_reference::tree_sum_f32(x, n); }
+void ref_layer_norm_row(const float *x, const float *gamma, const float *beta, size_t columns,
+                        double epsilon, double *value, double *error) {
+  namespace r = paralyn_reference;
+  std::vector<float> xs(x, x + columns), gs(gamma, gamma + columns), bs(beta, beta + columns);
+  const auto y = r::layer_norm_row(r::exact_values(xs), r::exact_values(gs), r::exact_values(bs),
+                                   epsilon);
+  for (size_t j = 0; j < columns; ++j) {
+    value[j] = y[j].v;
+    error[j] = y[j].e;
+  }
+}
+}

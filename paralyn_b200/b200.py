@@ -1,0 +1,96 @@
+"""Bindings of the additive B200 entry points (include/paralyn/b200.h)."""
+import ctypes as _c
+from enum import IntEnum
+
+from .native import Context, Event, Queue
+from .tensor import TensorDescRecord, _api
+
+UNIFORM, NORMAL = 0, 1
+
+
+class MatmulMode(IntEnum):
+    AUTO = 0
+    REFERENCE = 1
+    FFMA = 2
+    TF32X3 = 3
+
+
+def _b200(lib):
+    lib = _api(lib)
+    if not getattr(lib, "_b200_signatures", False):
+        h, u32, u64, ptr = _c.c_uint64, _c.c_uint32, _c.c_uint64, _c.POINTER
+        signatures = {
+            "pr_b200_matmul_mode_set": (_c.c_int, [h, u32]),
+            "pr_b200_matmul_mode_get": (_c.c_int, [h, ptr(u32)]),
+            "pr_b200_device_kernel_count": (_c.c_int, [h, ptr(u64)]),
+            "pr_b200_module_inspect": (_c.c_int, [_c.c_void_p, u64, _c.c_char_p, u64]),
+            "pr_b200_marker": (_c.c_int, [h, ptr(h)]),
+            "pr_b200_event_elapsed": (_c.c_int, [h, h, ptr(_c.c_double)]),
+            "pr_b200_fill_synthetic_f32": (_c.c_int, [h, ptr(TensorDescRecord), u64, u64, u32,
+                                                      _c.c_float, _c.c_float, ptr(h)]),
+        }
+        for name, (result, arguments) in signatures.items():
+            function = getattr(lib.api, name)
+            function.restype, function.argtypes = result, arguments
+        lib._b200_signatures = True
+    return lib
+
+
+def set_matmul_mode(context, mode):
+    lib = _b200(context._lib)
+    lib.check(lib.api.pr_b200_matmul_mode_set(context.handle, int(MatmulMode(mode))))
+
+
+def matmul_mode(context):
+    lib = _b200(context._lib)
+    value = _c.c_uint32()
+    lib.check(lib.api.pr_b200_matmul_mode_get(context.handle, _c.byref(value)))
+    return MatmulMode(value.value)
+
+
+def device_kernel_count(context):
+    """Device kernels the context has completed (waits for its queue)."""
+    lib = _b200(context._lib)
+    value = _c.c_uint64()
+    lib.check(lib.api.pr_b200_device_kernel_count(context.handle, _c.byref(value)))
+    return value.value
+
+
+def fill_synthetic_into(queue, descriptor, *, seed, first_draw=0, distribution=UNIFORM, p0=1.0, p1=0.0):
+    """Fill a contiguous tensor with the seeded stream (see paralyn_b200.synthetic)."""
+    if not isinstance(queue, Queue):
+        raise TypeError("fill_synthetic_into requires a Queue")
+    lib = _b200(queue._lib)
+    record = descriptor._native()
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_fill_synthetic_f32(queue.handle, _c.byref(record), seed, first_draw,
+                                                 distribution, p0, p1, _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
+
+
+def marker(queue):
+    """An empty command on the queue that records a device timestamp."""
+    lib = _b200(queue._lib)
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_marker(queue.handle, _c.byref(handle)))
+    return Event._adopt(lib, handle.value)
+
+
+def elapsed(first, second):
+    """Device seconds between the completion of two markers of one context."""
+    lib = _b200(first._lib)
+    seconds = _c.c_double()
+    lib.check(lib.api.pr_b200_event_elapsed(first.handle, second.handle, _c.byref(seconds)))
+    return seconds.value
+
+
+def inspect_module(data, library_path=None):
+    """{kernel name: native implementation} for a module artifact, without a device."""
+    from .native import library
+    lib = _b200(library(library_path))
+    data = bytes(data)
+    report = _c.create_string_buffer(1 << 16)
+    storage = _c.create_string_buffer(data, len(data)) if data else None
+    lib.check(lib.api.pr_b200_module_inspect(storage, len(data), report, len(report)))
+    pairs = [item.split("=", 1) for item in report.value.decode().split(";") if item]
+    return dict(pairs)

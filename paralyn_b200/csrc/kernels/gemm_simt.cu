@@ -1,0 +1,281 @@
+// FP32 SIMT GEMM for sm_100a: C[m,n] = op(A)[m,k] op(B)[k,n].
+//
+// Every output keeps one FP32 accumulator that takes k = 0, 1, ..., K-1 in order,
+// as the reference kernel does (runtime/tensor.cpp:44-77). Two summation modes:
+//   reference: sum = fl(sum + fl(a*b)) (__fmul_rn, __fadd_rn), bit-exact with the
+//              sequential checker (tests/native/tensor_tests.cpp:62-85);
+//   ffma:      sum = fma(a, b, sum), one rounding per step, within the
+//              2*K*2^-24*sum|a||b| bound.
+// Tiling: 128x128 outputs per 256-thread block, k-slices of 8 staged in shared
+// memory (A stored k-major so both operands are read as 128-bit vectors), two
+// shared buffers with register prefetch of the next slice, and an 8x8 register
+// tile per thread laid out as 2x2 quads of 4x4 (conflict-free LDS.128).
+// Blocks walk the output in groups of 8 tile-rows so consecutive blocks share B
+// in L2.
+#include "../runtime/builtin.hpp"
+#include <algorithm>
+
+namespace pb {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 8, THREADS = 256;
+
+struct GemmArgs {
+  const float *a, *b;
+  float *c;
+  int64_t m, n, k;       // m, n: extent computed; k: full depth
+  int64_t lda, ldb, ldc; // row strides of the stored matrices
+  bool vec_a, vec_b, vec_c;
+};
+
+template <int MODE> __device__ __forceinline__ float mac(float acc, float a, float b) {
+  if constexpr (MODE == matmul_reference)
+    return __fadd_rn(acc, __fmul_rn(a, b));
+  else
+    return __fmaf_rn(a, b, acc);
+}
+
+// Loads this thread's 4 values of the A slice [m0, m0+128) x [k0, k0+8).
+//  !TA: A[m][k] at a[m*lda + k]; thread t reads row t/2, k (t%2)*4 .. +3
+//   TA: A[m][k] at a[k*lda + m]; thread t reads k t/32, m (t%32)*4 .. +3
+template <bool TA>
+__device__ __forceinline__ void load_a(const GemmArgs &g, int64_t m0, int64_t k0, float r[4]) {
+  const int t = threadIdx.x;
+  if constexpr (!TA) {
+    const int64_t m = m0 + t / 2, k = k0 + (t % 2) * 4;
+    const float *p = g.a + m * g.lda + k;
+    if (m < g.m && g.vec_a && k + 3 < g.k) {
+      const float4 v = *reinterpret_cast<const float4 *>(p);
+      r[0] = v.x, r[1] = v.y, r[2] = v.z, r[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        r[j] = (m < g.m && k + j < g.k) ? p[j] : 0.0f;
+    }
+  } else {
+    const int64_t k = k0 + t / 32, m = m0 + (t % 32) * 4;
+    const float *p = g.a + k * g.lda + m;
+    if (k < g.k && g.vec_a && m + 3 < g.m) {
+      const float4 v = *reinterpret_cast<const float4 *>(p);
+      r[0] = v.x, r[1] = v.y, r[2] = v.z, r[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        r[j] = (k < g.k && m + j < g.m) ? p[j] : 0.0f;
+    }
+  }
+}
+
+//  !TB: B[k][n] at b[k*ldb + n]; thread t reads k t/32, n (t%32)*4 .. +3
+//   TB: B[k][n] at b[n*ldb + k]; thread t reads n t/2, k (t%2)*4 .. +3
+template <bool TB>
+__device__ __forceinline__ void load_b(const GemmArgs &g, int64_t n0, int64_t k0, float r[4]) {
+  const int t = threadIdx.x;
+  if constexpr (!TB) {
+    const int64_t k = k0 + t / 32, n = n0 + (t % 32) * 4;
+    const float *p = g.b + k * g.ldb + n;
+    if (k < g.k && g.vec_b && n + 3 < g.n) {
+      const float4 v = *reinterpret_cast<const float4 *>(p);
+      r[0] = v.x, r[1] = v.y, r[2] = v.z, r[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        r[j] = (k < g.k && n + j < g.n) ? p[j] : 0.0f;
+    }
+  } else {
+    const int64_t n = n0 + t / 2, k = k0 + (t % 2) * 4;
+    const float *p = g.b + n * g.ldb + k;
+    if (n < g.n && g.vec_b && k + 3 < g.k) {
+      const float4 v = *reinterpret_cast<const float4 *>(p);
+      r[0] = v.x, r[1] = v.y, r[2] = v.z, r[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        r[j] = (n < g.n && k + j < g.k) ? p[j] : 0.0f;
+    }
+  }
+}
+
+// Shared slices are k-major: sa[k][m], sb[k][n].
+template <bool TA> __device__ __forceinline__ void store_a(float (*sa)[BM], const float r[4]) {
+  const int t = threadIdx.x;
+  if constexpr (!TA) {
+    const int m = t / 2, k = (t % 2) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      sa[k + j][m] = r[j];
+  } else {
+    *reinterpret_cast<float4 *>(&sa[t / 32][(t % 32) * 4]) = make_float4(r[0], r[1], r[2], r[3]);
+  }
+}
+template <bool TB> __device__ __forceinline__ void store_b(float (*sb)[BN], const float r[4]) {
+  const int t = threadIdx.x;
+  if constexpr (!TB) {
+    *reinterpret_cast<float4 *>(&sb[t / 32][(t % 32) * 4]) = make_float4(r[0], r[1], r[2], r[3]);
+  } else {
+    const int n = t / 2, k = (t % 2) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      sb[k + j][n] = r[j];
+  }
+}
+
+template <int MODE, bool TA, bool TB>
+__global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs g) {
+  __shared__ __align__(16) float sa[2][BK][BM];
+  __shared__ __align__(16) float sb[2][BK][BN];
+  // Grouped raster: 8 tile-rows at a time, columns fastest within the group.
+  const int64_t tiles_m = (g.m + BM - 1) / BM, tiles_n = (g.n + BN - 1) / BN;
+  const int64_t id = blockIdx.x, group = 8;
+  const int64_t per_group = group * tiles_n;
+  const int64_t first_m = (id / per_group) * group;
+  const int64_t rows_in_group = min(group, tiles_m - first_m);
+  const int64_t tm = first_m + (id % per_group) % rows_in_group;
+  const int64_t tn = (id % per_group) / rows_in_group;
+  const int64_t m0 = tm * BM, n0 = tn * BN;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      acc[i][j] = 0.0f;
+
+  float ra[4], rb[4];
+  load_a<TA>(g, m0, 0, ra);
+  load_b<TB>(g, n0, 0, rb);
+  store_a<TA>(sa[0], ra);
+  store_b<TB>(sb[0], rb);
+  __syncthreads();
+
+  const int64_t slices = (g.k + BK - 1) / BK;
+  for (int64_t s = 0; s < slices; ++s) {
+    const int cur = s & 1;
+    const bool more = s + 1 < slices;
+    if (more) {
+      load_a<TA>(g, m0, (s + 1) * BK, ra);
+      load_b<TB>(g, n0, (s + 1) * BK, rb);
+    }
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[8], b[8];
+      const float4 a0 = *reinterpret_cast<const float4 *>(&sa[cur][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&sa[cur][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&sb[cur][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&sb[cur][kk][64 + tx * 4]);
+      a[0] = a0.x, a[1] = a0.y, a[2] = a0.z, a[3] = a0.w;
+      a[4] = a1.x, a[5] = a1.y, a[6] = a1.z, a[7] = a1.w;
+      b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w;
+      b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          acc[i][j] = mac<MODE>(acc[i][j], a[i], b[j]);
+    }
+    if (more) {
+      store_a<TA>(sa[cur ^ 1], ra);
+      store_b<TB>(sb[cur ^ 1], rb);
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (m >= g.m)
+      continue;
+    float *row = g.c + m * g.ldc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t n = n0 + h * 64 + tx * 4;
+      const float *v = &acc[i][4 * h];
+      if (g.vec_c && n + 3 < g.n) {
+        *reinterpret_cast<float4 *>(row + n) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < g.n)
+            row[n + j] = v[j];
+      }
+    }
+  }
+}
+
+template <int MODE, bool TA, bool TB> void run(const GemmArgs &g, cudaStream_t stream) {
+  const int64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + BN - 1) / BN);
+  gemm_simt<MODE, TA, TB><<<uint32_t(tiles), THREADS, 0, stream>>>(g);
+}
+
+template <int MODE> void dispatch(const GemmArgs &g, bool ta, bool tb, cudaStream_t stream) {
+  if (!ta && !tb)
+    run<MODE, false, false>(g, stream);
+  else if (!ta && tb)
+    run<MODE, false, true>(g, stream);
+  else if (ta && !tb)
+    run<MODE, true, false>(g, stream);
+  else
+    run<MODE, true, true>(g, stream);
+}
+
+bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
+
+} // namespace
+
+bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n,
+                        int64_t k, int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb);
+
+// (a, b, c, m, n, k, transpose_a, transpose_b) with a 16x16 block per 16x16 output
+// tile: the grid bounds the computed region to min(m, 16*grid.y) x min(n, 16*grid.x).
+void launch_provider_matmul(Launch &L) {
+  const uint32_t m = L.args[3].u32(), n = L.args[4].u32(), k = L.args[5].u32();
+  const uint32_t ta = L.args[6].u32(), tb = L.args[7].u32();
+  if (ta > 1 || tb > 1)
+    throw Failure(PR_INVALID_ARGUMENT, "Transpose flags must be 0 or 1");
+  const int64_t me = std::min<int64_t>(m, int64_t(L.grid.y) * 16);
+  const int64_t ne = std::min<int64_t>(n, int64_t(L.grid.x) * 16);
+  if (!me || !ne) {
+    L.variant = "empty";
+    return;
+  }
+  // Highest element index + 1 each operand is read or written at.
+  const uint64_t a_need = ta ? uint64_t(k ? k - 1 : 0) * m + me : uint64_t(me) * k;
+  const uint64_t b_need = tb ? uint64_t(ne) * k : uint64_t(k ? k - 1 : 0) * n + ne;
+  if (k) {
+    need_elements(L.args[0], a_need, "a");
+    need_elements(L.args[1], b_need, "b");
+  }
+  need_elements(L.args[2], uint64_t(me - 1) * n + ne, "c");
+  if (L.dry_run)
+    return;
+  GemmArgs g;
+  g.a = static_cast<const float *>(L.args[0].ptr);
+  g.b = static_cast<const float *>(L.args[1].ptr);
+  g.c = static_cast<float *>(L.args[2].ptr);
+  g.m = me;
+  g.n = ne;
+  g.k = k;
+  g.lda = ta ? m : k;
+  g.ldb = tb ? k : n;
+  g.ldc = n;
+  g.vec_a = aligned16(g.a) && g.lda % 4 == 0;
+  g.vec_b = aligned16(g.b) && g.ldb % 4 == 0;
+  g.vec_c = aligned16(g.c) && g.ldc % 4 == 0;
+  uint32_t mode = L.matmul_mode;
+  if (mode == matmul_auto || mode == matmul_tf32x3) {
+    if (launch_tf32x3_gemm(L, g.a, g.b, g.c, me, ne, k, g.lda, g.ldb, g.ldc, ta, tb))
+      return;
+    mode = matmul_ffma;
+  }
+  if (mode == matmul_reference) {
+    dispatch<matmul_reference>(g, ta, tb, L.stream);
+    L.variant = "simt_reference_order";
+  } else {
+    dispatch<matmul_ffma>(g, ta, tb, L.stream);
+    L.variant = "simt_ffma";
+  }
+  L.kernels = 1;
+}
+
+} // namespace pb

@@ -1,0 +1,41 @@
+// Library-internal interface between the C-ABI layer (abi.cpp) and the in-library
+// clients built on it: the tensor provider (provider.cpp) and the B200 additions
+// (b200.cpp). Nothing here is exported.
+#pragma once
+#include "engine.hpp"
+#include "module.hpp"
+#include <functional>
+#include <memory>
+
+namespace pb {
+
+enum class HandleKind { context, buffer, view, module, kernel, queue, event, collective };
+
+// Runs `fn` under the global API lock with the reference's error boundary:
+// success clears pr_last_error, a failure records (status, operation, message).
+pr_status api(const char *operation, const std::function<void()> &fn) noexcept;
+// Records a failure for `operation` without running anything (returns `code`).
+pr_status report_error(pr_status code, const char *operation, const std::string &message) noexcept;
+void clear_error() noexcept;
+// Opaque identity of the context that owns a live handle of exactly `kind`.
+pr_status handle_context(pr_handle handle, HandleKind kind, const void **out) noexcept;
+
+// Helpers for in-library clients; call only inside api().
+struct QueueAccess {
+  std::shared_ptr<Engine> engine;
+  const void *context = nullptr;
+};
+QueueAccess queue_access(pr_queue queue);
+std::shared_ptr<Engine> context_engine(pr_context context);
+std::shared_ptr<Allocation> buffer_allocation(pr_buffer buffer, const void *context);
+// Publishes an event handle for a submitted command (handle allocated first, as
+// pr_launch does, so a failure never leaves a command without its event).
+pr_event submit_command(pr_queue queue, const std::string &name, Launcher launcher, Dim3 grid,
+                        Dim3 block, std::vector<BoundArg> args,
+                        std::vector<std::shared_ptr<Allocation>> retained);
+pr_event submit_marker(pr_queue queue);
+double event_elapsed(pr_event first, pr_event second);
+pr_handle add_object(std::shared_ptr<void> object, HandleKind kind, const void *context);
+std::shared_ptr<void> get_object(pr_handle handle, HandleKind kind, const void **context);
+
+} // namespace pb

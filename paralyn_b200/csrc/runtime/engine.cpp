@@ -1,0 +1,701 @@
+#include "engine.hpp"
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <filesystem>
+#include <fstream>
+#include <iomanip>
+#include <limits>
+#include <sstream>
+#include <sys/utsname.h>
+#include <unistd.h>
+
+namespace pb {
+
+struct Accounting {
+  std::atomic<uint64_t> current{0}, peak{0};
+};
+
+namespace {
+
+std::mutex log_mutex;
+uint64_t log_sequence = 0;
+
+std::string json(const std::string &text) {
+  std::ostringstream out;
+  out << '"';
+  for (unsigned char c : text) {
+    if (c == '"' || c == '\\')
+      out << '\\' << char(c);
+    else if (c < 32)
+      out << "\\u" << std::hex << std::setw(4) << std::setfill('0') << unsigned(c) << std::dec;
+    else
+      out << char(c);
+  }
+  out << '"';
+  return out.str();
+}
+
+// CUDA runtime error classes, mirroring the driver-code classes of the reference
+// engine (backends/cuda/engine.cpp:29-94).
+Code code_of(cudaError_t e) {
+  switch (e) {
+  case cudaErrorInvalidValue:
+  case cudaErrorInvalidConfiguration:
+  case cudaErrorLaunchOutOfResources:
+    return Code::invalid_value;
+  case cudaErrorMemoryAllocation:
+    return Code::out_of_memory;
+  case cudaErrorNoDevice:
+  case cudaErrorInvalidDevice:
+  case cudaErrorInsufficientDriver:
+  case cudaErrorInitializationError:
+  case cudaErrorStubLibrary:
+  case cudaErrorSystemNotReady:
+  case cudaErrorSystemDriverMismatch:
+  case cudaErrorCompatNotSupportedOnDevice:
+    return Code::invalid_device;
+  case cudaErrorNoKernelImageForDevice:
+  case cudaErrorInvalidKernelImage:
+  case cudaErrorUnsupportedPtxVersion:
+    return Code::compilation;
+  case cudaErrorNotPermitted:
+  case cudaErrorNotSupported:
+    return Code::unsupported;
+  case cudaErrorInvalidResourceHandle:
+  case cudaErrorContextIsDestroyed:
+    return Code::internal;
+  default:
+    return Code::execution;
+  }
+}
+
+bool is_sticky(cudaError_t e) {
+  switch (e) {
+  case cudaErrorECCUncorrectable:
+  case cudaErrorIllegalAddress:
+  case cudaErrorLaunchTimeout:
+  case cudaErrorAssert:
+  case cudaErrorHardwareStackError:
+  case cudaErrorIllegalInstruction:
+  case cudaErrorMisalignedAddress:
+  case cudaErrorInvalidAddressSpace:
+  case cudaErrorInvalidPc:
+  case cudaErrorLaunchFailure:
+  case cudaErrorUnknown:
+  case cudaErrorContextIsDestroyed:
+    return true;
+  default:
+    return false;
+  }
+}
+
+std::string text_of(cudaError_t e) {
+  return std::string(cudaGetErrorName(e)) + " (" + cudaGetErrorString(e) + ")";
+}
+
+std::string os_description() {
+  struct utsname name {};
+  if (uname(&name) == 0)
+    return std::string(name.sysname) + " " + name.release;
+  return "unknown";
+}
+
+// Makes `device` current for one operation and restores the caller's device.
+class DeviceScope {
+  int previous_ = -1, device_;
+
+public:
+  explicit DeviceScope(int device) : device_(device) {
+    if (cudaGetDevice(&previous_) != cudaSuccess)
+      previous_ = -1;
+    if (previous_ != device_)
+      cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  }
+  ~DeviceScope() {
+    if (previous_ >= 0 && previous_ != device_)
+      cudaSetDevice(previous_);
+  }
+};
+
+struct Probe {
+  BackendStatus status;
+  std::vector<DeviceRecord> devices;
+};
+
+const Probe &probe() {
+  static const Probe value = [] {
+    Probe p;
+    cudaRuntimeGetVersion(&p.status.runtime_version);
+    if (cudaDriverGetVersion(&p.status.driver_version) != cudaSuccess)
+      p.status.driver_version = 0;
+    int count = 0;
+    const cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) {
+      p.status.reason = "CUDA unavailable: " + text_of(e) + ". There is no CPU fallback.";
+      cudaGetLastError();
+      return p;
+    }
+    const std::string os = os_description();
+    for (int i = 0; i < count; ++i) {
+      cudaDeviceProp prop{};
+      if (cudaGetDeviceProperties(&prop, i) != cudaSuccess)
+        continue;
+      DeviceRecord d;
+      d.ordinal = i;
+      d.name = prop.name;
+      d.os = os;
+      d.total_memory = prop.totalGlobalMem;
+      d.max_smem_block = prop.sharedMemPerBlock;
+      d.sm_count = prop.multiProcessorCount;
+      d.cc_major = prop.major;
+      d.cc_minor = prop.minor;
+      d.max_threads = prop.maxThreadsPerBlock;
+      d.max_block = {uint32_t(prop.maxThreadsDim[0]), uint32_t(prop.maxThreadsDim[1]),
+                     uint32_t(prop.maxThreadsDim[2])};
+      d.max_grid = {uint32_t(prop.maxGridSize[0]), uint32_t(prop.maxGridSize[1]),
+                    uint32_t(prop.maxGridSize[2])};
+      d.integrated = prop.integrated != 0;
+      d.registry_id = 0x4355444100000000ULL | (uint64_t(i) + 1);
+      std::ostringstream id;
+      id << "cuda:uuid:" << std::hex << std::setfill('0');
+      for (int b = 0; b < 16; ++b) {
+        if (b == 4 || b == 6 || b == 8 || b == 10)
+          id << '-';
+        id << std::setw(2) << unsigned(static_cast<unsigned char>(prop.uuid.bytes[b]));
+      }
+      d.stable_id = id.str();
+      p.devices.push_back(d);
+    }
+    p.status.device_count = int(p.devices.size());
+    p.status.available = !p.devices.empty();
+    if (!p.status.available)
+      p.status.reason = "No CUDA device available. There is no CPU fallback.";
+    return p;
+  }();
+  return value;
+}
+
+uint64_t next_trace_id() {
+  static std::atomic<uint64_t> next{1};
+  return (uint64_t(2) << 32) | next.fetch_add(1);
+}
+
+} // namespace
+
+void cuda_check(cudaError_t result, const char *operation) {
+  if (result != cudaSuccess)
+    throw Error(code_of(result), std::string("CUDA ") + operation + " failed: " + text_of(result));
+}
+
+void progress(const std::string &message) {
+  const char *path = std::getenv("PARALYN_RUNTIME_LOG");
+  if (!path || !*path)
+    return;
+  std::lock_guard<std::mutex> lock(log_mutex);
+  std::ofstream output(path, std::ios::app);
+  output << message;
+  output.close();
+  if (!output)
+    throw Error(Code::internal, "Cannot write PARALYN_RUNTIME_LOG");
+}
+
+void runtime_event(const std::string &category, const std::string &status,
+                   const std::string &detail, uint64_t context_id, uint64_t operation_id,
+                   uint64_t bytes) {
+  const char *path = std::getenv("PARALYN_EVENT_LOG");
+  if (!path || !*path)
+    return;
+  std::lock_guard<std::mutex> lock(log_mutex);
+  const double now =
+      std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+  std::ostringstream line;
+  line << std::setprecision(17) << "{\"schema\":\"paralyn.runtime.event\",\"schema_version\":1,"
+       << "\"sequence\":" << ++log_sequence << ",\"category\":" << json(category)
+       << ",\"status\":" << json(status) << ",\"detail\":" << json(detail)
+       << ",\"context_id\":" << context_id << ",\"operation_id\":" << operation_id
+       << ",\"bytes\":" << bytes << ",\"host_monotonic_seconds\":" << now << "}\n";
+  const std::string text = line.str();
+  FILE *file = std::fopen(path, "ab");
+  if (!file)
+    throw Error(Code::internal, "Cannot open PARALYN_EVENT_LOG");
+  bool ok = std::fwrite(text.data(), 1, text.size(), file) == text.size();
+  ok = std::fflush(file) == 0 && ok;
+  ok = fsync(fileno(file)) == 0 && ok;
+  ok = std::fclose(file) == 0 && ok;
+  if (!ok)
+    throw Error(Code::internal, "Cannot durably append PARALYN_EVENT_LOG");
+}
+
+const BackendStatus &backend_status() { return probe().status; }
+const std::vector<DeviceRecord> &devices() { return probe().devices; }
+
+Allocation::~Allocation() {
+  if (accounting)
+    accounting->current.fetch_sub(bytes);
+  if (!ptr)
+    return;
+  int previous = -1;
+  cudaGetDevice(&previous);
+  if (previous != device)
+    cudaSetDevice(device);
+  cudaFree(ptr);
+  if (previous >= 0 && previous != device)
+    cudaSetDevice(previous);
+}
+
+Engine::Engine(const DeviceRecord &device)
+    : device_(device), accounting_(std::make_shared<Accounting>()), trace_id_(next_trace_id()) {
+  DeviceScope scope(device_.ordinal);
+  cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  const cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(&status_host_), 64,
+                                      cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(stream_);
+    cuda_check(e, "cudaHostAlloc(status word)");
+  }
+  std::memset(status_host_, 0, 64);
+  cuda_check(cudaHostGetDevicePointer(reinterpret_cast<void **>(&status_device_), status_host_, 0),
+             "cudaHostGetDevicePointer");
+  if (const char *mode = std::getenv("PARALYN_MATMUL_MODE")) {
+    const std::string m = mode;
+    matmul_mode_ = m == "reference" ? matmul_reference
+                 : m == "ffma"      ? matmul_ffma
+                 : m == "tf32x3"    ? matmul_tf32x3
+                                    : matmul_auto;
+  }
+  runtime_event("context", "created", device_.stable_id, trace_id_);
+}
+
+Engine::~Engine() {
+  try {
+    synchronize();
+  } catch (...) {
+  }
+  try {
+    DeviceScope scope(device_.ordinal);
+    for (auto &work : pending_)
+      recycle(*work);
+    for (auto e : spare_events_)
+      cudaEventDestroy(e);
+    if (stream_)
+      cudaStreamDestroy(stream_);
+    if (status_host_)
+      cudaFreeHost(status_host_);
+  } catch (...) {
+  }
+}
+
+void Engine::healthy() const {
+  if (!terminal_failure_.empty())
+    throw Error(Code::execution, terminal_failure_);
+}
+
+void Engine::cuda_failure(cudaError_t code, const std::string &operation) {
+  const std::string text = "CUDA " + operation + " failed: " + text_of(code);
+  if (is_sticky(code) && terminal_failure_.empty())
+    terminal_failure_ = text;
+  cudaGetLastError();
+  throw Error(code_of(code), text);
+}
+
+void Engine::check_owner(const Allocation &allocation) const {
+  if (allocation.owner != this)
+    throw Error(Code::invalid_handle, "Buffer belongs to another context");
+}
+
+std::shared_ptr<Allocation> Engine::allocate(size_t bytes) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  healthy();
+  auto result = std::make_shared<Allocation>();
+  result->device = device_.ordinal;
+  result->bytes = bytes;
+  result->owner = this;
+  if (bytes) {
+    DeviceScope scope(device_.ordinal);
+    const cudaError_t e = cudaMalloc(&result->ptr, bytes);
+    if (e != cudaSuccess)
+      cuda_failure(e, "cudaMalloc");
+  }
+  result->accounting = accounting_;
+  const uint64_t now = accounting_->current.fetch_add(bytes) + bytes;
+  uint64_t peak = accounting_->peak.load();
+  while (peak < now && !accounting_->peak.compare_exchange_weak(peak, now)) {
+  }
+  return result;
+}
+
+static void copy_range(const Allocation &a, size_t offset, size_t bytes) {
+  if (offset > a.bytes || bytes > a.bytes - offset)
+    throw Error(Code::invalid_value, "Copy range exceeds allocation");
+}
+
+// Host pointers may be pageable or pinned; any UVA address (including device
+// memory of this process) is accepted because the copy kind is inferred.
+void Engine::write(const std::shared_ptr<Allocation> &allocation, size_t offset,
+                   const void *source, size_t bytes) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  check_owner(*allocation);
+  copy_range(*allocation, offset, bytes);
+  if (bytes && !source)
+    throw Error(Code::invalid_value, "Nonempty write requires a host pointer");
+  drain_locked();
+  const auto start = std::chrono::steady_clock::now();
+  if (bytes) {
+    DeviceScope scope(device_.ordinal);
+    cudaError_t e = cudaMemcpyAsync(static_cast<char *>(allocation->ptr) + offset, source, bytes,
+                                    cudaMemcpyDefault, stream_);
+    if (e == cudaSuccess)
+      e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess)
+      cuda_failure(e, "cudaMemcpy(host to device)");
+  }
+  counters_.h2d_seconds +=
+      std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+  counters_.h2d_bytes += bytes;
+  runtime_event("transfer", "completed", "host_to_device", trace_id_, 0, bytes);
+}
+
+void Engine::read(const std::shared_ptr<Allocation> &allocation, size_t offset, void *destination,
+                  size_t bytes) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  check_owner(*allocation);
+  copy_range(*allocation, offset, bytes);
+  if (bytes && !destination)
+    throw Error(Code::invalid_value, "Nonempty read requires a host pointer");
+  drain_locked();
+  const auto start = std::chrono::steady_clock::now();
+  if (bytes) {
+    DeviceScope scope(device_.ordinal);
+    cudaError_t e = cudaMemcpyAsync(destination, static_cast<const char *>(allocation->ptr) + offset,
+                                    bytes, cudaMemcpyDefault, stream_);
+    if (e == cudaSuccess)
+      e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess)
+      cuda_failure(e, "cudaMemcpy(device to host)");
+  }
+  counters_.d2h_seconds +=
+      std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+  counters_.d2h_bytes += bytes;
+  runtime_event("transfer", "completed", "device_to_host", trace_id_, 0, bytes);
+}
+
+void Engine::check_geometry(Dim3 grid, Dim3 block) const {
+  if (!grid.x || !grid.y || !grid.z || !block.x || !block.y || !block.z)
+    throw Error(Code::invalid_value, "Grid and block dimensions must be positive");
+  const auto &limit = device_.max_block;
+  if (block.x > limit.x || block.y > limit.y || block.z > limit.z)
+    throw Error(Code::invalid_value, "Block dimension exceeds CUDA device limits");
+  const uint64_t threads = uint64_t(block.x) * block.y * block.z;
+  if (threads > uint64_t(device_.max_threads))
+    throw Error(Code::invalid_value, "Block thread count exceeds CUDA device limits");
+  if (grid.x > device_.max_grid.x || grid.y > device_.max_grid.y || grid.z > device_.max_grid.z)
+    throw Error(Code::invalid_value, "Grid dimension exceeds CUDA device limits");
+  const uint64_t x = uint64_t(grid.x) * block.x, y = uint64_t(grid.y) * block.y,
+                 z = uint64_t(grid.z) * block.z;
+  if (x > UINT32_MAX || y > UINT32_MAX || z > UINT32_MAX)
+    throw Error(Code::invalid_value, "Logical grid dimension exceeds 32-bit indexing");
+}
+
+cudaEvent_t Engine::take_event() {
+  if (!spare_events_.empty()) {
+    auto e = spare_events_.back();
+    spare_events_.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  const cudaError_t r = cudaEventCreate(&e);
+  if (r != cudaSuccess)
+    cuda_failure(r, "cudaEventCreate");
+  return e;
+}
+
+void Engine::recycle(Work &work) {
+  for (auto *e : {&work.start, &work.end})
+    if (*e) {
+      spare_events_.push_back(*e);
+      *e = nullptr;
+    }
+}
+
+std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher, Dim3 grid,
+                                     Dim3 block, std::vector<BoundArg> args,
+                                     std::vector<std::shared_ptr<Allocation>> retained) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  healthy();
+  DeviceScope scope(device_.ordinal);
+  auto work = std::make_shared<Work>();
+  work->kernel = name;
+  work->grid = grid;
+  work->block = block;
+  work->retained = std::move(retained);
+  work->operation_id = next_operation_++;
+  Launch launch;
+  launch.stream = stream_;
+  launch.device = device_.ordinal;
+  launch.sm_count = device_.sm_count;
+  launch.status = status_device_;
+  launch.matmul_mode = matmul_mode_;
+  launch.grid = grid;
+  launch.block = block;
+  launch.args = std::move(args);
+  launch.dry_run = true;
+  launcher(launch); // validation: throws before anything is enqueued
+  launch.dry_run = false;
+  pending_.reserve(pending_.size() + 1);
+  executions_.reserve(executions_.size() + pending_.size() + 1);
+  work->start = take_event();
+  work->end = take_event();
+  runtime_event("submission", "prepared", name, trace_id_, work->operation_id);
+  cudaError_t e = cudaEventRecord(work->start, stream_);
+  if (e != cudaSuccess) {
+    recycle(*work);
+    cuda_failure(e, "cudaEventRecord");
+  }
+  try {
+    launcher(launch);
+  } catch (...) {
+    // Part of the command may be enqueued: let it finish before its views go.
+    cudaStreamSynchronize(stream_);
+    recycle(*work);
+    throw;
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(stream_);
+    recycle(*work);
+    cuda_failure(e, "kernel launch (" + name + ")");
+  }
+  work->kernels = launch.kernels;
+  work->variant = launch.variant;
+  pending_.push_back(work);
+  e = cudaEventRecord(work->end, stream_);
+  if (e != cudaSuccess) {
+    const std::string text = "CUDA cudaEventRecord after launch failed: " + text_of(e);
+    cudaStreamSynchronize(stream_);
+    if (terminal_failure_.empty())
+      terminal_failure_ = text;
+    work->failure = text;
+    throw Error(code_of(e), text);
+  }
+  progress("Kernel: " + name + " (" + launch.variant + ")\n");
+  return work;
+}
+
+void Engine::finish(const std::shared_ptr<Work> &work) {
+  if (work->recorded)
+    return;
+  std::string failure = work->failure;
+  bool completed = false;
+  double milliseconds = 0;
+  if (failure.empty()) {
+    cudaError_t e = cudaEventSynchronize(work->end);
+    if (e != cudaSuccess) {
+      failure = "CUDA command failed for " + work->kernel + ": " + text_of(e);
+      if (is_sticky(e) && terminal_failure_.empty())
+        terminal_failure_ = failure;
+    } else {
+      completed = true;
+      float ms = 0;
+      e = cudaEventElapsedTime(&ms, work->start, work->end);
+      if (e != cudaSuccess)
+        failure = "CUDA completed " + work->kernel + " without GPU duration evidence: " + text_of(e);
+      else if (!std::isfinite(ms) || ms < 0)
+        failure = "CUDA completed " + work->kernel + " with an invalid GPU duration";
+      else
+        milliseconds = ms;
+      // A kernel that gave up a bounded wait reports it through the status word.
+      const int status = __atomic_exchange_n(status_host_, 0, __ATOMIC_ACQ_REL);
+      if (status != 0 && failure.empty())
+        failure = "Kernel " + work->kernel + " abandoned a bounded wait (status " +
+                  std::to_string(status) + ")";
+    }
+  }
+  if (work->keep_end && completed) {
+    cudaEvent_t end = work->end;
+    work->end = nullptr;
+    recycle(*work);
+    work->end = end; // destroyed with the Work
+  } else {
+    recycle(*work);
+  }
+  work->info = {};
+  work->info.completed = completed;
+  if (completed && failure.empty()) {
+    work->info.duration_valid = true;
+    work->info.duration_seconds = milliseconds / 1000.0;
+    counters_.gpu_seconds += work->info.duration_seconds;
+    ++counters_.completed_launches;
+    counters_.device_kernels += work->kernels;
+  }
+  executions_.push_back({work->kernel, work->variant, failure, work->grid, work->block,
+                         work->kernels, work->info.duration_seconds, completed});
+  if (!failure.empty() && terminal_failure_.empty())
+    terminal_failure_ = failure;
+  work->failure = failure;
+  work->recorded = true;
+  work->retained.clear();
+  runtime_event("completion", failure.empty() ? "completed" : "failed",
+                failure.empty() ? work->kernel : failure, trace_id_, work->operation_id);
+}
+
+void Engine::drain_locked() {
+  DeviceScope scope(device_.ordinal);
+  for (const auto &work : pending_)
+    finish(work);
+  pending_.clear();
+  healthy();
+}
+
+void Engine::synchronize() {
+  std::lock_guard<std::mutex> lock(mutex_);
+  drain_locked();
+}
+
+EventInfo Engine::wait(const std::shared_ptr<Work> &work) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  auto end = std::find(pending_.begin(), pending_.end(), work);
+  if (end != pending_.end()) {
+    DeviceScope scope(device_.ordinal);
+    ++end;
+    for (auto it = pending_.begin(); it != end; ++it)
+      finish(*it);
+    pending_.erase(pending_.begin(), end);
+  }
+  healthy();
+  if (!work->recorded)
+    throw Error(Code::internal, "Event has no recorded command");
+  return work->info;
+}
+
+Work::~Work() {
+  if (keep_end && end && recorded) {
+    int previous = -1;
+    cudaGetDevice(&previous);
+    if (previous != device)
+      cudaSetDevice(device);
+    cudaEventDestroy(end);
+    if (previous >= 0 && previous != device)
+      cudaSetDevice(previous);
+  }
+}
+
+static void marker_launch(Launch &L) { L.variant = "marker"; }
+
+std::shared_ptr<Work> Engine::marker() {
+  auto work = submit("b200_marker", marker_launch, Dim3{}, Dim3{}, {}, {});
+  std::lock_guard<std::mutex> lock(mutex_);
+  work->keep_end = true;
+  work->device = device_.ordinal;
+  return work;
+}
+
+double Engine::elapsed(const std::shared_ptr<Work> &first, const std::shared_ptr<Work> &second) {
+  wait(first);
+  wait(second);
+  std::lock_guard<std::mutex> lock(mutex_);
+  if (!first->keep_end || !second->keep_end || !first->end || !second->end)
+    throw Error(Code::invalid_value, "Elapsed time is defined between two completed markers");
+  DeviceScope scope(device_.ordinal);
+  float ms = 0;
+  const cudaError_t e = cudaEventElapsedTime(&ms, first->end, second->end);
+  if (e != cudaSuccess)
+    cuda_failure(e, "cudaEventElapsedTime");
+  return ms / 1000.0;
+}
+
+Statistics Engine::statistics() const {
+  std::lock_guard<std::mutex> lock(mutex_);
+  return counters_;
+}
+
+void Engine::write_evidence(const std::string &directory) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  std::exception_ptr failure;
+  try {
+    drain_locked();
+  } catch (...) {
+    failure = std::current_exception();
+  }
+  namespace fs = std::filesystem;
+  fs::create_directories(directory);
+  std::ostringstream out;
+  out << std::setprecision(17) << "{\n  \"backend\": \"CUDA\",\n  \"device\": " << json(device_.name)
+      << ",\n  \"device_ordinal\": " << device_.ordinal
+      << ",\n  \"stable_device_id\": " << json(device_.stable_id)
+      << ",\n  \"compute_capability\": "
+      << json(std::to_string(device_.cc_major) + "." + std::to_string(device_.cc_minor))
+      << ",\n  \"kernels\": \"ahead-of-time sm_100a (nvcc)\""
+      << ",\n  \"cuda_runtime_version\": " << backend_status().runtime_version
+      << ",\n  \"cuda_driver_version\": " << backend_status().driver_version
+      << ",\n  \"os\": " << json(device_.os) << ",\n  \"cpu_fallback\": false"
+      << ",\n  \"runtime_owned_current_buffer_bytes\": " << accounting_->current.load()
+      << ",\n  \"runtime_owned_peak_buffer_bytes\": " << accounting_->peak.load()
+      << ",\n  \"host_to_device_bytes\": " << counters_.h2d_bytes
+      << ",\n  \"device_to_host_bytes\": " << counters_.d2h_bytes << ",\n  \"launches\": [\n";
+  for (size_t i = 0; i < executions_.size(); ++i) {
+    const auto &e = executions_[i];
+    const bool valid = e.complete && e.error.empty();
+    out << "    {\"kernel\": " << json(e.kernel) << ", \"variant\": " << json(e.variant)
+        << ", \"grid\": [" << e.grid.x << ',' << e.grid.y << ',' << e.grid.z << "], \"block\": ["
+        << e.block.x << ',' << e.block.y << ',' << e.block.z
+        << "], \"device_kernels\": " << e.kernels
+        << ", \"command_status\": " << json(e.complete ? "completed" : "failed")
+        << ", \"gpu_duration_seconds\": ";
+    if (valid)
+      out << e.duration;
+    else
+      out << "null";
+    out << ", \"gpu_duration_valid\": " << (valid ? "true" : "false")
+        << ", \"gpu_timestamps_valid\": false, \"gpu_clock_domain\": \"duration_only\""
+        << ", \"error\": " << json(e.error) << '}' << (i + 1 == executions_.size() ? "\n" : ",\n");
+  }
+  out << "  ]\n}\n";
+  std::ofstream file(fs::path(directory) / "execution.json", std::ios::binary);
+  file << out.str();
+  file.close();
+  if (!file)
+    throw Error(Code::internal, "Cannot write execution.json");
+  if (failure)
+    std::rethrow_exception(failure);
+}
+
+std::shared_ptr<Engine> create_engine(const std::string &selector) {
+  uint32_t ordinal = 0;
+  if (selector.rfind("cuda:", 0) == 0) {
+    const std::string digits = selector.substr(5);
+    if (digits.empty() || digits.size() > 10 ||
+        digits.find_first_not_of("0123456789") != std::string::npos)
+      throw Error(Code::invalid_device,
+                  "CUDA selectors have the form cuda:INDEX (decimal device ordinal)");
+    const auto value = std::stoull(digits);
+    if (value > 0x7fffffffULL)
+      throw Error(Code::invalid_device, "CUDA device ordinal is out of range for cuda:INDEX");
+    ordinal = uint32_t(value);
+  } else if (selector.rfind("hip:", 0) == 0 || selector.rfind("rocm:", 0) == 0) {
+    throw Error(Code::invalid_device, "The HIP/ROCm backend is not implemented.");
+  } else if (selector != "auto") {
+    throw Error(Code::invalid_device,
+                "This build has no Metal backend; select a CUDA device with cuda:INDEX or auto. "
+                "There is no CPU fallback.");
+  }
+  const auto &status = backend_status();
+  if (!status.available)
+    throw Error(Code::invalid_device, "CUDA backend unavailable: " + status.reason);
+  const auto &list = devices();
+  if (ordinal >= list.size())
+    throw Error(Code::invalid_device, "CUDA device index is out of range (" +
+                                          std::to_string(list.size()) +
+                                          " device(s) reported by the driver)");
+  const auto &d = list[ordinal];
+  if (d.cc_major != 10 || d.cc_minor != 0)
+    throw Error(Code::unsupported, "This build carries sm_100a kernels only; device " + d.name +
+                                       " has compute capability " + std::to_string(d.cc_major) +
+                                       "." + std::to_string(d.cc_minor));
+  return std::make_shared<Engine>(d);
+}
+
+} // namespace pb

@@ -1,0 +1,142 @@
+// CUDA engine: one instance per context. It owns one ordered stream on a device's
+// primary context, the allocations made through it, a list of submitted work with
+// per-launch start/end events (duration-only timing), a sticky terminal failure and
+// the launch log written as execution.json.
+//
+// Behaviour follows the reference's CUDA engine (backends/cuda/engine.cpp):
+// copies drain the queue first and are blocking (:435-470), each launch is
+// bracketed by two events (:684-715), completion is observed in submission order
+// (:719-799), the first command failure becomes sticky (:396-404, :762-773) and
+// evidence lists every launch (:800-858). Unlike it, kernels are compiled ahead of
+// time for sm_100a and launched through the CUDA runtime API.
+#pragma once
+#include "builtin.hpp"
+#include <memory>
+#include <mutex>
+
+namespace pb {
+
+struct DeviceRecord {
+  int ordinal = 0;
+  std::string name, stable_id, os;
+  uint64_t total_memory = 0, max_smem_block = 0, registry_id = 0;
+  int sm_count = 0, cc_major = 0, cc_minor = 0, max_threads = 0;
+  Dim3 max_block, max_grid;
+  bool integrated = false;
+};
+
+struct BackendStatus {
+  bool available = false;
+  int device_count = 0, driver_version = 0, runtime_version = 0;
+  std::string reason;
+};
+
+// Queried once per process; absence of a driver or device is a status, not a throw.
+const BackendStatus &backend_status();
+const std::vector<DeviceRecord> &devices();
+
+struct Allocation {
+  int device = 0;
+  void *ptr = nullptr;
+  size_t bytes = 0;
+  const void *owner = nullptr; // identity of the creating engine
+  std::shared_ptr<struct Accounting> accounting;
+  ~Allocation();
+};
+
+struct EventInfo {
+  bool completed = false, duration_valid = false;
+  double duration_seconds = 0;
+};
+
+struct Work {
+  cudaEvent_t start = nullptr, end = nullptr;
+  std::vector<std::shared_ptr<Allocation>> retained;
+  std::string kernel, variant;
+  Dim3 grid, block;
+  uint32_t kernels = 0;
+  uint64_t operation_id = 0;
+  bool recorded = false;
+  bool keep_end = false; // markers keep their end timestamp for elapsed-time queries
+  int device = 0;
+  EventInfo info;
+  std::string failure;
+  ~Work();
+};
+
+struct Statistics {
+  uint64_t h2d_bytes = 0, d2h_bytes = 0, completed_launches = 0, device_kernels = 0;
+  double h2d_seconds = 0, d2h_seconds = 0, gpu_seconds = 0;
+};
+
+class Engine : public std::enable_shared_from_this<Engine> {
+public:
+  explicit Engine(const DeviceRecord &device);
+  ~Engine();
+  Engine(const Engine &) = delete;
+  Engine &operator=(const Engine &) = delete;
+
+  const DeviceRecord &device() const { return device_; }
+  std::shared_ptr<Allocation> allocate(size_t bytes);
+  void write(const std::shared_ptr<Allocation> &, size_t offset, const void *source, size_t bytes);
+  void read(const std::shared_ptr<Allocation> &, size_t offset, void *destination, size_t bytes);
+  // Checks a pr_launch geometry against the device limits (reference engine.cpp:597-616).
+  void check_geometry(Dim3 grid, Dim3 block) const;
+  // Runs `launcher` between two events on the context stream; retains the views.
+  std::shared_ptr<Work> submit(const std::string &name, Launcher launcher, Dim3 grid, Dim3 block,
+                               std::vector<BoundArg> args,
+                               std::vector<std::shared_ptr<Allocation>> retained);
+  EventInfo wait(const std::shared_ptr<Work> &work);
+  // An empty command that records a device timestamp (kept until the Work dies).
+  std::shared_ptr<Work> marker();
+  // Device seconds between the completion of two markers of this engine.
+  double elapsed(const std::shared_ptr<Work> &first, const std::shared_ptr<Work> &second);
+  void synchronize();
+  void write_evidence(const std::string &directory);
+  void check_owner(const Allocation &allocation) const;
+  cudaStream_t stream() const { return stream_; }
+  uint32_t matmul_mode() const { return matmul_mode_; }
+  void set_matmul_mode(uint32_t mode) { matmul_mode_ = mode; }
+  Statistics statistics() const;
+
+private:
+  struct Execution {
+    std::string kernel, variant, error;
+    Dim3 grid, block;
+    uint32_t kernels;
+    double duration;
+    bool complete;
+  };
+  void healthy() const;
+  [[noreturn]] void cuda_failure(cudaError_t code, const std::string &operation);
+  void finish(const std::shared_ptr<Work> &work);
+  void drain_locked();
+  cudaEvent_t take_event();
+  void recycle(Work &work);
+
+  DeviceRecord device_;
+  cudaStream_t stream_ = nullptr;
+  int *status_host_ = nullptr, *status_device_ = nullptr;
+  mutable std::mutex mutex_;
+  std::vector<std::shared_ptr<Work>> pending_;
+  std::vector<Execution> executions_;
+  std::vector<cudaEvent_t> spare_events_;
+  std::string terminal_failure_;
+  Statistics counters_;
+  std::shared_ptr<struct Accounting> accounting_;
+  uint64_t next_operation_ = 1;
+  uint64_t trace_id_ = 0;
+  uint32_t matmul_mode_ = matmul_auto;
+};
+
+// "cuda:K" or "auto" (cuda:0). Metal/HIP selectors are unavailable in this build.
+std::shared_ptr<Engine> create_engine(const std::string &selector);
+
+// JSON-lines runtime events to PARALYN_EVENT_LOG, progress to PARALYN_RUNTIME_LOG
+// (reference runtime/telemetry.cpp:36-86); both are no-ops when unset.
+void runtime_event(const std::string &category, const std::string &status,
+                   const std::string &detail, uint64_t context_id = 0, uint64_t operation_id = 0,
+                   uint64_t bytes = 0);
+void progress(const std::string &message);
+
+} // namespace pb

@@ -1,0 +1,549 @@
+// The tensor-operator provider (paralyn/tensor.h).
+//
+// Like the reference provider (runtime/tensor.cpp:1-7) it is an ordinary client of
+// the public C ABI: it validates descriptors, checks handle ownership and the
+// provider's entry schema, creates exact-extent views and submits the entry with
+// pr_launch on the caller's queue. The validation order and the status of every
+// rejection follow runtime/tensor.cpp:448-1038, so callers see the same errors.
+// The entries run the sm_100a kernels of paralyn_b200/csrc/kernels.
+#include "abi_internal.hpp"
+#include <array>
+#include <cmath>
+#include <cstring>
+#include <initializer_list>
+#include <limits>
+#include <mutex>
+#include <unordered_set>
+
+namespace pb {
+namespace {
+
+constexpr uint64_t max_elements = uint64_t(std::numeric_limits<int32_t>::max());
+constexpr uint32_t tile = 16, group = 256;
+constexpr uint64_t max_rows = std::numeric_limits<uint32_t>::max() / group;
+static_assert(max_rows == PR_TENSOR_ROW_OPERATOR_MAX_ROWS, "row limit");
+constexpr uint64_t max_layer_norm_columns = uint64_t(1) << 24;
+
+// Captures the inner call's structured error before cleanup can clear it.
+void call(pr_status status) {
+  if (status == PR_SUCCESS)
+    return;
+  pr_error inner{};
+  pr_last_error(&inner);
+  fail(status, std::string(inner.operation) + ": " + inner.message);
+}
+
+template <class F> pr_status boundary(const char *operation, F &&fn) noexcept {
+  try {
+    fn();
+    clear_error();
+    return PR_SUCCESS;
+  } catch (const Failure &f) {
+    return report_error(f.status, operation, f.what());
+  } catch (const Error &e) {
+    return report_error(status_of(e.code), operation, e.what());
+  } catch (const std::bad_alloc &) {
+    return report_error(PR_OUT_OF_MEMORY, operation, "Allocation failed");
+  } catch (const std::exception &e) {
+    return report_error(PR_INTERNAL_ERROR, operation, e.what());
+  } catch (...) {
+    return report_error(PR_INTERNAL_ERROR, operation, "Unknown operator failure");
+  }
+}
+
+// Provider-owned temporary handle (views, kernels); the launch retains what it needs.
+struct Owned {
+  pr_handle handle = 0;
+  Owned() = default;
+  Owned(const Owned &) = delete;
+  Owned &operator=(const Owned &) = delete;
+  ~Owned() {
+    if (handle)
+      pr_release(handle);
+  }
+};
+
+struct Layout {
+  uint64_t count = 0, bytes = 0;
+  bool contiguous = true;
+};
+
+bool mul(uint64_t a, uint64_t b, uint64_t &out) {
+  if (a && b > std::numeric_limits<uint64_t>::max() / a)
+    return false;
+  out = a * b;
+  return true;
+}
+
+Layout validate(const pr_tensor_desc_v1 *d, const char *label) {
+  const std::string name(label);
+  require(d, PR_INVALID_ARGUMENT, "Missing tensor descriptor");
+  require(d->version == PR_TENSOR_VERSION_1, PR_UNSUPPORTED, "Unsupported tensor descriptor version");
+  require(d->struct_size == sizeof(pr_tensor_desc_v1), PR_INVALID_ARGUMENT,
+          "Tensor descriptor size mismatch");
+  if (d->dtype != PR_F32)
+    fail(PR_UNSUPPORTED, name + ": only PR_F32 tensors are supported");
+  if (d->rank > PR_TENSOR_MAX_RANK)
+    fail(PR_INVALID_ARGUMENT, name + ": rank exceeds PR_TENSOR_MAX_RANK");
+  if (d->byte_offset % 4)
+    fail(PR_INVALID_ARGUMENT, name + ": byte offset must be four-byte aligned");
+  Layout layout;
+  layout.count = 1;
+  for (uint32_t i = d->rank; i < PR_TENSOR_MAX_RANK; ++i)
+    if (d->shape[i] || d->strides[i])
+      fail(PR_INVALID_ARGUMENT, name + ": unused dimensions must be zero");
+  for (uint32_t i = 0; i < d->rank; ++i) {
+    if (d->strides[i] < 0)
+      fail(PR_UNSUPPORTED, name + ": negative strides are unsupported");
+    if (!mul(layout.count, d->shape[i], layout.count))
+      fail(PR_OUT_OF_BOUNDS, name + ": element count overflows");
+  }
+  if (layout.count > max_elements)
+    fail(PR_UNSUPPORTED, name + ": tensors support at most INT32_MAX elements");
+  uint64_t expected = 1, last = 0;
+  for (uint32_t r = d->rank; r-- > 0;) {
+    if (d->shape[r] != 1 && uint64_t(d->strides[r]) != expected)
+      layout.contiguous = false;
+    expected *= d->shape[r];
+    uint64_t span = 0;
+    if (layout.count && (!mul(d->shape[r] - 1, uint64_t(d->strides[r]), span) ||
+                         span > std::numeric_limits<uint64_t>::max() - last))
+      fail(PR_OUT_OF_BOUNDS, name + ": stride extent overflows");
+    if (layout.count)
+      last += span;
+  }
+  if (!layout.count)
+    layout.contiguous = true;
+  if (layout.count) {
+    if (last >= std::numeric_limits<uint64_t>::max() / 4)
+      fail(PR_OUT_OF_BOUNDS, name + ": byte extent overflows");
+    layout.bytes = (last + 1) * 4;
+  }
+  uint64_t size = 0;
+  call(pr_buffer_size(d->buffer, &size));
+  if (d->byte_offset > size || layout.bytes > size - d->byte_offset)
+    fail(PR_OUT_OF_BOUNDS, name + ": tensor extent exceeds its buffer");
+  return layout;
+}
+
+Layout operand(const pr_tensor_desc_v1 *d, const char *label, uint32_t rank) {
+  const Layout layout = validate(d, label);
+  if (d->rank != rank)
+    fail(PR_INVALID_ARGUMENT, std::string(label) + ": expected rank " + std::to_string(rank));
+  if (!layout.contiguous)
+    fail(PR_UNSUPPORTED, std::string(label) + ": v1 operators require contiguous row-major layout");
+  return layout;
+}
+
+std::string shape_text(const pr_tensor_desc_v1 *d) {
+  std::string s = "[";
+  for (uint32_t i = 0; i < d->rank; ++i)
+    s += (i ? "," : "") + std::to_string(d->shape[i]);
+  return s + "]";
+}
+
+void expect_dims(const pr_tensor_desc_v1 *d, const char *label, std::initializer_list<uint64_t> dims) {
+  uint32_t i = 0;
+  bool same = d->rank == dims.size();
+  std::string wanted = "[";
+  for (uint64_t v : dims) {
+    same = same && d->shape[i] == v;
+    wanted += (i++ ? "," : "") + std::to_string(v);
+  }
+  if (!same)
+    fail(PR_INVALID_ARGUMENT,
+         std::string(label) + " shape " + shape_text(d) + " does not match expected " + wanted + "]");
+}
+
+// Output/input allocation rule; buffer handles map one-to-one to allocations.
+void no_alias(const pr_tensor_desc_v1 *out, const Layout &o, const pr_tensor_desc_v1 *in,
+              const Layout &i, const char *label) {
+  if (!in || out->buffer != in->buffer)
+    return;
+  const bool overlap = o.bytes && i.bytes && out->byte_offset < in->byte_offset + i.bytes &&
+                       in->byte_offset < out->byte_offset + o.bytes;
+  if (overlap)
+    fail(PR_INVALID_ARGUMENT, std::string("Output overlaps input ") + label +
+                                  "; in-place tensor operations are not supported");
+  fail(PR_UNSUPPORTED, std::string("Output shares an allocation with input ") + label +
+                           "; operators require distinct writable allocations");
+}
+
+// Provider identity: exactly the module handles returned by pr_tensor_operators_load.
+std::mutex registry_mutex;
+std::unordered_set<pr_module> &providers() {
+  static std::unordered_set<pr_module> value;
+  return value;
+}
+bool is_provider(pr_module module) {
+  std::lock_guard<std::mutex> lock(registry_mutex);
+  return providers().count(module) != 0;
+}
+
+const void *owner(pr_handle handle, HandleKind kind, const char *label) {
+  const void *context = nullptr;
+  const pr_status status = handle_context(handle, kind, &context);
+  if (status != PR_SUCCESS) {
+    pr_error inner{};
+    pr_last_error(&inner);
+    fail(status, std::string(label) + ": " + inner.message);
+  }
+  return context;
+}
+
+void same_context(pr_queue queue, pr_module operators,
+                  std::initializer_list<std::pair<const pr_tensor_desc_v1 *, const char *>> tensors) {
+  const void *context = owner(queue, HandleKind::queue, "queue");
+  if (owner(operators, HandleKind::module, "operators") != context)
+    fail(PR_CONTEXT_MISMATCH, "Queue and operator module belong to different contexts");
+  if (!is_provider(operators))
+    fail(PR_INVALID_ARGUMENT,
+         "Module is not the tensor operator provider (load it with pr_tensor_operators_load)");
+  for (const auto &t : tensors)
+    if (t.first && owner(t.first->buffer, HandleKind::buffer, t.second) != context)
+      fail(PR_CONTEXT_MISMATCH, std::string(t.second) + ": tensor buffer belongs to a different context");
+}
+
+// Resolves an entry and checks its schema against the provider table.
+void kernel(pr_module operators, const char *name, Owned &out) {
+  const Builtin *entry = find_builtin(name);
+  call(pr_module_kernel(operators, name, &out.handle));
+  uint32_t count = 0;
+  call(pr_kernel_parameter_count(out.handle, &count));
+  bool same = entry && count == entry->params.size();
+  for (uint32_t i = 0; same && i < count; ++i) {
+    pr_parameter_info info{};
+    call(pr_kernel_parameter(out.handle, i, &info));
+    const auto &p = entry->params[i];
+    same = !std::strcmp(info.name, p.name.c_str()) && info.is_buffer == uint32_t(p.buffer) &&
+           info.type == (p.type == Scalar::F32 ? PR_F32 : PR_U32);
+  }
+  require(same, PR_INVALID_ARGUMENT,
+          "Module is not the tensor operator provider (load it with pr_tensor_operators_load)");
+}
+
+void view(const pr_tensor_desc_v1 *d, const Layout &l, pr_access access, Owned &out) {
+  call(pr_view_create(d->buffer, d->byte_offset, l.bytes, 4, access, &out.handle));
+}
+pr_argument buffer(const Owned &v) {
+  pr_argument a{};
+  a.type = PR_BUFFER;
+  a.view = v.handle;
+  return a;
+}
+pr_argument u32(uint64_t value) {
+  pr_argument a{};
+  a.type = PR_U32;
+  a.u32 = uint32_t(value);
+  return a;
+}
+pr_argument f32(float value) {
+  pr_argument a{};
+  a.type = PR_F32;
+  a.f32 = value;
+  return a;
+}
+pr_dim3 linear(uint64_t count) { return {uint32_t((count + group - 1) / group), 1, 1}; }
+
+template <class Record> void header(const Record *op, const char *name) {
+  require(op, PR_INVALID_ARGUMENT, (std::string("Missing ") + name + " record").c_str());
+  require(op->version == PR_TENSOR_VERSION_1, PR_UNSUPPORTED,
+          (std::string("Unsupported ") + name + " record version").c_str());
+  require(op->struct_size == sizeof(Record), PR_INVALID_ARGUMENT,
+          (std::string(name) + " record size mismatch").c_str());
+}
+
+void row_limit(uint64_t rows, const char *operation) {
+  if (rows > max_rows)
+    fail(PR_UNSUPPORTED, std::string(operation) + " supports at most " + std::to_string(max_rows) +
+                             " rows (got " + std::to_string(rows) + ")");
+}
+
+} // namespace
+} // namespace pb
+
+using namespace pb;
+
+PB_EXPORT pr_status pr_tensor_desc_contiguous(pr_buffer buffer, uint64_t byte_offset, pr_type dtype,
+                                              uint32_t rank, const uint64_t *dims,
+                                              pr_tensor_desc_v1 *out) {
+  return boundary("tensor_desc_contiguous", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing tensor descriptor output");
+    require(rank <= PR_TENSOR_MAX_RANK, PR_INVALID_ARGUMENT, "Rank exceeds PR_TENSOR_MAX_RANK");
+    require(dims || !rank, PR_INVALID_ARGUMENT, "Missing tensor shape");
+    pr_tensor_desc_v1 d{};
+    d.struct_size = sizeof(d);
+    d.version = PR_TENSOR_VERSION_1;
+    d.buffer = buffer;
+    d.byte_offset = byte_offset;
+    d.dtype = dtype;
+    d.rank = rank;
+    uint64_t stride = 1;
+    for (uint32_t r = rank; r-- > 0;) {
+      d.shape[r] = dims[r];
+      require(stride <= uint64_t(std::numeric_limits<int64_t>::max()), PR_OUT_OF_BOUNDS,
+              "Contiguous stride overflows");
+      d.strides[r] = int64_t(stride);
+      if (dims[r] && !mul(stride, dims[r], stride))
+        fail(PR_OUT_OF_BOUNDS, "Contiguous stride overflows");
+    }
+    *out = d;
+  });
+}
+
+PB_EXPORT pr_status pr_tensor_desc_validate(const pr_tensor_desc_v1 *desc, uint64_t *required_bytes) {
+  return boundary("tensor_desc_validate", [&] {
+    const Layout layout = validate(desc, "tensor");
+    if (required_bytes)
+      *required_bytes = layout.bytes;
+  });
+}
+
+PB_EXPORT pr_status pr_tensor_operators_artifact(void *data, uint64_t capacity, uint64_t *bytes) {
+  return boundary("tensor_operators_artifact", [&] {
+    require(bytes, PR_INVALID_ARGUMENT, "Missing artifact size output");
+    const auto &value = provider_artifact();
+    *bytes = value.size();
+    if (data) {
+      require(capacity >= value.size(), PR_OUT_OF_BOUNDS, "Artifact capacity is too small");
+      std::memcpy(data, value.data(), value.size());
+    }
+  });
+}
+
+PB_EXPORT pr_status pr_tensor_operators_load(pr_context context, pr_module *out) {
+  return boundary("tensor_operators_load", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing module output");
+    *out = 0;
+    const auto &value = provider_artifact();
+    call(pr_module_load(context, value.data(), value.size(), out));
+    try {
+      std::lock_guard<std::mutex> lock(registry_mutex);
+      providers().insert(*out);
+    } catch (...) {
+      pr_release(*out);
+      *out = 0;
+      throw;
+    }
+  });
+}
+
+PB_EXPORT pr_status pr_tensor_operators_capabilities(pr_tensor_operators_capabilities_v1 *out) {
+  return boundary("tensor_operators_capabilities", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing capability record");
+    require(out->version == PR_TENSOR_VERSION_1, PR_UNSUPPORTED,
+            "Unsupported tensor capability record version");
+    require(out->struct_size == sizeof(pr_tensor_operators_capabilities_v1), PR_INVALID_ARGUMENT,
+            "Tensor capability record size mismatch");
+    pr_tensor_operators_capabilities_v1 caps{};
+    caps.struct_size = sizeof(caps);
+    caps.version = PR_TENSOR_VERSION_1;
+    caps.operations = PR_TENSOR_OP_MATMUL | PR_TENSOR_OP_BIAS_ACTIVATION | PR_TENSOR_OP_LAYER_NORM |
+                      PR_TENSOR_OP_ADD;
+    caps.activations = PR_TENSOR_ACTIVATION_BIT(PR_ACTIVATION_NONE) |
+                       PR_TENSOR_ACTIVATION_BIT(PR_ACTIVATION_RELU) |
+                       PR_TENSOR_ACTIVATION_BIT(PR_ACTIVATION_GELU_TANH);
+    caps.reductions = 0;
+    caps.max_tensor_elements = max_elements;
+    caps.max_row_operator_rows = max_rows;
+    caps.max_layer_norm_columns = max_layer_norm_columns;
+    *out = caps;
+  });
+}
+
+PB_EXPORT pr_status pr_matmul_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
+                                  pr_event *out) {
+  return boundary("matmul_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    require(op, PR_INVALID_ARGUMENT, "Missing matmul record");
+    require(op->version == PR_TENSOR_VERSION_1, PR_UNSUPPORTED, "Unsupported matmul record version");
+    require(op->struct_size == sizeof(pr_matmul_v1), PR_INVALID_ARGUMENT, "Matmul record size mismatch");
+    require(op->transpose_a <= 1 && op->transpose_b <= 1, PR_INVALID_ARGUMENT,
+            "Transpose flags must be 0 or 1");
+    require(op->a && op->b && op->c, PR_INVALID_ARGUMENT, "Missing matmul tensor");
+    const Layout a = operand(op->a, "A", 2), b = operand(op->b, "B", 2), c = operand(op->c, "C", 2);
+    const uint64_t m = op->m, n = op->n, k = op->k;
+    require(m <= max_elements && n <= max_elements && k <= max_elements, PR_UNSUPPORTED,
+            "Matmul dimensions must not exceed INT32_MAX");
+    if (op->transpose_a)
+      expect_dims(op->a, "A (transposed storage [k,m])", {k, m});
+    else
+      expect_dims(op->a, "A [m,k]", {m, k});
+    if (op->transpose_b)
+      expect_dims(op->b, "B (transposed storage [n,k])", {n, k});
+    else
+      expect_dims(op->b, "B [k,n]", {k, n});
+    expect_dims(op->c, "C [m,n]", {m, n});
+    no_alias(op->c, c, op->a, a, "A");
+    no_alias(op->c, c, op->b, b, "B");
+    same_context(queue, operators, {{op->a, "A"}, {op->b, "B"}, {op->c, "C"}});
+    Owned fn;
+    kernel(operators, k ? "paralyn_matmul_f32" : "paralyn_fill_f32", fn);
+    if (!m || !n)
+      return; // no output elements: nothing is submitted and no event is invented
+    Owned cv;
+    view(op->c, c, PR_READ_WRITE, cv);
+    if (!k) {
+      const std::array<pr_argument, 3> args{buffer(cv), u32(m * n), f32(0.0f)};
+      call(pr_launch(queue, fn.handle, linear(m * n), {group, 1, 1}, args.data(), 3, out));
+      return;
+    }
+    Owned av, bv;
+    view(op->a, a, PR_READ, av);
+    view(op->b, b, PR_READ, bv);
+    const std::array<pr_argument, 8> args{buffer(av), buffer(bv), buffer(cv), u32(m), u32(n), u32(k),
+                                          u32(op->transpose_a), u32(op->transpose_b)};
+    const pr_dim3 grid{uint32_t((n + tile - 1) / tile), uint32_t((m + tile - 1) / tile), 1};
+    call(pr_launch(queue, fn.handle, grid, {tile, tile, 1}, args.data(), 8, out));
+  });
+}
+
+PB_EXPORT pr_status pr_bias_activation_f32(pr_queue queue, pr_module operators,
+                                           const pr_bias_activation_v1 *op, pr_event *out) {
+  return boundary("bias_activation_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    require(op, PR_INVALID_ARGUMENT, "Missing bias/activation record");
+    require(op->version == PR_TENSOR_VERSION_1, PR_UNSUPPORTED,
+            "Unsupported bias/activation record version");
+    require(op->struct_size == sizeof(pr_bias_activation_v1), PR_INVALID_ARGUMENT,
+            "Bias/activation record size mismatch");
+    require(op->activation == PR_ACTIVATION_NONE || op->activation == PR_ACTIVATION_RELU ||
+                op->activation == PR_ACTIVATION_GELU_TANH,
+            PR_INVALID_ARGUMENT, "Unknown activation");
+    require(op->reserved == 0, PR_INVALID_ARGUMENT, "Reserved field must be zero");
+    require(op->x && op->out, PR_INVALID_ARGUMENT, "Missing input or output tensor");
+    const Layout x = operand(op->x, "x", 2), o = operand(op->out, "out", 2);
+    const uint64_t rows = op->x->shape[0], columns = op->x->shape[1];
+    expect_dims(op->out, "out", {rows, columns});
+    Layout bias;
+    if (op->bias) {
+      bias = operand(op->bias, "bias", 1);
+      if (op->bias->shape[0] != columns)
+        fail(PR_INVALID_ARGUMENT, "bias shape " + shape_text(op->bias) + " does not match expected [" +
+                                      std::to_string(columns) + "]");
+    }
+    no_alias(op->out, o, op->x, x, "x");
+    no_alias(op->out, o, op->bias, bias, "bias");
+    same_context(queue, operators, {{op->x, "x"}, {op->bias, "bias"}, {op->out, "out"}});
+    Owned fn;
+    kernel(operators, op->bias ? "paralyn_bias_activation_f32" : "paralyn_activation_f32", fn);
+    const uint64_t count = rows * columns;
+    if (!count)
+      return;
+    Owned xv, ov, bv;
+    view(op->x, x, PR_READ, xv);
+    view(op->out, o, PR_READ_WRITE, ov);
+    if (op->bias) {
+      view(op->bias, bias, PR_READ, bv);
+      const std::array<pr_argument, 6> args{buffer(xv), buffer(bv), buffer(ov), u32(count),
+                                            u32(columns), u32(op->activation)};
+      call(pr_launch(queue, fn.handle, linear(count), {group, 1, 1}, args.data(), 6, out));
+    } else {
+      const std::array<pr_argument, 4> args{buffer(xv), buffer(ov), u32(count), u32(op->activation)};
+      call(pr_launch(queue, fn.handle, linear(count), {group, 1, 1}, args.data(), 4, out));
+    }
+  });
+}
+
+// The remaining transformer-block operators keep their symbols and record checks;
+// their kernels are not part of this build.
+PB_EXPORT pr_status pr_batched_matmul_f32(pr_queue, pr_module, const pr_batched_matmul_v1 *op,
+                                          pr_event *out) {
+  return boundary("batched_matmul_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    header(op, "batched matmul");
+    fail(PR_UNSUPPORTED, "Batched matmul has no sm_100a implementation in this build");
+  });
+}
+
+PB_EXPORT pr_status pr_reduce_rows_f32(pr_queue, pr_module, const pr_reduce_rows_v1 *op,
+                                       pr_event *out) {
+  return boundary("reduce_rows_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    header(op, "row reduction");
+    fail(PR_UNSUPPORTED, "Row reductions have no sm_100a implementation in this build");
+  });
+}
+
+PB_EXPORT pr_status pr_softmax_rows_f32(pr_queue, pr_module, const pr_softmax_rows_v1 *op,
+                                        pr_event *out) {
+  return boundary("softmax_rows_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    header(op, "softmax");
+    fail(PR_UNSUPPORTED, "Row softmax has no sm_100a implementation in this build");
+  });
+}
+
+PB_EXPORT pr_status pr_layer_norm_f32(pr_queue queue, pr_module operators, const pr_layer_norm_v1 *op,
+                                      pr_event *out) {
+  return boundary("layer_norm_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    header(op, "layer norm");
+    require(std::isfinite(op->epsilon) && op->epsilon > 0.0f, PR_INVALID_ARGUMENT,
+            "epsilon must be finite and greater than zero");
+    require(op->reserved == 0, PR_INVALID_ARGUMENT, "Reserved field must be zero");
+    require(op->x && op->gamma && op->beta && op->out, PR_INVALID_ARGUMENT,
+            "Missing layer norm tensor (x, gamma, beta and out are required)");
+    const Layout x = operand(op->x, "x", 2), g = operand(op->gamma, "gamma", 1),
+                 b = operand(op->beta, "beta", 1), o = operand(op->out, "out", 2);
+    const uint64_t rows = op->x->shape[0], columns = op->x->shape[1];
+    expect_dims(op->out, "out", {rows, columns});
+    expect_dims(op->gamma, "gamma", {columns});
+    expect_dims(op->beta, "beta", {columns});
+    require(columns <= max_layer_norm_columns, PR_UNSUPPORTED,
+            "layer norm supports at most 2^24 columns (exact FP32 column count)");
+    row_limit(rows, "layer norm");
+    no_alias(op->out, o, op->x, x, "x");
+    no_alias(op->out, o, op->gamma, g, "gamma");
+    no_alias(op->out, o, op->beta, b, "beta");
+    same_context(queue, operators,
+                 {{op->x, "x"}, {op->gamma, "gamma"}, {op->beta, "beta"}, {op->out, "out"}});
+    Owned fn;
+    kernel(operators, "paralyn_layer_norm_f32", fn);
+    if (!x.count)
+      return;
+    Owned xv, gv, bv, ov;
+    view(op->x, x, PR_READ, xv);
+    view(op->gamma, g, PR_READ, gv);
+    view(op->beta, b, PR_READ, bv);
+    view(op->out, o, PR_READ_WRITE, ov);
+    const std::array<pr_argument, 6> args{buffer(xv), buffer(gv), buffer(bv), buffer(ov),
+                                          u32(columns), f32(op->epsilon)};
+    call(pr_launch(queue, fn.handle, {uint32_t(rows), 1, 1}, {group, 1, 1}, args.data(), 6, out));
+  });
+}
+
+PB_EXPORT pr_status pr_add_f32(pr_queue queue, pr_module operators, const pr_add_v1 *op, pr_event *out) {
+  return boundary("add_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    header(op, "add");
+    require(op->x && op->y && op->out, PR_INVALID_ARGUMENT, "Missing input or output tensor");
+    const uint32_t rank = op->x->rank;
+    const Layout x = operand(op->x, "x", rank), y = operand(op->y, "y", rank),
+                 o = operand(op->out, "out", rank);
+    for (uint32_t i = 0; i < rank; ++i)
+      if (op->y->shape[i] != op->x->shape[i] || op->out->shape[i] != op->x->shape[i])
+        fail(PR_INVALID_ARGUMENT, "add shapes differ: x " + shape_text(op->x) + ", y " +
+                                      shape_text(op->y) + ", out " + shape_text(op->out));
+    no_alias(op->out, o, op->x, x, "x");
+    no_alias(op->out, o, op->y, y, "y");
+    same_context(queue, operators, {{op->x, "x"}, {op->y, "y"}, {op->out, "out"}});
+    Owned fn;
+    kernel(operators, "paralyn_add_f32", fn);
+    if (!x.count)
+      return;
+    Owned xv, yv, ov;
+    view(op->x, x, PR_READ, xv);
+    view(op->y, y, PR_READ, yv);
+    view(op->out, o, PR_READ_WRITE, ov);
+    const std::array<pr_argument, 4> args{buffer(xv), buffer(yv), buffer(ov), u32(x.count)};
+    call(pr_launch(queue, fn.handle, linear(x.count), {group, 1, 1}, args.data(), 4, out));
+  });
+}

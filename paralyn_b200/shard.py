@@ -1,0 +1,115 @@
+"""Row sharding of the GEMM -> LayerNorm path across the GPUs of one node.
+
+GEMM rows and LayerNorm rows are independent, so a rank computes the rows
+[r0, r1) of X with the whole of W on its own device: Z = X[r0:r1] W, then
+Y = LayerNorm(Z) with replicated gamma/beta. There is no exchange on the data
+path; the gathered output, when a caller wants one, is a separate step.
+
+One process drives one GPU (RANK / LOCAL_RANK / WORLD_SIZE from the launcher).
+Each rank opens its own context "cuda:LOCAL_RANK" and calls the unchanged
+reference entry points (pr_matmul_f32, pr_layer_norm_f32) on descriptors of its
+shard; the synthetic inputs of a shard are the same draws the unsharded tensor
+would use, so the union of the shards is bit-identical to one-device results.
+"""
+import os
+from dataclasses import dataclass
+
+from . import b200
+from .native import Context
+from .tensor import TensorDescriptor, layer_norm_into, matmul_into, operators_of
+
+
+def row_range(rows, world, rank):
+    """Balanced contiguous [r0, r1) of `rows` for `rank` of `world`."""
+    if not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, extra = divmod(rows, world)
+    r0 = rank * base + min(rank, extra)
+    return r0, r0 + base + (1 if rank < extra else 0)
+
+
+@dataclass(frozen=True)
+class Topology:
+    rank: int
+    world: int
+    local_rank: int
+
+    @classmethod
+    def from_environment(cls):
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", str(rank)))
+        return cls(rank, world, local)
+
+    @property
+    def selector(self):
+        return f"cuda:{self.local_rank}"
+
+
+class ChainShard:
+    """One rank's part of Y = LayerNorm(X W) for X [rows, k], W [k, n].
+
+    Buffers live on the rank's device for the object's lifetime: X rows
+    [r0, r1), W, gamma, beta, the GEMM output Z and the result Y.
+    Inputs come from the seeded stream of `seed`: X ~ N(0, 1) first, then
+    W ~ N(0, w_std); gamma = 1, beta = 0 unless given.
+    """
+
+    def __init__(self, context, rows, k, n, world=1, rank=0, *, seed=4, w_std=1.0 / 64.0, epsilon=1e-5):
+        self.context = context
+        self.rows, self.k, self.n, self.epsilon = rows, k, n, epsilon
+        self.r0, self.r1 = row_range(rows, world, rank)
+        self.local_rows = self.r1 - self.r0
+        self.resources = operators_of(context)
+        self.queue = self.resources.queue
+        m = self.local_rows
+        self.x = context.buffer(4 * m * k)
+        self.w = context.buffer(4 * k * n)
+        self.gamma = context.buffer(4 * n)
+        self.beta = context.buffer(4 * n)
+        self.z = context.buffer(4 * m * n)
+        self.y = context.buffer(4 * m * n)
+        self.xd = TensorDescriptor(self.x, (m, k))
+        self.wd = TensorDescriptor(self.w, (k, n))
+        self.gd = TensorDescriptor(self.gamma, (n,))
+        self.bd = TensorDescriptor(self.beta, (n,))
+        self.zd = TensorDescriptor(self.z, (m, n))
+        self.yd = TensorDescriptor(self.y, (m, n))
+        self.seed, self.w_std = seed, w_std
+
+    def fill_synthetic(self, gamma=1.0, beta=0.0):
+        """Device-side generation of this shard's inputs (draw offsets of the full stream)."""
+        events = [
+            b200.fill_synthetic_into(self.queue, self.xd, seed=self.seed, first_draw=2 * self.r0 * self.k,
+                                     distribution=b200.NORMAL, p0=0.0, p1=1.0),
+            b200.fill_synthetic_into(self.queue, self.wd, seed=self.seed, first_draw=2 * self.rows * self.k,
+                                     distribution=b200.NORMAL, p0=0.0, p1=self.w_std),
+        ]
+        import numpy as np
+        self.gamma.write(np.full(self.n, gamma, np.float32))
+        self.beta.write(np.full(self.n, beta, np.float32))
+        for e in events:
+            if e is not None:
+                e.wait()
+                e.close()
+
+    def step(self):
+        """Enqueue Z = X W and Y = LayerNorm(Z); returns the two events."""
+        mm = matmul_into(self.queue, self.resources.module, self.xd, self.wd, self.zd,
+                         m=self.local_rows, n=self.n, k=self.k)
+        ln = layer_norm_into(self.queue, self.resources.module, self.zd, self.gd, self.bd, self.yd,
+                             epsilon=self.epsilon)
+        return mm, ln
+
+    def flops(self):
+        return 2 * self.local_rows * self.n * self.k
+
+    def close(self):
+        for buf in (self.x, self.w, self.gamma, self.beta, self.z, self.y):
+            buf.close()
+
+
+def open_rank_context():
+    """The calling rank's topology and its context on cuda:LOCAL_RANK."""
+    topology = Topology.from_environment()
+    return topology, Context(topology.selector)

@@ -1,0 +1,132 @@
+"""GPU parity of pr_matmul_f32 against the oracle.
+
+Modes (paralyn/b200.h): REFERENCE must equal the sequential FP32 checker bit for
+bit (tests/native/tensor_tests.cpp:62-85,143-146); FFMA, TF32X3 and AUTO must
+satisfy the FP32 contract |C - C_exact| <= 2*K*2^-24*sum|a||b| per element.
+Shapes follow the reference suite ({1,15,16,17,33,47,65,129,257,300}, all four
+transpose combinations, byte offsets and canaries, tensor_tests.cpp:121-151); the
+MLP output SHA-256 of docs/tensors-matmul.md:79 is reproduced in REFERENCE mode;
+the 4096^3 benchmark shape is checked on sampled rows.
+"""
+import hashlib
+import importlib
+
+import numpy as np
+import pytest
+
+import oracle
+import paralyn_b200 as p
+from paralyn_b200 import synthetic
+
+from test_oracle import MLP_OUTPUT_SHA256, mlp_inputs
+
+pytestmark = pytest.mark.gpu
+T = importlib.import_module("paralyn_b200.tensor")
+SIZES = (1, 15, 16, 17, 33, 47, 65, 129, 257, 300)
+
+
+def gpu_matmul(context, a, b, m, n, k, ta=False, tb=False):
+    """Matmul through descriptors with 12-byte offsets and canaries (tensor_tests.cpp:126-136)."""
+    res = T.operators_of(context)
+    canary = np.float32(-777.0)
+
+    def upload(values, before, after):
+        data = np.concatenate([np.full(before, canary, np.float32), values.ravel(), np.full(after, canary, np.float32)])
+        buf = context.buffer(data.nbytes)
+        buf.write(data)
+        return buf
+
+    ab, bb = upload(a, 3, 2), upload(b, 1, 5)
+    cb = upload(np.full(m * n, 12345.0, np.float32), 3, 4)
+    event = T.matmul_into(res.queue, res.module, T.TensorDescriptor(ab, (k, m) if ta else (m, k), 12),
+                          T.TensorDescriptor(bb, (n, k) if tb else (k, n), 4),
+                          T.TensorDescriptor(cb, (m, n), 12), m=m, n=n, k=k, transpose_a=ta, transpose_b=tb)
+    out = np.frombuffer(cb.read(), np.float32)
+    assert np.all(out[:3] == canary) and np.all(out[-4:] == canary), "canary overwritten"
+    c = out[3:3 + m * n].reshape(m, n).copy()
+    for x in (event, ab, bb, cb):
+        if x is not None:
+            x.close()
+    return event, c
+
+
+@pytest.mark.parametrize("ta", (False, True))
+@pytest.mark.parametrize("tb", (False, True))
+def test_reference_order_is_bit_exact(context, ta, tb):
+    p.set_matmul_mode(context, p.MatmulMode.REFERENCE)
+    for i, (m, n, k) in enumerate([(s, t, u) for s in SIZES for t in SIZES[::3] for u in SIZES[1::3]]):
+        a = synthetic.uniform(1000 + i, 0, m * k)
+        b = synthetic.uniform(2000 + i, 0, k * n)
+        event, c = gpu_matmul(context, a, b, m, n, k, ta, tb)
+        assert event is not None
+        assert c.tobytes() == oracle.matmul(a, b, m, n, k, ta, tb).tobytes(), (m, n, k, ta, tb)
+
+
+@pytest.mark.parametrize("mode", (p.MatmulMode.FFMA, p.MatmulMode.TF32X3, p.MatmulMode.AUTO))
+@pytest.mark.parametrize("ta,tb", ((False, False), (True, False), (False, True), (True, True)))
+def test_fast_modes_meet_fp32_contract(context, mode, ta, tb):
+    p.set_matmul_mode(context, mode)
+    for i, (m, n, k) in enumerate(((1, 1, 1), (17, 33, 15), (129, 300, 257), (300, 129, 64), (256, 256, 512),
+                                   (130, 260, 1000))):
+        a = synthetic.uniform(3000 + i, 0, m * k)
+        b = synthetic.uniform(4000 + i, 0, k * n)
+        _, c = gpu_matmul(context, a, b, m, n, k, ta, tb)
+        exact, magnitude = oracle.matmul_exact(a, b, m, n, k, ta, tb)
+        bound = oracle.matmul_tolerance(magnitude, k)
+        assert np.all(np.abs(c.astype(np.float64) - exact) <= bound), (mode, m, n, k)
+
+
+def test_empty_and_k0(context):
+    p.set_matmul_mode(context, p.MatmulMode.AUTO)
+    event, c = gpu_matmul(context, np.zeros(0, np.float32), np.zeros(0, np.float32), 3, 5, 0)
+    assert event is not None and np.all(c == 0.0) and not np.signbit(c).any()
+    event, _ = gpu_matmul(context, np.zeros(0, np.float32), np.zeros(10, np.float32), 0, 5, 2)
+    assert event is None
+
+
+def test_mlp_golden_hash_on_gpu(context):
+    p.set_matmul_mode(context, p.MatmulMode.REFERENCE)
+    x, w1, b1, w2, b2 = mlp_inputs()
+    with p.tensor(x, shape=(64, 257), context=context) as tx, p.tensor(w1, shape=(257, 130), context=context) as tw1, \
+            p.tensor(b1, shape=(130,), context=context) as tb1, p.tensor(w2, shape=(130, 11), context=context) as tw2, \
+            p.tensor(b2, shape=(11,), context=context) as tb2:
+        with p.matmul(tx, tw1) as z1, p.bias_add(z1, tb1, relu=True) as h, p.matmul(h, tw2) as z2, \
+                p.bias_add(z2, tb2) as y:
+            out = np.asarray(y.to_host(), np.float32)
+    assert hashlib.sha256(out.astype("<f4").tobytes()).hexdigest() == MLP_OUTPUT_SHA256
+
+
+@pytest.mark.parametrize("mode", (p.MatmulMode.AUTO, p.MatmulMode.FFMA))
+def test_benchmark_shape_sampled_rows(context, mode):
+    # C = A B, M = N = K = 4096, A, B ~ U[-1,1) from seed 3 (one stream: A then B).
+    p.set_matmul_mode(context, mode)
+    m = n = k = 4096
+    a = synthetic.uniform(3, 0, m * k)
+    b = synthetic.uniform(3, m * k, k * n)
+    with p.tensor(a, shape=(m, k), context=context) as ta, p.tensor(b, shape=(k, n), context=context) as tb, \
+            p.matmul(ta, tb) as tc:
+        c = np.asarray(tc.to_host(), np.float32).reshape(m, n)
+    rows = np.array([0, 1, 127, 128, 2047, 4000, 4095])
+    exact, magnitude = oracle.matmul_exact(a.reshape(m, k)[rows].ravel(), b, len(rows), n, k)
+    assert np.all(np.abs(c[rows].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
+
+
+def test_matmul_validation(context):
+    res = T.operators_of(context)
+    buf = context.buffer(4096)
+    d = T.TensorDescriptor
+    with pytest.raises(p.Error) as error:  # C overlapping A
+        T.matmul_into(res.queue, res.module, d(buf, (4, 4)), d(buf, (4, 4), 64), d(buf, (4, 4), 32), m=4, n=4, k=4)
+    assert error.value.code == p.Status.INVALID_ARGUMENT and error.value.operation == "matmul_f32"
+    with pytest.raises(p.Error) as error:  # C in A's allocation at disjoint bytes
+        T.matmul_into(res.queue, res.module, d(buf, (4, 4)), d(buf, (4, 4), 64), d(buf, (4, 4), 1024), m=4, n=4, k=4)
+    assert error.value.code == p.Status.UNSUPPORTED
+    c = context.buffer(64)
+    with pytest.raises(p.Error) as error:  # shape disagreement
+        T.matmul_into(res.queue, res.module, d(buf, (4, 3)), d(buf, (4, 4), 64), d(c, (4, 4)), m=4, n=4, k=4)
+    assert error.value.code == p.Status.INVALID_ARGUMENT
+    with pytest.raises(p.Error) as error:
+        T.matmul_into(res.queue, res.module, d(buf, (4, 4)), d(buf, (4, 4), 64), d(c, (4, 4)), m=4, n=4, k=4 + (1 << 31))
+    assert error.value.code in (p.Status.UNSUPPORTED, p.Status.INVALID_ARGUMENT)
+    c.close()
+    buf.close()

@@ -1,10 +1,405 @@
-// 3xTF32 tensor-core GEMM (tcgen05) — not yet part of this build; the launcher
-// declines every shape so matmul falls back to the SIMT FFMA kernel.
+// FP32 GEMM on the sm_100a tensor cores by 3xTF32 splitting (tcgen05 + TMA + TMEM).
+//
+// Every FP32 operand x is split into two TF32 values, hi = rna_tf32(x) and
+// lo = rna_tf32(x - hi) (x - hi is exact in FP32), so x = hi + lo + r with
+// |r| <= 2^-22 |x|. Each product is a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi (the
+// dropped a_lo*b_lo and the residuals are <= ~2^-20.4 |a*b|), accumulated in FP32
+// in tensor memory. For k >= 16 this is far inside the FP32 contract
+// |C - C_exact| <= 2*k*2^-24*sum|a||b| that the FFMA path also meets; smaller k is
+// declined and runs on the SIMT kernel. Non-finite inputs can turn an
+// infinite product into NaN (inf - inf in the split).
+//
+// Structure:
+//  1. split kernel: op(A) -> A_hi, A_lo [M_pad][K_pad] and op(B)^T -> B_hi, B_lo
+//     [N_pad][K_pad] in the context workspace, K contiguous, zero padded (one read,
+//     two writes of each operand; a 32x32 shared-memory transpose for the
+//     transposed layouts).
+//  2. GEMM kernel, one 128x256 output tile per CTA, 6 warps:
+//     warp 0 lane 0: TMA producer. Each 16-deep k-slice is four 2-D boxes
+//       (A_hi, A_lo 128x16; B_hi, B_lo 256x16; 64-byte rows, SWIZZLE_64B) into a
+//       4-stage ring of 48 KB stages, signalled by mbarrier transaction counts.
+//     warp 1: allocates 256 TMEM columns; lane 0 issues per 8-deep step three
+//       tcgen05.mma.kind::tf32 (128x256x8, both operands K-major from shared
+//       memory descriptors) and releases each stage with tcgen05.commit.
+//     warps 2-5: epilogue. tcgen05.ld 32 lanes x 32 columns per warp, masked
+//       stores to C (row stride ldc).
+//  Every wait is bounded (about two seconds of SM clock); on expiry the kernel
+//  records a status code in host-mapped memory, stops issuing, frees its TMEM and
+//  returns, and the engine reports PR_EXECUTION_FAILED.
 #include "../runtime/builtin.hpp"
+#include <cuda.h>
+#include <algorithm>
 
 namespace pb {
-bool launch_tf32x3_gemm(Launch &, const float *, const float *, float *, int64_t, int64_t, int64_t,
-                        int64_t, int64_t, int64_t, bool, bool) {
-  return false;
+namespace {
+
+constexpr int TM = 128, TN = 256, TK = 16, STAGES = 4, THREADS = 192;
+constexpr int A_BYTES = TM * TK * 4, B_BYTES = TN * TK * 4;
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t TMEM_COLUMNS = 256;
+constexpr long long WAIT_CYCLES = 4000000000ll; // ~2 s at 1.9 GHz
+constexpr int STATUS_TIMEOUT_PRODUCER = 0x7f3201, STATUS_TIMEOUT_MMA = 0x7f3202,
+              STATUS_TIMEOUT_EPILOGUE = 0x7f3203;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: false when the phase did not complete within WAIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity))
+    return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - start > WAIT_CYCLES)
+      return false;
+  return true;
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_64B (64-byte rows, 8-row
+// 512-byte atoms): start >> 4, leading byte offset 16 (unused for swizzled
+// K-major), stride byte offset 512, descriptor version 1, layout type 4.
+__device__ __forceinline__ uint64_t desc_k_sw64(uint32_t addr) {
+  return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(16 >> 4) << 16) | (uint64_t(512 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(4) << 61);
+}
+
+// Instruction descriptor: D f32, A and B tf32, both K-major, N = 256, M = 128.
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(TN >> 3) << 17) |
+                           (uint32_t(TM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_load_32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi/lo split of op(X) into [rows_pad][k_pad] (K contiguous), zero padded.
+// Element (r, k) of op(X) is x[r*ld + k], or x[k*ld + r] when `transposed`.
+__global__ void __launch_bounds__(256) split_tf32(const float *__restrict__ x, int64_t ld, int transposed,
+                                                  int64_t rows, int64_t k, float *__restrict__ hi,
+                                                  float *__restrict__ lo, int64_t k_pad) {
+  __shared__ float tile[32][33];
+  const int64_t r0 = int64_t(blockIdx.y) * 32, k0 = int64_t(blockIdx.x) * 32;
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32; // 32 x 8
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int a = ty + 8 * j;
+    if (!transposed) {
+      const int64_t r = r0 + a, kk = k0 + tx;
+      tile[a][tx] = (r < rows && kk < k) ? x[r * ld + kk] : 0.0f;
+    } else {
+      const int64_t kk = k0 + a, r = r0 + tx;
+      tile[tx][a] = (r < rows && kk < k) ? x[kk * ld + r] : 0.0f;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int a = ty + 8 * j;
+    const float v = tile[a][tx];
+    const float h = tf32_rna(v);
+    const float l = tf32_rna(v - h);
+    const int64_t offset = (r0 + a) * k_pad + k0 + tx;
+    hi[offset] = h;
+    lo[offset] = l;
+  }
+}
+
+struct TileArgs {
+  float *c;
+  int64_t m, n, ldc;
+  int k_blocks, tiles_m, tiles_n;
+  int *status;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tf32x3(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                const TileArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *accum = empty + STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *issued = abort_flag + 1;   // k-slices the producer has requested
+  volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // Grouped raster: 8 tile-rows at a time so consecutive CTAs share B tiles in L2.
+  const int id = blockIdx.x, group = 8, per_group = group * args.tiles_n;
+  const int first_m = (id / per_group) * group;
+  const int rows_in_group = min(group, args.tiles_m - first_m);
+  const int tm = first_m + (id % per_group) % rows_in_group;
+  const int tn = (id % per_group) / rows_in_group;
+  const int m0 = tm * TM, n0 = tn * TN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLUMNS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) { // TMA producer
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (kb >= STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
+          atomicExch(args.status, STATUS_TIMEOUT_PRODUCER);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag)
+          break;
+        uint8_t *stage = smem + s * STAGE_BYTES;
+        mbar_expect_tx(&full[s], STAGE_BYTES);
+        tma_load_2d(stage, &a_hi, &full[s], kb * TK, m0);
+        tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, m0);
+        tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, n0);
+        tma_load_2d(stage + 2 * A_BYTES + B_BYTES, &b_lo, &full[s], kb * TK, n0);
+        *issued = kb + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) { // MMA issuer
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(&full[s], (kb / STAGES) & 1)) {
+          atomicExch(args.status, STATUS_TIMEOUT_MMA);
+          *abort_flag = 1;
+          break;
+        }
+        *consumed = kb + 1;
+        if (*abort_flag)
+          break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t stage = smem_u32(smem + s * STAGE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TK / 8; ++kk) {
+          const uint32_t step = kk * 32; // 8 tf32 = 32 bytes along the 64-byte row
+          const uint64_t ah = desc_k_sw64(stage + step), al = desc_k_sw64(stage + A_BYTES + step);
+          const uint64_t bh = desc_k_sw64(stage + 2 * A_BYTES + step);
+          const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + B_BYTES + step);
+          mma_tf32(tmem, ah, bh, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32(tmem, ah, bl, 1u);
+          mma_tf32(tmem, al, bh, 1u);
+        }
+        mma_commit(&empty[s]);
+      }
+      // Always committed: it fires once every MMA this thread issued has finished,
+      // so TMEM is quiet before the epilogue reads it or the block frees it.
+      mma_commit(accum);
+    }
+  } else { // epilogue warps 2..5: TMEM lanes 32*(warp % 4) ..
+    const int sub = warp % 4;
+    // The accumulator is ready after the whole k loop: budget ~2 s plus 50 us per slice.
+    bool ready = mbar_try_wait(accum, 0);
+    const long long start = clock64(), budget = WAIT_CYCLES + 100000ll * args.k_blocks;
+    while (!ready && clock64() - start < budget)
+      ready = mbar_try_wait(accum, 0);
+    if (!ready) {
+      atomicExch(args.status, STATUS_TIMEOUT_EPILOGUE);
+      *abort_flag = 1;
+    } else if (!*abort_flag) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int64_t row = int64_t(m0) + 32 * sub + lane;
+      float *crow = args.c + row * args.ldc;
+      const bool vec = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 15u) == 0);
+#pragma unroll 1
+      for (int col = 0; col < TN; col += 32) {
+        float v[32];
+        tmem_load_32(tmem + (uint32_t(32 * sub) << 16) + uint32_t(col), v);
+        if (row < args.m) {
+          const int64_t n_first = int64_t(n0) + col;
+          if (vec && n_first + 31 < args.n) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4 *>(crow + n_first + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n_first + j < args.n)
+                crow[n_first + j] = v[j];
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    // Let the copies that were requested but never consumed land (bounded) before
+    // the block's shared memory is released.
+    for (int kb = *consumed; kb < *issued; ++kb)
+      (void)mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLUMNS)
+                 : "memory");
+  }
+}
+
+// ---- host side ----
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                 CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                 CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<EncodeTiled>(nullptr);
+    }
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+bool make_map(CUtensorMap *map, float *base, int64_t rows_pad, int64_t k_pad, uint32_t box_rows) {
+  const EncodeTiled encode = encoder();
+  if (!encode)
+    return false;
+  const cuuint64_t dims[2] = {cuuint64_t(k_pad), cuuint64_t(rows_pad)};
+  const cuuint64_t strides[1] = {cuuint64_t(k_pad) * 4};
+  const cuuint32_t box[2] = {TK, box_rows};
+  const cuuint32_t element[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, element,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int64_t round_up(int64_t v, int64_t to) { return (v + to - 1) / to * to; }
+
+} // namespace
+
+// Plans and enqueues the 3xTF32 GEMM; returns false (nothing enqueued) when the
+// shape is outside what this kernel covers or scratch is unavailable.
+bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                        int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb) {
+  if (k < 16 || m < 1 || n < 1)
+    return false;
+  if (L.matmul_mode == matmul_auto && (k < 64 || m * n < 128 * 256))
+    return false;
+  if (!encoder() || !L.workspace)
+    return false;
+  const int64_t k_pad = round_up(k, 32), m_pad = round_up(m, TM), n_pad = round_up(n, TN);
+  const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / TN;
+  if (tiles_m * tiles_n > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 || n_pad / 32 > 65535)
+    return false; // split-kernel grid.y limit
+  const size_t bytes = size_t(8) * size_t(k_pad) * size_t(m_pad + n_pad);
+  if (L.dry_run)
+    return true;
+  auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
+  if (!scratch)
+    return false;
+  float *ahi = scratch, *alo = ahi + m_pad * k_pad, *bhi = alo + m_pad * k_pad, *blo = bhi + n_pad * k_pad;
+  CUtensorMap maps[4];
+  if (!make_map(&maps[0], ahi, m_pad, k_pad, TM) || !make_map(&maps[1], alo, m_pad, k_pad, TM) ||
+      !make_map(&maps[2], bhi, n_pad, k_pad, TN) || !make_map(&maps[3], blo, n_pad, k_pad, TN))
+    return false;
+  static bool configured[64] = {};
+  if (L.device < 0 || L.device >= 64)
+    return false;
+  if (!configured[L.device]) { // per device: the attribute belongs to the device's context
+    if (cudaFuncSetAttribute(gemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    configured[L.device] = true;
+  }
+  // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi,
+                                                                                    alo, k_pad);
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi,
+                                                                                    blo, k_pad);
+  TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
+  gemm_tf32x3<<<uint32_t(tiles_m * tiles_n), THREADS, SMEM_BYTES, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+  L.kernels = 3;
+  L.variant = "tcgen05_tf32x3";
+  return true;
+}
+
 } // namespace pb

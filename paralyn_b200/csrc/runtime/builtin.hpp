@@ -47,6 +47,10 @@ struct Launch {
   uint32_t matmul_mode = matmul_auto;
   Dim3 grid, block;            // the caller's launch geometry
   std::vector<BoundArg> args;  // in parameter order
+  // Device scratch of at least `bytes`, valid for kernels enqueued on `stream` by
+  // this launch (a grow-only per-context workspace); null when unavailable.
+  void *(*workspace)(void *owner, size_t bytes) = nullptr;
+  void *workspace_owner = nullptr;
   bool dry_run = false;        // validate and plan only; enqueue nothing
   uint32_t kernels = 0;        // device kernels enqueued (filled by the launcher)
   std::string variant;         // which implementation ran (filled by the launcher)

@@ -283,6 +283,8 @@ Engine::~Engine() {
       cudaEventDestroy(e);
     if (stream_)
       cudaStreamDestroy(stream_);
+    if (workspace_)
+      cudaFree(workspace_);
     if (status_host_)
       cudaFreeHost(status_host_);
   } catch (...) {
@@ -442,6 +444,8 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
   launch.grid = grid;
   launch.block = block;
   launch.args = std::move(args);
+  launch.workspace = &Engine::workspace_hook;
+  launch.workspace_owner = this;
   launch.dry_run = true;
   launcher(launch); // validation: throws before anything is enqueued
   launch.dry_run = false;
@@ -584,6 +588,30 @@ Work::~Work() {
 }
 
 static void marker_launch(Launch &L) { L.variant = "marker"; }
+
+// Called by launchers with the engine lock held. Growing waits for the stream so
+// no queued kernel still reads the old block; the old block is then freed.
+void *Engine::workspace_hook(void *self, size_t bytes) {
+  auto *engine = static_cast<Engine *>(self);
+  if (bytes <= engine->workspace_bytes_)
+    return engine->workspace_;
+  const size_t rounded = (bytes + (size_t(64) << 20) - 1) & ~((size_t(64) << 20) - 1);
+  if (engine->workspace_) {
+    if (cudaStreamSynchronize(engine->stream_) != cudaSuccess)
+      return nullptr;
+    cudaFree(engine->workspace_);
+    engine->workspace_ = nullptr;
+    engine->workspace_bytes_ = 0;
+  }
+  void *p = nullptr;
+  if (cudaMalloc(&p, rounded) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  engine->workspace_ = p;
+  engine->workspace_bytes_ = rounded;
+  return p;
+}
 
 std::shared_ptr<Work> Engine::marker() {
   auto work = submit("b200_marker", marker_launch, Dim3{}, Dim3{}, {}, {});

@@ -113,6 +113,9 @@ private:
   void drain_locked();
   cudaEvent_t take_event();
   void recycle(Work &work);
+  static void *workspace_hook(void *self, size_t bytes);
+  void *workspace_ = nullptr;
+  size_t workspace_bytes_ = 0;
 
   DeviceRecord device_;
   cudaStream_t stream_ = nullptr;

@@ -52,6 +52,37 @@ pr_status pr_b200_device_kernel_count(pr_context context, uint64_t *out);
 pr_status pr_b200_marker(pr_queue queue, pr_event *out);
 pr_status pr_b200_event_elapsed(pr_event first, pr_event second, double *seconds);
 
+/* C[m,n] = op(A) op(B) with the 3xTF32 tensor-core kernel, for callers that cannot
+ * allocate device memory. No counterpart in the reference ABI.
+ *
+ * Who needs it: a host framework that owns all device memory and hands a plug-in
+ * only input and output pointers, or a latency-critical loop that must not call
+ * cudaMalloc (which can synchronize the device). pr_matmul_f32 needs a scratch
+ * workspace for the split operands and grows it with cudaMalloc; this entry point
+ * instead uses one fixed 64 MiB array compiled into the library (every GPU that
+ * loads the library holds it until the process exits) and calls no allocator.
+ *
+ * a, b, c are device pointers of the calling thread's current device; A is stored
+ * [m,k] (or [k,m] with transpose_a), B [k,n] (or [n,k] with transpose_b), C [m,n];
+ * lda, ldb, ldc are the row strides in elements of the stored matrices. The work
+ * is enqueued on `stream` (a cudaStream_t; NULL is the legacy default stream) and
+ * the call returns without waiting. `status` (optional, device-accessible) is set
+ * non-zero if a kernel abandoned a bounded wait.
+ *
+ * Limits: 16 <= k, 1 <= m, n, and 8 * round_up(k,32) * (round_up(m,128) +
+ * round_up(n,256)) <= 64 MiB (e.g. 1024 x 1024 x 4096 or 2048^3); larger shapes are
+ * rejected with PR_OUT_OF_BOUNDS. Every call shares the one array and overwrites
+ * the part it reads before reading it, so nothing carries over between calls;
+ * calls that overlap on the GPU (other streams, other threads) race on it.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture. Results satisfy |err| <= 2*k*2^-24*sum|a||b|, like
+ * PR_B200_MATMUL_TF32X3 in pr_matmul_f32. */
+pr_status pr_b200_matmul_tf32x3_static_f32(const float *a, const float *b, float *c, uint64_t m, uint64_t n,
+                                           uint64_t k, uint64_t lda, uint64_t ldb, uint64_t ldc,
+                                           uint32_t transpose_a, uint32_t transpose_b, void *stream,
+                                           int32_t *status);
+
 /* Parses and verifies a module artifact without a device, as pr_module_load
  * would, and writes "kernel=implementation;" for each entry into report
  * (NUL-terminated, truncated to capacity). Same statuses as pr_module_load:

@@ -403,3 +403,108 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
 }
 
 } // namespace pb
+
+// ---- allocation-free variant (pr_b200_matmul_tf32x3_static_f32) ----
+// Same split and GEMM kernels, with the split operands in one fixed device array
+// instead of the context workspace, for callers that cannot allocate device memory.
+#include "../runtime/abi_internal.hpp"
+#include "paralyn/b200.h"
+#include <mutex>
+
+namespace pb {
+namespace {
+
+constexpr size_t STATIC_SCRATCH_BYTES = size_t(64) << 20;
+static __device__ __align__(256) float static_scratch[STATIC_SCRATCH_BYTES / sizeof(float)];
+static __device__ int32_t static_status; // timeout record when the caller passes no status word
+
+constexpr int MAX_DEVICES = 64;
+std::mutex static_setup_mutex;
+void *static_scratch_ptr[MAX_DEVICES] = {};
+int32_t *static_status_ptr[MAX_DEVICES] = {};
+bool static_configured[MAX_DEVICES] = {};
+
+// Once per device, with that device current: the device addresses of the array
+// and the status word (host code cannot use the symbols' host-side names as
+// device addresses), and the kernel's shared-memory limit.
+pr_status static_setup(int device, const char *op) {
+  std::lock_guard<std::mutex> lock(static_setup_mutex);
+  if (static_configured[device])
+    return PR_SUCCESS;
+  void *scratch = nullptr, *status = nullptr;
+  if (cudaGetSymbolAddress(&scratch, static_scratch) != cudaSuccess ||
+      cudaGetSymbolAddress(&status, static_status) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error_fixed(PR_DEVICE_UNAVAILABLE, op, "cudaGetSymbolAddress of the static workspace failed");
+  }
+  if (cudaFuncSetAttribute(gemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error_fixed(PR_DEVICE_UNAVAILABLE, op, "cannot configure the GEMM kernel's shared memory");
+  }
+  static_scratch_ptr[device] = scratch;
+  static_status_ptr[device] = static_cast<int32_t *>(status);
+  static_configured[device] = true;
+  return PR_SUCCESS;
+}
+
+} // namespace
+} // namespace pb
+
+using namespace pb;
+
+PB_EXPORT pr_status pr_b200_matmul_tf32x3_static_f32(const float *a, const float *b, float *c, uint64_t m,
+                                                     uint64_t n, uint64_t k, uint64_t lda, uint64_t ldb,
+                                                     uint64_t ldc, uint32_t transpose_a, uint32_t transpose_b,
+                                                     void *stream, int32_t *status) {
+  static const char op[] = "b200_matmul_tf32x3_static_f32";
+  if (!a || !b || !c)
+    return set_error_fixed(PR_INVALID_ARGUMENT, op, "a, b and c must be device pointers");
+  if (transpose_a > 1 || transpose_b > 1)
+    return set_error_fixed(PR_INVALID_ARGUMENT, op, "Transpose flags must be 0 or 1");
+  if (m < 1 || n < 1 || k < 16)
+    return set_error_fixed(PR_UNSUPPORTED, op, "The 3xTF32 kernel needs m >= 1, n >= 1 and k >= 16");
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+    return set_error_fixed(PR_UNSUPPORTED, op, "Matmul dimensions must not exceed INT32_MAX");
+  if ((transpose_a ? lda < m : lda < k) || (transpose_b ? ldb < k : ldb < n) || ldc < n)
+    return set_error_fixed(PR_INVALID_ARGUMENT, op, "A row stride is smaller than its row");
+  if ((uintptr_t(a) | uintptr_t(b) | uintptr_t(c)) & 3u)
+    return set_error_fixed(PR_INVALID_ARGUMENT, op, "a, b and c must be 4-byte aligned");
+  const int64_t k_pad = round_up(int64_t(k), 32), m_pad = round_up(int64_t(m), TM), n_pad = round_up(int64_t(n), TN);
+  if (uint64_t(8) * uint64_t(k_pad) * uint64_t(m_pad + n_pad) > STATIC_SCRATCH_BYTES)
+    return set_error_fixed(PR_OUT_OF_BOUNDS, op,
+                           "Shape exceeds the 64 MiB static workspace: 8*round_up(k,32)*(round_up(m,128)+"
+                           "round_up(n,256)) bytes must be at most 67108864");
+  if (m_pad / 32 > 65535 || n_pad / 32 > 65535)
+    return set_error_fixed(PR_UNSUPPORTED, op, "Shape exceeds the split kernel's grid");
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= MAX_DEVICES) {
+    cudaGetLastError();
+    return set_error_fixed(PR_DEVICE_UNAVAILABLE, op, "No current CUDA device");
+  }
+  if (!encoder())
+    return set_error_fixed(PR_DEVICE_UNAVAILABLE, op, "cuTensorMapEncodeTiled is unavailable");
+  const pr_status setup = static_setup(device, op);
+  if (setup != PR_SUCCESS)
+    return setup;
+  float *ahi = static_cast<float *>(static_scratch_ptr[device]);
+  float *alo = ahi + m_pad * k_pad, *bhi = alo + m_pad * k_pad, *blo = bhi + n_pad * k_pad;
+  CUtensorMap maps[4];
+  if (!make_map(&maps[0], ahi, m_pad, k_pad, TM) || !make_map(&maps[1], alo, m_pad, k_pad, TM) ||
+      !make_map(&maps[2], bhi, n_pad, k_pad, TN) || !make_map(&maps[3], blo, n_pad, k_pad, TN))
+    return set_error_fixed(PR_INTERNAL_ERROR, op, "Tensor map encoding failed");
+  auto s = static_cast<cudaStream_t>(stream);
+  // The split writes every element of the four operand blocks the GEMM reads
+  // (padding included), so the previous call's contents are never read.
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, s>>>(a, int64_t(lda), transpose_a ? 1 : 0,
+                                                                              int64_t(m), int64_t(k), ahi, alo, k_pad);
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, s>>>(b, int64_t(ldb), transpose_b ? 0 : 1,
+                                                                              int64_t(n), int64_t(k), bhi, blo, k_pad);
+  TileArgs t{c, int64_t(m), int64_t(n), int64_t(ldc), int(k_pad / TK), int(m_pad / TM), int(n_pad / TN),
+             status ? status : static_status_ptr[device]};
+  gemm_tf32x3<<<uint32_t((m_pad / TM) * (n_pad / TN)), THREADS, SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], maps[3], t);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return set_error_fixed(PR_EXECUTION_FAILED, op, cudaGetErrorString(e));
+  clear_error();
+  return PR_SUCCESS;
+}

@@ -368,6 +368,15 @@ pr_status report_error(pr_status code, const char *operation, const std::string 
 
 void clear_error() noexcept { last_error = {}; }
 
+pr_status set_error_fixed(pr_status code, const char *operation, const char *message) noexcept {
+  last_error.code = code;
+  std::strncpy(last_error.operation, operation ? operation : "", sizeof(last_error.operation) - 1);
+  last_error.operation[sizeof(last_error.operation) - 1] = 0;
+  std::strncpy(last_error.message, message ? message : "", sizeof(last_error.message) - 1);
+  last_error.message[sizeof(last_error.message) - 1] = 0;
+  return code;
+}
+
 pr_status handle_context(pr_handle h, HandleKind kind, const void **out) noexcept {
   return api("handle_context", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing context identity output");

@@ -17,6 +17,9 @@ pr_status api(const char *operation, const std::function<void()> &fn) noexcept;
 // Records a failure for `operation` without running anything (returns `code`).
 pr_status report_error(pr_status code, const char *operation, const std::string &message) noexcept;
 void clear_error() noexcept;
+// Records a failure from fixed strings without allocating (for entry points that
+// must not allocate); does not take the API lock or write the event log.
+pr_status set_error_fixed(pr_status code, const char *operation, const char *message) noexcept;
 // Opaque identity of the context that owns a live handle of exactly `kind`.
 pr_status handle_context(pr_handle handle, HandleKind kind, const void **out) noexcept;
 

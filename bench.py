@@ -48,7 +48,9 @@ def parse():
     return ap.parse_args()
 
 
-DEFAULT_STEPS = {"chain": 2, "gemm": 20, "layernorm": 50, "affine": 100, "add": 200}
+# Sized so the timed region lasts about a second (the clock sampler needs several
+# 200 ms samples inside it).
+DEFAULT_STEPS = {"chain": 100, "gemm": 1500, "layernorm": 8000, "affine": 8000, "add": 20000}
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -100,6 +102,8 @@ class Clocks:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            time.sleep(0.4)  # nvidia-smi's first sample arrives before the timed work starts
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
@@ -326,7 +330,7 @@ def run_ours(args, group):
     group.barrier()
     kernels = p.device_kernel_count(ctx) - kernels_before  # markers launch no kernel
     durations = [e.timing().duration_seconds for e in dominant]
-    variant = last_variant(ctx)
+    variant = last_variant(ctx, args.workload)
     for e in timed + [start, stop]:
         e.close()
     worst = group.max(seconds)
@@ -335,10 +339,12 @@ def run_ours(args, group):
 
     e2e = None
     if not args.no_e2e:
-        e2e = end_to_end(w, ctx, group, steps=1 if args.workload == "chain" else steps)
+        # About 2 GB of host<->device traffic per e2e measurement (PCIe-bound).
+        e2e_steps = max(1, min(steps, int(2e9 // (w.h2d + w.d2h))))
+        e2e = end_to_end(w, ctx, group, steps=e2e_steps)
 
     dom = sum(durations) / len(durations)
-    roofline = roofline_for(w, dom, variant)
+    roofline = roofline_for(w, dom, variant, worst)
     line = {"metric": w.metric, "value": round(value, 3), "unit": w.unit, "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": w.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded SplitMix64 stream generated on device)",
@@ -350,15 +356,22 @@ def run_ours(args, group):
     return line
 
 
-def last_variant(ctx):
+DOMINANT_ENTRY = {"chain": "paralyn_matmul_f32", "gemm": "paralyn_matmul_f32",
+                  "layernorm": "paralyn_layer_norm_f32", "affine": "array_affine_scalar", "add": "array_add"}
+
+
+def last_variant(ctx, workload):
+    """Implementation the library chose for the dominant entry (from the evidence log)."""
+    import shutil
     import tempfile
-    d = Path(tempfile.mkdtemp(prefix="paralyn_evidence_")) / "e"
-    ctx.write_evidence(str(d))
-    launches = json.loads((d / "execution.json").read_text())["launches"]
+    root = Path(tempfile.mkdtemp(prefix="paralyn_evidence_"))
+    try:
+        ctx.write_evidence(str(root / "e"))
+        launches = json.loads((root / "e" / "execution.json").read_text())["launches"]
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
     for launch in reversed(launches):
-        if launch["kernel"] not in ("b200_marker", "b200_synthetic_f32"):
-            if launch["kernel"] == "paralyn_layer_norm_f32":
-                continue
+        if launch["kernel"] == DOMINANT_ENTRY[workload]:
             return launch["variant"]
     return None
 
@@ -398,7 +411,10 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}, "fallback"
 
 
-def roofline_for(w, seconds, variant):
+def roofline_for(w, seconds, variant, region_seconds):
+    """Dominant kernel vs its roofline. Tensor-bound kernels timed inside a region of
+    half a second or more are compared with the sustained (power-capped) GEMM figure,
+    shorter ones with the burst figure."""
     peaks, basis = measured_peaks()
     traffic = load_traffic().get(w.name)
     if w.name in ("layernorm", "affine", "add"):
@@ -410,10 +426,13 @@ def roofline_for(w, seconds, variant):
     flops = 2 * (w.chain.local_rows if w.name == "chain" else w.m_local) * w.n * w.k
     achieved = flops / seconds / 1e12
     if variant and "tf32x3" in variant:
-        peak = peaks["bf16_tflops"] / 2 / 3
+        sustained = region_seconds >= 0.5 and "bf16_tflops_sustained" in peaks
+        peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"] / 2 / 3
+        which = "sustained" if sustained else "burst"
         return {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
-                "peak_basis": f"{basis} bf16 cuBLAS burst / 2 (TF32 rate) / 3 (three TF32 products per FP32 product)"}
+                "peak_basis": f"{basis} bf16 cuBLAS {which} / 2 (TF32 rate) / 3 (three TF32 products per "
+                              "FP32 product)"}
     sms = 148
     peak = sms * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
     return {"bound": "fp32_ffma", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",

@@ -307,7 +307,8 @@ def run_ours(args, group):
     world = group.world
     ctx = p.Context(f"cuda:{group.local_rank}")
     w = Workload(args.workload, ctx, group)
-    steps = args.steps or DEFAULT_STEPS[args.workload]
+    # Sharded workloads shrink per GPU as N grows; keep the timed region near a second.
+    steps = args.steps or DEFAULT_STEPS[args.workload] * (world if w.scaling == "strong" else 1)
     warm = []
     for _ in range(args.warmup):
         warm += w.step()[0]
@@ -379,6 +380,7 @@ def last_variant(ctx, workload):
 def end_to_end(w, ctx, group, steps):
     """Same steps with host buffers: pinned inputs copied in, result copied out, every step."""
     import torch
+    torch.cuda.set_device(group.local_rank)  # pinned host memory comes from this rank's GPU context
     ins, (out_buf, out_bytes) = w.io_buffers()
     pinned_in = [(buf, torch.empty(nbytes, dtype=torch.uint8, pin_memory=True), nbytes) for buf, nbytes in ins]
     for buf, host, nbytes in pinned_in:  # the device's current inputs become the host copy
@@ -453,6 +455,7 @@ def cpu_sample(workload, budget_seconds):
     import numpy as np
     import oracle
     from paralyn_b200 import synthetic
+    oracle.use_all_cores()
     if workload in ("chain", "gemm"):
         k = n = 4096
         b = synthetic.normal(4, 0, k * n, 0.0, 1.0 / 64) if workload == "chain" else synthetic.uniform(3, 0, k * n)

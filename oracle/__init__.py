@@ -37,6 +37,7 @@ def lib():
         _lib = _c.CDLL(str(LIBRARY))
         sig = {
             "orc_threads": (_c.c_int, []),
+            "orc_set_threads": (None, [_c.c_int]),
             "orc_add_f32": (None, [_f32p, _f32p, _f32p, _size]),
             "orc_add_f32_mt": (None, [_f32p, _f32p, _f32p, _size]),
             "orc_affine_f32": (None, [_f32p, _f32p, _f32p, _size, _c.c_float]),
@@ -69,6 +70,13 @@ def _f32(x):
 
 def threads():
     return lib().orc_threads()
+
+
+def use_all_cores():
+    """Team size = the host threads this process may run on (ignores OMP_NUM_THREADS)."""
+    import os
+    lib().orc_set_threads(len(os.sched_getaffinity(0)))
+    return threads()
 
 
 def add(a, b, threaded=False):

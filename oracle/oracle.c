@@ -325,3 +325,14 @@ void orc_bias_activation_f32(const float *x, const float *bias, float *out, size
       out[i * columns + j] = v;
     }
 }
+
+/* Sets the OpenMP team size of the _mt variants (launchers such as torchrun export
+ * OMP_NUM_THREADS=1 into every process). */
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0)
+    omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}

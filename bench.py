@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", action="store_true",
+                    help="chain: also gather Y on every GPU (LayerNorm writes its rows to all ranks over NVLink)")
     return ap.parse_args()
 
 
@@ -79,6 +81,14 @@ class Group:
         t = torch.tensor([float(value)], dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return t.item()
+
+    def exchange(self, value):
+        """Every rank's `value` (host objects over the gloo control plane)."""
+        if not self.dist:
+            return [value]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, value)
+        return out
 
     def close(self):
         if self.dist:
@@ -147,7 +157,7 @@ class Clocks:
 class Workload:
     """Holds device inputs/outputs for one rank and runs steps through the public API."""
 
-    def __init__(self, name, ctx, group):
+    def __init__(self, name, ctx, group, gather=False):
         import numpy as np
         import importlib
         import paralyn_b200 as p
@@ -162,6 +172,9 @@ class Workload:
             self.rows, self.k, self.n = 65536, 4096, 4096
             self.chain = shard.ChainShard(ctx, self.rows, self.k, self.n, world, rank, seed=4, w_std=1.0 / 64.0)
             self.chain.fill_synthetic()
+            self.gather = None
+            if gather:
+                self.gather = shard.GatheredOutput(ctx, self.rows, self.n, group.exchange, rank)
             self.units_total = 2 * self.rows * self.n * self.k
             self.units_local = self.chain.flops()
             self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "strong"
@@ -170,6 +183,8 @@ class Workload:
                                        "gamma=1, beta=0, eps=1e-5, seed 4",
                            "rows": self.rows, "k": self.k, "n": self.n, "rows_per_gpu": self.chain.local_rows,
                            "parallelism": f"rows{world}", "l2": "inputs larger than L2 (X shard >= 128 MiB)"}
+            if self.gather:
+                self.config["gathered_output"] = "Y gathered on every GPU by the fused LayerNorm (NVLink stores)"
             self.h2d = 4 * self.chain.local_rows * self.k
             self.d2h = 4 * self.chain.local_rows * self.n
         elif name == "gemm":
@@ -263,7 +278,7 @@ class Workload:
         """Enqueue one step; returns (events, dominant-kernel event)."""
         p = self.p
         if self.name == "chain":
-            mm, ln = self.chain.step()
+            mm, ln = self.chain.step(self.gather)
             return [mm, ln], mm
         if self.name == "gemm":
             D = self.T.TensorDescriptor
@@ -306,7 +321,7 @@ def run_ours(args, group):
     from paralyn_b200 import b200
     world = group.world
     ctx = p.Context(f"cuda:{group.local_rank}")
-    w = Workload(args.workload, ctx, group)
+    w = Workload(args.workload, ctx, group, gather=args.gather)
     # Sharded workloads shrink per GPU as N grows; keep the timed region near a second.
     steps = args.steps or DEFAULT_STEPS[args.workload] * (world if w.scaling == "strong" else 1)
     warm = []

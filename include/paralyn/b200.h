@@ -45,6 +45,26 @@ pr_status pr_b200_fill_synthetic_f32(pr_queue queue, const pr_tensor_desc_v1 *ou
  * waits for the queue first. */
 pr_status pr_b200_device_kernel_count(pr_context context, uint64_t *out);
 
+/* ---- Row-sharded outputs gathered over NVLink ----
+ * One process drives one GPU. To gather the rows every rank computes into one
+ * [rows, columns] tensor on every GPU, each rank exports its gathered buffer
+ * (pr_b200_buffer_export: a CUDA IPC handle plus the size, 72 bytes, passed to the
+ * other ranks by any host channel) and imports the others' (pr_b200_buffer_import:
+ * a buffer handle of the importing context that refers to the peer GPU's memory).
+ * pr_b200_layer_norm_gather_f32 then normalizes the local rows and writes each
+ * output row both to op->out and, at row row_offset + i, into every tensor of
+ * `gathered` (local and imported): a fused LayerNorm + all-gather in one kernel
+ * whose stores cross NVLink directly. The gathered tensors are complete once every
+ * rank's command has completed (the kernel ends with a system-scope fence); the
+ * ranks synchronize on the host before reading them. */
+#define PR_B200_PEER_HANDLE_BYTES 72u
+#define PR_B200_MAX_GATHER 8u
+pr_status pr_b200_buffer_export(pr_buffer buffer, void *handle);
+pr_status pr_b200_buffer_import(pr_context context, const void *handle, pr_buffer *out);
+pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module operators, const pr_layer_norm_v1 *op,
+                                        const pr_tensor_desc_v1 *const *gathered, uint32_t count,
+                                        uint64_t row_offset, pr_event *out);
+
 /* Enqueues an empty command whose only effect is a device timestamp on the
  * context queue. pr_b200_event_elapsed returns the device time between the
  * completion of `first` and of `second` (markers or any commands of one context),

@@ -24,6 +24,9 @@ def _b200(lib):
             "pr_b200_matmul_mode_get": (_c.c_int, [h, ptr(u32)]),
             "pr_b200_device_kernel_count": (_c.c_int, [h, ptr(u64)]),
             "pr_b200_module_inspect": (_c.c_int, [_c.c_void_p, u64, _c.c_char_p, u64]),
+            "pr_b200_buffer_export": (_c.c_int, [h, _c.c_void_p]),
+            "pr_b200_buffer_import": (_c.c_int, [h, _c.c_void_p, ptr(h)]),
+            "pr_b200_layer_norm_gather_f32": (_c.c_int, [h, h, _c.c_void_p, _c.c_void_p, u32, u64, ptr(h)]),
             "pr_b200_marker": (_c.c_int, [h, ptr(h)]),
             "pr_b200_event_elapsed": (_c.c_int, [h, h, ptr(_c.c_double)]),
             "pr_b200_fill_synthetic_f32": (_c.c_int, [h, ptr(TensorDescRecord), u64, u64, u32,
@@ -65,6 +68,43 @@ def fill_synthetic_into(queue, descriptor, *, seed, first_draw=0, distribution=U
     handle = _c.c_uint64()
     lib.check(lib.api.pr_b200_fill_synthetic_f32(queue.handle, _c.byref(record), seed, first_draw,
                                                  distribution, p0, p1, _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
+
+
+PEER_HANDLE_BYTES = 72
+
+
+def export_buffer(buffer):
+    """Bytes another process passes to import_buffer to map this buffer (same node)."""
+    lib = _b200(buffer._lib)
+    out = _c.create_string_buffer(PEER_HANDLE_BYTES)
+    lib.check(lib.api.pr_b200_buffer_export(buffer.handle, out))
+    return out.raw
+
+
+def import_buffer(context, handle):
+    """A Buffer of `context` that refers to a peer process's exported buffer."""
+    from .native import Buffer
+    lib = _b200(context._lib)
+    data = _c.create_string_buffer(bytes(handle), PEER_HANDLE_BYTES)
+    result = _c.c_uint64()
+    lib.check(lib.api.pr_b200_buffer_import(context.handle, data, _c.byref(result)))
+    return Buffer._adopt(lib, result.value)
+
+
+def layer_norm_gather_into(queue, operators, x, gamma, beta, out, gathered, *, row_offset, epsilon=1e-5):
+    """LayerNorm of x's rows into `out`, each output row also written at row
+    row_offset + i of every descriptor in `gathered` (local or imported)."""
+    from .tensor import LayerNormRecord, TENSOR_VERSION_1
+    lib = _b200(queue._lib)
+    descs = [d._native() for d in (x, gamma, beta, out)]
+    record = LayerNormRecord(_c.sizeof(LayerNormRecord), TENSOR_VERSION_1, float(epsilon), 0,
+                             *(_c.pointer(d) for d in descs))
+    natives = [g._native() for g in gathered]
+    array = (_c.POINTER(TensorDescRecord) * max(1, len(natives)))(*(_c.pointer(d) for d in natives))
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_layer_norm_gather_f32(queue.handle, operators.handle, _c.byref(record), array,
+                                                    len(natives), row_offset, _c.byref(handle)))
     return Event._adopt(lib, handle.value) if handle.value else None
 
 

@@ -33,6 +33,23 @@ namespace {
 
 constexpr unsigned full_mask = 0xffffffffu;
 
+// Extra destinations of every output row: row r of this launch also lands at row
+// row_offset + r of each dest (tensors of this or peer GPUs, [*, columns]).
+struct Gather {
+  float *dest[8];
+  uint32_t count;
+  uint64_t row_offset;
+};
+
+template <bool GATHER>
+__device__ __forceinline__ void store4(float *yr, const Gather &g, uint64_t row, uint32_t columns, uint32_t col,
+                                       const float4 &y) {
+  *reinterpret_cast<float4 *>(yr + col) = y;
+  if constexpr (GATHER)
+    for (uint32_t d = 0; d < g.count; ++d)
+      *reinterpret_cast<float4 *>(g.dest[d] + (g.row_offset + row) * columns + col) = y;
+}
+
 // Tree over the 8 chains of every thread of the warp (mapping above); returns the
 // reference's p[0] in every lane.
 __device__ __forceinline__ float warp_tree(float (&s)[8]) {
@@ -180,10 +197,11 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
                : "memory");
 }
 
-template <int R>
+template <int R, bool GATHER>
 __global__ void __launch_bounds__(32 * BULK_WARPS, 1)
     layer_norm_bulk(const float *__restrict__ x, const float *__restrict__ gamma, const float *__restrict__ beta,
-                    float *__restrict__ out, uint32_t rows, uint32_t columns, float epsilon, int *status) {
+                    float *__restrict__ out, uint32_t rows, uint32_t columns, float epsilon, int *status,
+                    const Gather gather) {
   extern __shared__ __align__(128) float smem[];
   constexpr int SLOT = 256 * R; // floats
   float *sg = smem, *sb = smem + SLOT;
@@ -244,9 +262,10 @@ __global__ void __launch_bounds__(32 * BULK_WARPS, 1)
       for (int h = 0; h < 2; ++h) {
         const uint32_t col = 256u * i + 128u * h + 4u * lane;
         if (col < columns)
-          *reinterpret_cast<float4 *>(yr + col) =
-              normalize4(*reinterpret_cast<const float4 *>(xs + col), *reinterpret_cast<const float4 *>(sg + col),
-                         *reinterpret_cast<const float4 *>(sb + col), mean, rstd);
+          store4<GATHER>(yr, gather, row, columns, col,
+                         normalize4(*reinterpret_cast<const float4 *>(xs + col),
+                                    *reinterpret_cast<const float4 *>(sg + col),
+                                    *reinterpret_cast<const float4 *>(sb + col), mean, rstd));
       }
     consumed = j + 1;
     // Refill this slot with the row two steps ahead once every lane is done with it.
@@ -265,6 +284,8 @@ __global__ void __launch_bounds__(32 * BULK_WARPS, 1)
   if (!ok)
     for (uint64_t j = consumed; j < issued; ++j)
       (void)mbar_wait(bar0 + j % BULK_SLOTS, uint32_t((j / BULK_SLOTS) & 1));
+  if constexpr (GATHER)
+    __threadfence_system(); // peer stores are visible system-wide when the command completes
 }
 
 // ---- generic: one 256-thread block per row, the reference lane mapping ----
@@ -284,9 +305,10 @@ __device__ __forceinline__ float block_tree(float value, float (*scratch)[32]) {
   return __shfl_sync(full_mask, s, 0);
 }
 
+template <bool GATHER>
 __global__ void __launch_bounds__(256) layer_norm_block_rows(const float *x, const float *gamma,
                                                              const float *beta, float *out,
-                                                             uint32_t columns, float epsilon) {
+                                                             uint32_t columns, float epsilon, const Gather gather) {
   __shared__ float scratch[2][8][32];
   const uint32_t t = threadIdx.x;
   const uint64_t row = blockIdx.x;
@@ -304,8 +326,15 @@ __global__ void __launch_bounds__(256) layer_norm_block_rows(const float *x, con
   }
   const float variance = __fdiv_rn(block_tree(q, scratch[1]), n);
   const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, epsilon)));
-  for (uint32_t j = t; j < columns; j += 256)
-    yr[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[j], mean), rstd), gamma[j]), beta[j]);
+  for (uint32_t j = t; j < columns; j += 256) {
+    const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[j], mean), rstd), gamma[j]), beta[j]);
+    yr[j] = y;
+    if constexpr (GATHER)
+      for (uint32_t d = 0; d < gather.count; ++d)
+        gather.dest[d][(gather.row_offset + row) * columns + j] = y;
+  }
+  if constexpr (GATHER)
+    __threadfence_system();
 }
 
 template <int R>
@@ -319,14 +348,14 @@ template <int R> size_t bulk_smem() {
   return sizeof(float) * 256 * R * (2 + BULK_WARPS * BULK_SLOTS) + 8 * (BULK_WARPS * BULK_SLOTS + 1);
 }
 
-template <int R>
+template <int R, bool GATHER = false>
 bool launch_bulk(Launch &L, const float *x, const float *g, const float *b, float *y, uint32_t rows,
-                 uint32_t columns, float eps) {
+                 uint32_t columns, float eps, const Gather &gather = Gather{}) {
   static bool configured[64] = {};
   if (L.device < 0 || L.device >= 64)
     return false;
   if (!configured[L.device]) {
-    if (cudaFuncSetAttribute(layer_norm_bulk<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(layer_norm_bulk<R, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(bulk_smem<R>())) != cudaSuccess) {
       cudaGetLastError();
       return false;
@@ -334,9 +363,9 @@ bool launch_bulk(Launch &L, const float *x, const float *g, const float *b, floa
     configured[L.device] = true;
   }
   const uint32_t blocks = uint32_t(std::min<uint64_t>(uint64_t(L.sm_count), (rows + BULK_WARPS - 1) / BULK_WARPS));
-  layer_norm_bulk<R><<<blocks, 32 * BULK_WARPS, bulk_smem<R>(), L.stream>>>(x, g, b, y, rows, columns, eps,
-                                                                           L.status);
-  L.variant = "bulk_rows_r" + std::to_string(R);
+  layer_norm_bulk<R, GATHER><<<blocks, 32 * BULK_WARPS, bulk_smem<R>(), L.stream>>>(x, g, b, y, rows, columns,
+                                                                                   eps, L.status, gather);
+  L.variant = std::string(GATHER ? "bulk_rows_gather_r" : "bulk_rows_r") + std::to_string(R);
   return true;
 }
 
@@ -381,8 +410,54 @@ void launch_provider_layer_norm(Launch &L) {
       launch_warp_rows<16>(L, x, g, b, y, rows, columns, eps);
     return;
   }
-  layer_norm_block_rows<<<rows, 256, 0, L.stream>>>(x, g, b, y, columns, eps);
+  layer_norm_block_rows<false><<<rows, 256, 0, L.stream>>>(x, g, b, y, columns, eps, Gather{});
   L.variant = "block_rows";
+}
+
+// (x, gamma, beta, out views, columns, epsilon, rows, row_offset lo/hi, count,
+//  count gathered views): LayerNorm whose output rows are also written into every
+//  gathered tensor at row_offset + row (local or peer memory).
+void launch_layer_norm_gather(Launch &L) {
+  const auto &a = L.args;
+  const uint32_t columns = a[4].u32(), rows = a[6].u32(), count = a[9].u32();
+  const float eps = a[5].f32();
+  const uint64_t row_offset = uint64_t(a[7].u32()) | uint64_t(a[8].u32()) << 32;
+  if (count > 8 || a.size() != 10 + count)
+    throw Failure(PR_INVALID_ARGUMENT, "Malformed gather launch");
+  if (!columns || !rows) {
+    L.variant = "empty";
+    return;
+  }
+  const uint64_t elements = uint64_t(rows) * columns;
+  need_elements(a[0], elements, "x");
+  need_elements(a[1], columns, "gamma");
+  need_elements(a[2], columns, "beta");
+  need_elements(a[3], elements, "out");
+  Gather gather{};
+  gather.count = count;
+  gather.row_offset = row_offset;
+  bool aligned = true;
+  for (uint32_t d = 0; d < count; ++d) {
+    need_elements(a[10 + d], (row_offset + rows) * columns, "gathered");
+    gather.dest[d] = static_cast<float *>(a[10 + d].ptr);
+    aligned = aligned && (uintptr_t(gather.dest[d]) & 15u) == 0;
+  }
+  if (L.dry_run)
+    return;
+  const auto *x = static_cast<const float *>(a[0].ptr);
+  const auto *g = static_cast<const float *>(a[1].ptr);
+  const auto *b = static_cast<const float *>(a[2].ptr);
+  auto *y = static_cast<float *>(a[3].ptr);
+  aligned = aligned && ((uintptr_t(x) | uintptr_t(g) | uintptr_t(b) | uintptr_t(y)) & 15u) == 0;
+  L.kernels = 1;
+  if (aligned && columns % 4 == 0 && columns > 1024 && columns <= 4096) {
+    const bool done = columns > 2048 ? launch_bulk<16, true>(L, x, g, b, y, rows, columns, eps, gather)
+                                     : launch_bulk<8, true>(L, x, g, b, y, rows, columns, eps, gather);
+    if (done)
+      return;
+  }
+  layer_norm_block_rows<true><<<rows, 256, 0, L.stream>>>(x, g, b, y, columns, eps, gather);
+  L.variant = "block_rows_gather";
 }
 
 } // namespace pb

@@ -400,6 +400,19 @@ std::shared_ptr<Engine> context_engine(pr_context context) {
   return get<ContextObj>(context, HandleKind::context)->engine;
 }
 
+pr_buffer add_buffer(pr_context context, std::shared_ptr<Allocation> allocation) {
+  auto ctx = get<ContextObj>(context, HandleKind::context);
+  ctx->engine->check_owner(*allocation);
+  return add(std::make_shared<BufferObj>(ctx, std::move(allocation)));
+}
+
+std::shared_ptr<Allocation> allocation_of(pr_buffer buffer, std::shared_ptr<Engine> *engine) {
+  auto b = get<BufferObj>(buffer, HandleKind::buffer);
+  if (engine)
+    *engine = b->owner->engine;
+  return b->allocation;
+}
+
 std::shared_ptr<Allocation> buffer_allocation(pr_buffer buffer, const void *context) {
   auto b = get<BufferObj>(buffer, HandleKind::buffer);
   require(b->owner.get() == context, PR_CONTEXT_MISMATCH, "Buffer belongs to a different context");

@@ -30,6 +30,10 @@ struct QueueAccess {
 };
 QueueAccess queue_access(pr_queue queue);
 std::shared_ptr<Engine> context_engine(pr_context context);
+// A buffer handle of `context` that owns `allocation` (used for imported peer memory).
+pr_buffer add_buffer(pr_context context, std::shared_ptr<Allocation> allocation);
+// The allocation behind a buffer handle and its owning context's engine.
+std::shared_ptr<Allocation> allocation_of(pr_buffer buffer, std::shared_ptr<Engine> *engine);
 std::shared_ptr<Allocation> buffer_allocation(pr_buffer buffer, const void *context);
 // Publishes an event handle for a submitted command (handle allocated first, as
 // pr_launch does, so a failure never leaves a command without its event).

@@ -63,6 +63,30 @@ PB_EXPORT pr_status pr_b200_device_kernel_count(pr_context context, uint64_t *ou
   });
 }
 
+static_assert(sizeof(PeerHandle) == PR_B200_PEER_HANDLE_BYTES, "peer handle size");
+
+PB_EXPORT pr_status pr_b200_buffer_export(pr_buffer buffer, void *handle) {
+  return api("b200_buffer_export", [&] {
+    require(handle, PR_INVALID_ARGUMENT, "Missing handle output");
+    std::shared_ptr<Engine> engine;
+    auto allocation = allocation_of(buffer, &engine);
+    const PeerHandle h = engine->export_allocation(*allocation);
+    std::memcpy(handle, &h, sizeof(h));
+  });
+}
+
+PB_EXPORT pr_status pr_b200_buffer_import(pr_context context, const void *handle, pr_buffer *out) {
+  return api("b200_buffer_import", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing buffer output");
+    *out = 0;
+    require(handle, PR_INVALID_ARGUMENT, "Missing peer handle");
+    PeerHandle h;
+    std::memcpy(&h, handle, sizeof(h));
+    auto engine = context_engine(context);
+    *out = add_buffer(context, engine->import_allocation(h));
+  });
+}
+
 PB_EXPORT pr_status pr_b200_marker(pr_queue queue, pr_event *out) {
   return api("b200_marker", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");

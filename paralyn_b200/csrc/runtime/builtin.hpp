@@ -51,6 +51,11 @@ struct Launch {
   // this launch (a grow-only per-context workspace); null when unavailable.
   void *(*workspace)(void *owner, size_t bytes) = nullptr;
   void *workspace_owner = nullptr;
+  // A second stream of the context for work that overlaps `stream` inside one
+  // launch, and four timing-free events to order the two. A launcher that uses it
+  // must make `stream` wait for everything it put on `side_stream`.
+  cudaStream_t side_stream = nullptr;
+  cudaEvent_t side_events[4] = {};
   bool dry_run = false;        // validate and plan only; enqueue nothing
   uint32_t kernels = 0;        // device kernels enqueued (filled by the launcher)
   std::string variant;         // which implementation ran (filled by the launcher)

@@ -242,7 +242,10 @@ Allocation::~Allocation() {
   cudaGetDevice(&previous);
   if (previous != device)
     cudaSetDevice(device);
-  cudaFree(ptr);
+  if (imported)
+    cudaIpcCloseMemHandle(ptr);
+  else
+    cudaFree(ptr);
   if (previous >= 0 && previous != device)
     cudaSetDevice(previous);
 }
@@ -258,6 +261,10 @@ Engine::Engine(const DeviceRecord &device)
     cuda_check(e, "cudaHostAlloc(status word)");
   }
   std::memset(status_host_, 0, 64);
+  cuda_check(cudaStreamCreateWithFlags(&side_stream_, cudaStreamNonBlocking),
+             "cudaStreamCreate(side)");
+  for (auto &event : side_events_)
+    cuda_check(cudaEventCreateWithFlags(&event, cudaEventDisableTiming), "cudaEventCreate(side)");
   cuda_check(cudaHostGetDevicePointer(reinterpret_cast<void **>(&status_device_), status_host_, 0),
              "cudaHostGetDevicePointer");
   if (const char *mode = std::getenv("PARALYN_MATMUL_MODE")) {
@@ -283,6 +290,11 @@ Engine::~Engine() {
       cudaEventDestroy(e);
     if (stream_)
       cudaStreamDestroy(stream_);
+    if (side_stream_)
+      cudaStreamDestroy(side_stream_);
+    for (auto event : side_events_)
+      if (event)
+        cudaEventDestroy(event);
     if (workspace_)
       cudaFree(workspace_);
     if (status_host_)
@@ -326,6 +338,39 @@ std::shared_ptr<Allocation> Engine::allocate(size_t bytes) {
   const uint64_t now = accounting_->current.fetch_add(bytes) + bytes;
   uint64_t peak = accounting_->peak.load();
   while (peak < now && !accounting_->peak.compare_exchange_weak(peak, now)) {
+  }
+  return result;
+}
+
+PeerHandle Engine::export_allocation(const Allocation &allocation) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  check_owner(allocation);
+  if (allocation.imported || !allocation.ptr)
+    throw Error(Code::invalid_value, "Only non-empty buffers allocated by this context can be exported");
+  DeviceScope scope(device_.ordinal);
+  PeerHandle h{};
+  const cudaError_t e = cudaIpcGetMemHandle(&h.handle, allocation.ptr);
+  if (e != cudaSuccess)
+    cuda_failure(e, "cudaIpcGetMemHandle");
+  h.bytes = allocation.bytes;
+  return h;
+}
+
+std::shared_ptr<Allocation> Engine::import_allocation(const PeerHandle &handle) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  healthy();
+  if (!handle.bytes)
+    throw Error(Code::invalid_value, "Peer handle describes an empty allocation");
+  DeviceScope scope(device_.ordinal);
+  auto result = std::make_shared<Allocation>();
+  result->device = device_.ordinal;
+  result->bytes = handle.bytes;
+  result->owner = this;
+  result->imported = true;
+  const cudaError_t e = cudaIpcOpenMemHandle(&result->ptr, handle.handle, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    result->ptr = nullptr;
+    cuda_failure(e, "cudaIpcOpenMemHandle");
   }
   return result;
 }
@@ -446,6 +491,9 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
   launch.args = std::move(args);
   launch.workspace = &Engine::workspace_hook;
   launch.workspace_owner = this;
+  launch.side_stream = side_stream_;
+  for (int i = 0; i < 4; ++i)
+    launch.side_events[i] = side_events_[i];
   launch.dry_run = true;
   launcher(launch); // validation: throws before anything is enqueued
   launch.dry_run = false;
@@ -463,6 +511,7 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
     launcher(launch);
   } catch (...) {
     // Part of the command may be enqueued: let it finish before its views go.
+    cudaStreamSynchronize(side_stream_);
     cudaStreamSynchronize(stream_);
     recycle(*work);
     throw;
@@ -597,7 +646,8 @@ void *Engine::workspace_hook(void *self, size_t bytes) {
     return engine->workspace_;
   const size_t rounded = (bytes + (size_t(64) << 20) - 1) & ~((size_t(64) << 20) - 1);
   if (engine->workspace_) {
-    if (cudaStreamSynchronize(engine->stream_) != cudaSuccess)
+    if (cudaStreamSynchronize(engine->side_stream_) != cudaSuccess ||
+        cudaStreamSynchronize(engine->stream_) != cudaSuccess)
       return nullptr;
     cudaFree(engine->workspace_);
     engine->workspace_ = nullptr;

@@ -40,8 +40,16 @@ struct Allocation {
   void *ptr = nullptr;
   size_t bytes = 0;
   const void *owner = nullptr; // identity of the creating engine
+  bool imported = false;       // a peer GPU's allocation mapped into this context (CUDA IPC)
   std::shared_ptr<struct Accounting> accounting;
   ~Allocation();
+};
+
+// What pr_b200_buffer_export hands to another process: the CUDA IPC handle of
+// the allocation and its size.
+struct PeerHandle {
+  cudaIpcMemHandle_t handle;
+  uint64_t bytes;
 };
 
 struct EventInfo {
@@ -78,6 +86,10 @@ public:
 
   const DeviceRecord &device() const { return device_; }
   std::shared_ptr<Allocation> allocate(size_t bytes);
+  PeerHandle export_allocation(const Allocation &allocation);
+  // Maps another process's exported allocation (any GPU of this node) into this
+  // context; kernels of this context then read and write it over NVLink.
+  std::shared_ptr<Allocation> import_allocation(const PeerHandle &handle);
   void write(const std::shared_ptr<Allocation> &, size_t offset, const void *source, size_t bytes);
   void read(const std::shared_ptr<Allocation> &, size_t offset, void *destination, size_t bytes);
   // Checks a pr_launch geometry against the device limits (reference engine.cpp:597-616).
@@ -119,6 +131,8 @@ private:
 
   DeviceRecord device_;
   cudaStream_t stream_ = nullptr;
+  cudaStream_t side_stream_ = nullptr;
+  cudaEvent_t side_events_[4] = {};
   int *status_host_ = nullptr, *status_device_ = nullptr;
   mutable std::mutex mutex_;
   std::vector<std::shared_ptr<Work>> pending_;

@@ -547,3 +547,91 @@ PB_EXPORT pr_status pr_add_f32(pr_queue queue, pr_module operators, const pr_add
     call(pr_launch(queue, fn.handle, linear(x.count), {group, 1, 1}, args.data(), 4, out));
   });
 }
+
+// ---- LayerNorm with the output rows also gathered into peer tensors (b200.h) ----
+namespace pb {
+void launch_layer_norm_gather(Launch &);
+}
+
+PB_EXPORT pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module operators, const pr_layer_norm_v1 *op,
+                                                  const pr_tensor_desc_v1 *const *gathered, uint32_t count,
+                                                  uint64_t row_offset, pr_event *out) {
+  return boundary("layer_norm_gather_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    header(op, "layer norm");
+    require(std::isfinite(op->epsilon) && op->epsilon > 0.0f, PR_INVALID_ARGUMENT,
+            "epsilon must be finite and greater than zero");
+    require(op->reserved == 0, PR_INVALID_ARGUMENT, "Reserved field must be zero");
+    require(op->x && op->gamma && op->beta && op->out, PR_INVALID_ARGUMENT,
+            "Missing layer norm tensor (x, gamma, beta and out are required)");
+    require(count <= 8, PR_INVALID_ARGUMENT, "At most 8 gathered tensors");
+    require(gathered || !count, PR_INVALID_ARGUMENT, "Missing gathered tensors");
+    const Layout x = operand(op->x, "x", 2), g = operand(op->gamma, "gamma", 1),
+                 b = operand(op->beta, "beta", 1), o = operand(op->out, "out", 2);
+    const uint64_t rows = op->x->shape[0], columns = op->x->shape[1];
+    expect_dims(op->out, "out", {rows, columns});
+    expect_dims(op->gamma, "gamma", {columns});
+    expect_dims(op->beta, "beta", {columns});
+    require(columns <= max_layer_norm_columns, PR_UNSUPPORTED,
+            "layer norm supports at most 2^24 columns (exact FP32 column count)");
+    row_limit(rows, "layer norm");
+    no_alias(op->out, o, op->x, x, "x");
+    no_alias(op->out, o, op->gamma, g, "gamma");
+    no_alias(op->out, o, op->beta, b, "beta");
+    std::vector<Layout> layouts;
+    for (uint32_t i = 0; i < count; ++i) {
+      require(gathered[i], PR_INVALID_ARGUMENT, "Missing gathered tensor");
+      layouts.push_back(operand(gathered[i], "gathered", 2));
+      require(gathered[i]->shape[1] == columns, PR_INVALID_ARGUMENT, "gathered: column count differs from x");
+      require(row_offset <= gathered[i]->shape[0] && rows <= gathered[i]->shape[0] - row_offset,
+              PR_OUT_OF_BOUNDS, "gathered: rows [row_offset, row_offset + rows) exceed the tensor");
+      no_alias(gathered[i], layouts.back(), op->x, x, "x");
+      no_alias(gathered[i], layouts.back(), op->gamma, g, "gamma");
+      no_alias(gathered[i], layouts.back(), op->beta, b, "beta");
+    }
+    same_context(queue, operators,
+                 {{op->x, "x"}, {op->gamma, "gamma"}, {op->beta, "beta"}, {op->out, "out"}});
+    for (uint32_t i = 0; i < count; ++i)
+      same_context(queue, operators, {{gathered[i], "gathered"}});
+    Owned fn;
+    kernel(operators, "paralyn_layer_norm_f32", fn);
+    if (!x.count)
+      return;
+    call(api("layer_norm_gather_f32", [&] {
+      const QueueAccess q = queue_access(queue);
+      std::vector<BoundArg> args;
+      std::vector<std::shared_ptr<Allocation>> retained;
+      auto view = [&](const pr_tensor_desc_v1 *d, const Layout &l) {
+        auto allocation = buffer_allocation(d->buffer, q.context);
+        BoundArg a;
+        a.buffer = true;
+        a.ptr = static_cast<char *>(allocation->ptr) + d->byte_offset;
+        a.bytes = l.bytes;
+        args.push_back(a);
+        retained.push_back(std::move(allocation));
+      };
+      auto scalar = [&](uint32_t bits) {
+        BoundArg a;
+        a.bits = bits;
+        args.push_back(a);
+      };
+      view(op->x, x);
+      view(op->gamma, g);
+      view(op->beta, b);
+      view(op->out, o);
+      uint32_t eps_bits;
+      std::memcpy(&eps_bits, &op->epsilon, 4);
+      scalar(uint32_t(columns));
+      scalar(eps_bits);
+      scalar(uint32_t(rows));
+      scalar(uint32_t(row_offset));
+      scalar(uint32_t(row_offset >> 32));
+      scalar(count);
+      for (uint32_t i = 0; i < count; ++i)
+        view(gathered[i], layouts[i]);
+      *out = submit_command(queue, "b200_layer_norm_gather_f32", launch_layer_norm_gather,
+                            Dim3{uint32_t(rows), 1, 1}, Dim3{256, 1, 1}, std::move(args), std::move(retained));
+    }));
+  });
+}

@@ -93,12 +93,18 @@ class ChainShard:
                 e.wait()
                 e.close()
 
-    def step(self):
-        """Enqueue Z = X W and Y = LayerNorm(Z); returns the two events."""
+    def step(self, gathered=None):
+        """Enqueue Z = X W and Y = LayerNorm(Z); with `gathered` (a GatheredOutput)
+        the LayerNorm also writes its rows into every rank's gathered Y. Returns the
+        two events."""
         mm = matmul_into(self.queue, self.resources.module, self.xd, self.wd, self.zd,
                          m=self.local_rows, n=self.n, k=self.k)
-        ln = layer_norm_into(self.queue, self.resources.module, self.zd, self.gd, self.bd, self.yd,
-                             epsilon=self.epsilon)
+        if gathered is None:
+            ln = layer_norm_into(self.queue, self.resources.module, self.zd, self.gd, self.bd, self.yd,
+                                 epsilon=self.epsilon)
+        else:
+            ln = b200.layer_norm_gather_into(self.queue, self.resources.module, self.zd, self.gd, self.bd,
+                                             self.yd, gathered.targets, row_offset=self.r0, epsilon=self.epsilon)
         return mm, ln
 
     def flops(self):
@@ -107,6 +113,27 @@ class ChainShard:
     def close(self):
         for buf in (self.x, self.w, self.gamma, self.beta, self.z, self.y):
             buf.close()
+
+
+class GatheredOutput:
+    """A [rows, columns] tensor on every rank that all ranks write their rows into.
+
+    Each rank allocates its copy, exports it, and maps every other rank's copy
+    into its own context; `exchange(value)` must return every rank's value in rank
+    order (any host channel: a gloo all_gather_object, a shared dict, ...). The
+    fused LayerNorm writes rows straight into all copies over NVLink.
+    """
+
+    def __init__(self, context, rows, columns, exchange, rank):
+        self.local = context.buffer(4 * rows * columns)
+        handles = exchange(b200.export_buffer(self.local))
+        self.peers = [b200.import_buffer(context, h) for r, h in enumerate(handles) if r != rank]
+        self.targets = [TensorDescriptor(buf, (rows, columns)) for buf in [self.local] + self.peers]
+
+    def close(self):
+        for buf in self.peers:
+            buf.close()
+        self.local.close()
 
 
 def open_rank_context():

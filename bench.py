@@ -301,6 +301,58 @@ class Workload:
                               block=(256, 1, 1))
         return [e], e
 
+    def streamed_step(self, host_in, host_out):
+        """One step with inputs and result in host memory, pipelined over slices:
+        per slice an upload, the step's kernels on that slice and a download, all
+        enqueued at once (stream-ordered copies overlap the other slices' kernels).
+        host_in: addresses matching io_buffers()[0]; host_out: address for the result.
+        Returns the events."""
+        p, b200, D = self.p, self.b200, self.T.TensorDescriptor
+        if self.name == "chain":
+            slices = max(1, min(8, self.chain.local_rows // 1024))
+            return self.chain.step_from_host(host_in[0], host_out, slices=slices, gathered=self.gather)
+        events = []
+
+        def cuts(total, parts, align):
+            return sorted({min(total, -(-total * i // parts) // align * align) for i in range(1, parts)} | {0, total})
+
+        if self.name in ("gemm", "layernorm"):
+            rows, width_in, width_out = ((self.m_local, self.k, self.n) if self.name == "gemm"
+                                         else (self.rows_local, self.cols, self.cols))
+            src, dst = (self.a, self.c) if self.name == "gemm" else (self.x, self.y)
+            c = cuts(rows, 4, 128)
+            for lo, hi in zip(c, c[1:]):
+                n_rows, io, oo = hi - lo, 4 * lo * width_in, 4 * lo * width_out
+                events.append(b200.write_async(self.queue, src, host_in[0] + io, offset=io, nbytes=4 * n_rows * width_in))
+                if self.name == "gemm":
+                    events.append(self.T.matmul_into(self.queue, self.res.module, D(self.a, (n_rows, self.k), io),
+                                                     D(self.b, (self.k, self.n)), D(self.c, (n_rows, self.n), oo),
+                                                     m=n_rows, n=self.n, k=self.k))
+                else:
+                    events.append(self.T.layer_norm_into(self.queue, self.res.module, D(self.x, (n_rows, self.cols), io),
+                                                         D(self.g, (self.cols,)), D(self.bt, (self.cols,)),
+                                                         D(self.y, (n_rows, self.cols), oo), epsilon=1e-5))
+                events.append(b200.read_async(self.queue, dst, host_out + oo, offset=oo, nbytes=4 * n_rows * width_out))
+            return events
+        if self.name == "affine":
+            ins, out = [self.x], self.y
+        else:
+            a, b, c_buf = self.bufs[0][:3]
+            ins, out = [a, b], c_buf
+        c = cuts(self.count, 8 if self.name == "affine" else 1, 1024)  # 12 MiB add: one slice
+        for lo, hi in zip(c, c[1:]):
+            n_el, off = hi - lo, 4 * lo
+            for buf, host in zip(ins, host_in):
+                events.append(b200.write_async(self.queue, buf, host + off, offset=off, nbytes=4 * n_el))
+            views = [buf.view(offset=off, size=4 * n_el, access=p.Access.READ) for buf in ins]
+            views.append(out.view(offset=off, size=4 * n_el, access=p.Access.WRITE))
+            scalars = [p.u32(n_el)] + ([p.f32(1.5), p.f32(-0.25)] if self.name == "affine" else [])
+            events.append(self.queue.launch(self.kernel, views + scalars, grid=((n_el + 255) // 256, 1, 1),
+                                            block=(256, 1, 1)))
+            events.append(b200.read_async(self.queue, out, host_out + off, offset=off, nbytes=4 * n_el))
+            events += views  # closed with the events once the step is done
+        return events
+
     def io_buffers(self):
         """(device buffer written from host, device buffer read back) for the e2e leg."""
         if self.name == "chain":
@@ -355,8 +407,8 @@ def run_ours(args, group):
 
     e2e = None
     if not args.no_e2e:
-        # About 2 GB of host<->device traffic per e2e measurement (PCIe-bound).
-        e2e_steps = max(1, min(steps, int(2e9 // (w.h2d + w.d2h))))
+        # About 8 GB of host<->device traffic per e2e measurement (PCIe-bound).
+        e2e_steps = max(2, min(steps, int(8e9 // (w.h2d + w.d2h))))
         e2e = end_to_end(w, ctx, group, steps=e2e_steps)
 
     dom = sum(durations) / len(durations)
@@ -393,7 +445,13 @@ def last_variant(ctx, workload):
 
 
 def end_to_end(w, ctx, group, steps):
-    """Same steps with host buffers: pinned inputs copied in, result copied out, every step."""
+    """The same steps with host buffers, through the public API: every step copies its
+    inputs in from pinned host memory and its result out to pinned host memory.
+
+    The headline leg pipelines each step over slices with the stream-ordered copies
+    (pr_b200_buffer_write_async / read_async), so PCIe traffic in both directions
+    overlaps the kernels; `blocking` repeats it with the reference's blocking
+    pr_buffer_write / pr_buffer_read around whole-step launches."""
     import torch
     torch.cuda.set_device(group.local_rank)  # pinned host memory comes from this rank's GPU context
     ins, (out_buf, out_bytes) = w.io_buffers()
@@ -401,24 +459,45 @@ def end_to_end(w, ctx, group, steps):
     for buf, host, nbytes in pinned_in:  # the device's current inputs become the host copy
         buf.read_into(host.data_ptr(), nbytes)
     pinned_out = torch.empty(out_bytes, dtype=torch.uint8, pin_memory=True)
+    host_in = [host.data_ptr() for _, host, _ in pinned_in]
+
+    def close(events):
+        for e in events:
+            e.close()
+
+    close(w.streamed_step(host_in, pinned_out.data_ptr()))  # warm-up (first-use costs)
     ctx.synchronize()
     group.barrier()
     t0 = time.perf_counter()
+    pending = []
     for _ in range(steps):
-        for buf, host, nbytes in pinned_in:
-            buf.write_from(host.data_ptr(), nbytes)
-        events, _ = w.step()
-        out_buf.read_into(pinned_out.data_ptr(), out_bytes)
-        for e in events:
-            e.close()
+        pending.append(w.streamed_step(host_in, pinned_out.data_ptr()))
+        if len(pending) > 2:  # keep at most two steps in flight; release older events
+            close(pending.pop(0))
+    for events in pending:
+        close(events)
     ctx.synchronize()
     seconds = time.perf_counter() - t0
     group.barrier()
     worst = group.max(seconds)
+
+    group.barrier()
+    t0 = time.perf_counter()
+    for buf, host, nbytes in pinned_in:
+        buf.write_from(host.data_ptr(), nbytes)
+    events, _ = w.step()
+    out_buf.read_into(pinned_out.data_ptr(), out_bytes)
+    close(events)
+    ctx.synchronize()
+    blocking = group.max(time.perf_counter() - t0)
+    group.barrier()
     return {"value": round(w.units_total * steps / worst * w.scale, 3), "unit": w.unit,
             "h2d_bytes_per_step": sum(n for _, _, n in pinned_in), "d2h_bytes_per_step": out_bytes,
-            "timing": "host wall clock around blocking pr_buffer_write / launches / pr_buffer_read, max over ranks",
-            "steps": steps}
+            "timing": "host wall clock over the steps (inputs uploaded from and results downloaded to pinned host "
+                      "memory every step, pipelined over row/element slices with stream-ordered copies), max over ranks",
+            "steps": steps,
+            "blocking": {"value": round(w.units_total / blocking * w.scale, 3), "unit": w.unit, "steps": 1,
+                         "timing": "one step between blocking pr_buffer_write and pr_buffer_read"}}
 
 
 def measured_peaks():

@@ -65,8 +65,32 @@ pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module operators, con
                                         const pr_tensor_desc_v1 *const *gathered, uint32_t count,
                                         uint64_t row_offset, pr_event *out);
 
+/* ---- Stream-ordered host copies (no counterpart in the reference) ----
+ * pr_buffer_write / pr_buffer_read drain the queue and block, as the reference
+ * specifies. These two enqueue the copy as a command of `queue` and return at
+ * once. A copy starts after every earlier command of the queue that touches the
+ * same bytes of the buffer with at least one of the two writing them, and later
+ * commands that touch those bytes in that way start after it; commands on other
+ * bytes run concurrently with it (copies use the GPU's copy engines, one lane per
+ * direction), so uploading the next slice of an input, computing on the current
+ * one and downloading the previous result overlap. The host memory must stay
+ * valid (and, for a write, unchanged) until the event completes; the copy only
+ * overlaps when the host memory is page-locked (pr_b200_host_register, or memory
+ * from cudaHostAlloc). bytes == 0 gives *event = 0 and enqueues nothing; a range
+ * past the buffer's end is PR_OUT_OF_BOUNDS. */
+pr_status pr_b200_buffer_write_async(pr_queue queue, pr_buffer buffer, uint64_t offset,
+                                     const void *source, uint64_t bytes, pr_event *event);
+pr_status pr_b200_buffer_read_async(pr_queue queue, pr_buffer buffer, uint64_t offset,
+                                    void *destination, uint64_t bytes, pr_event *event);
+/* Page-locks (and unlocks) a caller-owned host range for every device
+ * (cudaHostRegister, portable); registering the same range twice is
+ * PR_INVALID_ARGUMENT. */
+pr_status pr_b200_host_register(void *pointer, uint64_t bytes);
+pr_status pr_b200_host_unregister(void *pointer);
+
 /* Enqueues an empty command whose only effect is a device timestamp on the
- * context queue. pr_b200_event_elapsed returns the device time between the
+ * context queue; it follows every earlier command, copies included.
+ * pr_b200_event_elapsed returns the device time between the
  * completion of `first` and of `second` (markers or any commands of one context),
  * waiting for both. Used to time a region of queued work on the device. */
 pr_status pr_b200_marker(pr_queue queue, pr_event *out);

@@ -57,6 +57,13 @@ def lib():
             "orc_matmul_exact": (None, [_f32p, _f32p, _f64p, _f64p, _size, _size, _size, _c.c_int,
                                         _c.c_int]),
             "orc_bias_activation_f32": (None, [_f32p, _c.c_void_p, _f32p, _size, _size, _c.c_int]),
+            "orc_reduce_rows_f32": (None, [_f32p, _f32p, _size, _size, _c.c_int]),
+            "orc_softmax_bound": (None, [_f32p, _size, _size, _size, _c.c_int, _c.c_float, _f64p, _f64p,
+                                         _c.c_void_p]),
+            "orc_batched_matmul_f32": (None, [_f32p, _View, _f32p, _View, _f32p, _View, _size, _size, _size,
+                                              _size]),
+            "orc_batched_dot_bound": (None, [_f32p, _View, _f32p, _View, _size, _size, _size, _size, _f64p,
+                                             _f64p]),
         }
         for name, (restype, argtypes) in sig.items():
             f = getattr(_lib, name)
@@ -156,6 +163,59 @@ def bias_activation(x, bias, activation):
     return out
 
 
+def reduce_rows(x, op):
+    """Row sums (op 0) or maxima (op 1) of x [rows, columns] in the reference's fixed order."""
+    x = _f32(x)
+    rows, columns = x.shape
+    out = np.empty(rows, np.float32)
+    lib().orc_reduce_rows_f32(x, out, rows, columns, int(op))
+    return out
+
+
+def softmax_bound(x, scale, causal=False):
+    """(value, error) float64 arrays for softmax over the last axis of x [..., rows, columns]
+    (causal: row i of each batch keeps i + columns - rows + 1 leading entries)."""
+    x = _f32(x)
+    rows, columns = x.shape[-2], x.shape[-1]
+    all_rows = int(np.prod(x.shape[:-1]))
+    value = np.empty(x.shape, np.float64)
+    error = np.empty(x.shape, np.float64)
+    scratch = np.empty(4 * columns + 4, np.float64)
+    lib().orc_softmax_bound(x, all_rows, rows, columns, int(bool(causal)), float(scale), value, error,
+                            scratch.ctypes.data)
+    return value, error
+
+
+class _View(_c.Structure):
+    _fields_ = [("offset", _c.c_int64), ("s0", _c.c_int64), ("s1", _c.c_int64), ("s2", _c.c_int64)]
+
+
+def batched_matmul(a, a_view, b, b_view, c, c_view, batch, m, n, k):
+    """Sequential reference-order C[z] = A[z] B[z] over strided views into flat storage;
+    views are (element offset, (stride0, stride1, stride2)); writes only addressed elements of c."""
+    a, b = _f32(a), _f32(b)
+    assert c.dtype == np.float32 and c.flags.c_contiguous
+    views = [_View(off, *strides) for off, strides in (a_view, b_view, c_view)]
+    lib().orc_batched_matmul_f32(a, views[0], b, views[1], c, views[2], batch, m, n, k)
+    return c
+
+
+def batched_dot_bound(a, a_view, b, b_view, batch, m, n, k):
+    """(value, error) float64 [batch, m, n] for the same products."""
+    a, b = _f32(a), _f32(b)
+    value = np.empty((batch, m, n), np.float64)
+    error = np.empty((batch, m, n), np.float64)
+    va, vb = (_View(off, *strides) for off, strides in (a_view, b_view))
+    lib().orc_batched_dot_bound(a, va, b, vb, batch, m, n, k, value, error)
+    return value, error
+
+
+def within(gpu, value, error):
+    """The reference's acceptance rule: |gpu - value| <= error + 2^-45 |value| + 2^-126; NaN fails."""
+    gpu = np.asarray(gpu, np.float64)
+    return np.abs(gpu - value) <= error + 2.0 ** -45 * np.abs(value) + 1.1754943508222875e-38
+
+
 def matmul_tolerance(magnitude, k):
     """Per-element bound of the FP32 GEMM contract: 2 * k * 2^-24 * sum|a||b|."""
     return 2.0 * k * 2.0 ** -24 * magnitude
@@ -176,4 +236,10 @@ def reference():
         _ref.ref_tree_sum_f32.argtypes = [_f32p, _c.c_size_t]
         _ref.ref_layer_norm_row.restype = None
         _ref.ref_layer_norm_row.argtypes = [_f32p, _f32p, _f32p, _c.c_size_t, _c.c_double, _f64p, _f64p]
+        _ref.ref_tree_max_f32.restype = _c.c_float
+        _ref.ref_tree_max_f32.argtypes = [_f32p, _c.c_size_t]
+        _ref.ref_softmax_row.restype = None
+        _ref.ref_softmax_row.argtypes = [_f32p, _c.c_size_t, _c.c_double, _c.c_size_t, _f64p, _f64p]
+        _ref.ref_dot.restype = None
+        _ref.ref_dot.argtypes = [_f32p, _f32p, _c.c_size_t, _c.POINTER(_c.c_double), _c.POINTER(_c.c_double)]
     return _ref

@@ -23,6 +23,19 @@
  *                          sequential checker tests/native/tensor_tests.cpp:62-85
  *   orc_matmul_exact       float64 exact sum and sum|a*b| of the same checker
  *   orc_bias_activation_f32 runtime/tensor.cpp:82-124 (NONE and RELU only)
+ *   orc_reduce_rows_f32    runtime/tensor.cpp:214-246 (lane-sequential sum from
+ *                          +0.0 / max from -inf, then the 256-lane tree; the max
+ *                          rule of :184-191); emulation as in
+ *                          examples/native/transformer_reference.hpp:165-191
+ *   orc_softmax_bound      float64 running bound of softmax_row,
+ *                          examples/native/transformer_reference.hpp:70-73, :122-132
+ *                          (exp budgeted at 4 ulp, division at 2.5 ulp)
+ *   orc_batched_matmul_f32 runtime/tensor.cpp:130-166: per output one accumulator,
+ *                          increasing k, FP32 product then FP32 sum, arbitrary
+ *                          non-negative element strides; checker
+ *                          tests/native/transformer_ops_tests.cpp:129-169
+ *   orc_batched_dot_bound  float64 dot bound of the same checker (gamma_k,
+ *                          examples/native/transformer_reference.hpp:100-111)
  *
  * Threaded (_mt) variants split rows or ranges across OpenMP threads; each
  * output element is still computed in the reference order, so they are
@@ -335,4 +348,117 @@ void orc_set_threads(int n) {
 #else
   (void)n;
 #endif
+}
+
+/* ---- transformer-block row operators ---- */
+
+/* NaN if either is NaN (the first one), +0.0 preferred over -0.0, else the larger. */
+static float max2(float a, float b) {
+  if (isnan(a))
+    return a;
+  if (isnan(b))
+    return b;
+  if (b > a)
+    return b;
+  if (b == a && signbit(a) && !signbit(b))
+    return b;
+  return a;
+}
+
+static float tree_max_f32(const float *x, size_t n) {
+  float p[ORC_LANES];
+  for (unsigned t = 0; t < ORC_LANES; ++t) {
+    float m = -INFINITY;
+    for (size_t j = t; j < n; j += ORC_LANES)
+      m = max2(m, x[j]);
+    p[t] = m;
+  }
+  for (unsigned w = ORC_LANES / 2; w > 0; w >>= 1)
+    for (unsigned t = 0; t < w; ++t)
+      p[t] = max2(p[t], p[t + w]);
+  return p[0];
+}
+
+/* op 0 = sum, 1 = max; empty rows give +0.0 / -inf. */
+void orc_reduce_rows_f32(const float *x, float *out, size_t rows, size_t columns, int op) {
+  for (size_t r = 0; r < rows; ++r)
+    out[r] = op == 1 ? tree_max_f32(x + r * columns, columns) : orc_tree_sum_f32(x + r * columns, columns);
+}
+
+static orc_b b_exp(orc_b a) {
+  orc_b r;
+  r.v = exp(a.v);
+  const double e0 = r.v * expm1(a.e);
+  r.e = e0 + rounded(r.v + e0, 4.0 * 2.0 * ORC_U);
+  return r;
+}
+
+/* Rows of `columns` entries, `all_rows` of them; row i of a batch of `rows` rows has
+ * visible = causal ? i + (columns - rows) + 1 : columns leading entries; the rest are
+ * exact zeros (value 0, error 0). scratch needs 2*columns orc_b. */
+void orc_softmax_bound(const float *x, size_t all_rows, size_t rows, size_t columns, int causal,
+                       float scale, double *value, double *error, void *scratch) {
+  orc_b *v = (orc_b *)scratch, *e = v + columns;
+  const orc_b s_scale = {(double)scale, 0.0};
+  for (size_t r = 0; r < all_rows; ++r) {
+    const float *xr = x + r * columns;
+    const size_t visible = causal ? (r % rows) + (columns - rows) + 1 : columns;
+    orc_b m = {-INFINITY, 0.0};
+    for (size_t j = 0; j < visible; ++j) {
+      const orc_b xj = {(double)xr[j], 0.0};
+      v[j] = b_mul(s_scale, xj);
+      m.v = v[j].v > m.v ? v[j].v : m.v;
+      m.e = v[j].e > m.e ? v[j].e : m.e;
+    }
+    for (size_t j = 0; j < visible; ++j)
+      e[j] = b_exp(b_sub(v[j], m));
+    const orc_b sum = b_tree_sum(e, visible);
+    for (size_t j = 0; j < columns; ++j) {
+      orc_b y = {0.0, 0.0};
+      if (j < visible)
+        y = b_div(e[j], sum);
+      value[r * columns + j] = y.v;
+      error[r * columns + j] = y.e;
+    }
+  }
+}
+
+/* Element (z, i, j) of a strided 3-D operand: base[off + z*s0 + i*s1 + j*s2]. */
+typedef struct {
+  int64_t offset, s0, s1, s2;
+} orc_view;
+
+void orc_batched_matmul_f32(const float *a, orc_view av, const float *b, orc_view bv, float *c,
+                            orc_view cv, size_t batch, size_t m, size_t n, size_t k) {
+  for (size_t z = 0; z < batch; ++z)
+    for (size_t i = 0; i < m; ++i)
+      for (size_t j = 0; j < n; ++j) {
+        float sum = 0.0f;
+        for (size_t p = 0; p < k; ++p) {
+          const float x = a[av.offset + z * av.s0 + i * av.s1 + p * av.s2];
+          const float y = b[bv.offset + z * bv.s0 + p * bv.s1 + j * bv.s2];
+          const float product = x * y;
+          sum = sum + product;
+        }
+        c[cv.offset + z * cv.s0 + i * cv.s1 + j * cv.s2] = sum;
+      }
+}
+
+/* value/error per output, in [batch][m][n] order. */
+void orc_batched_dot_bound(const float *a, orc_view av, const float *b, orc_view bv, size_t batch,
+                           size_t m, size_t n, size_t k, double *value, double *error) {
+  for (size_t z = 0; z < batch; ++z)
+    for (size_t i = 0; i < m; ++i)
+      for (size_t j = 0; j < n; ++j) {
+        double v = 0, magnitude = 0;
+        for (size_t p = 0; p < k; ++p) {
+          const double x = a[av.offset + z * av.s0 + i * av.s1 + p * av.s2];
+          const double y = b[bv.offset + z * bv.s0 + p * bv.s1 + j * bv.s2];
+          v += x * y;
+          magnitude += fabs(x * y);
+        }
+        const size_t o = (z * m + i) * n + j;
+        value[o] = v;
+        error[o] = gamma_n((double)k) * magnitude + (double)k * ORC_TINY;
+      }
 }

@@ -8,6 +8,9 @@
 //                       kernel of a .prk; returns the generated CUDA text
 //   ref_tree_sum_f32    tree_sum_f32 (examples/native/transformer_reference.hpp:172-181)
 //   ref_layer_norm_row  layer_norm_row float64 bound (same header :133-147)
+//   ref_tree_max_f32    tree_max_f32 (same header :182-191)
+//   ref_softmax_row     softmax_row float64 bound (same header :122-132)
+//   ref_dot             dot float64 bound (same header :101-111)
 #include "paralyn/artifact.hpp"
 #include "paralyn/cuda_codegen.hpp"
 #include "transformer_reference.hpp"
@@ -46,5 +49,21 @@ void ref_layer_norm_row(const float *x, const float *gamma, const float *beta, s
     value[j] = y[j].v;
     error[j] = y[j].e;
   }
+}
+float ref_tree_max_f32(const float *x, size_t n) { return paralyn_reference::tree_max_f32(x, n); }
+void ref_softmax_row(const float *x, size_t columns, double scale, size_t visible, double *value,
+                     double *error) {
+  namespace r = paralyn_reference;
+  const auto y = r::softmax_row(r::exact_values(std::vector<float>(x, x + columns)), scale, visible);
+  for (size_t j = 0; j < columns; ++j) {
+    value[j] = y[j].v;
+    error[j] = y[j].e;
+  }
+}
+void ref_dot(const float *a, const float *b, size_t k, double *value, double *error) {
+  namespace r = paralyn_reference;
+  const auto d = r::dot(r::exact_values(std::vector<float>(a, a + k)), r::exact_values(std::vector<float>(b, b + k)));
+  *value = d.v;
+  *error = d.e;
 }
 }

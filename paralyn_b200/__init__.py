@@ -16,9 +16,10 @@ from .native import (ABI_VERSION, ARTIFACT_MSL_SOURCE, ARTIFACT_SPIRV_MSL, ARTIF
                      device_capabilities, devices, f32, i32, library, u32)
 from .array import Array, add, affine, affine_scalar, asarray, float32
 from .tensor import (Activation, Reduce, Tensor, TensorDescriptor, TensorOperatorCapabilities,
-                     add_into, bias_activation_into, bias_add, bias_gelu, gelu, layer_norm,
-                     layer_norm_into, load_tensor_operators, matmul, matmul_into, relu,
-                     residual_add, tensor, tensor_operators_artifact,
+                     add_into, batched_matmul, batched_matmul_into, bias_activation_into, bias_add,
+                     bias_gelu, gelu, layer_norm, layer_norm_into, load_tensor_operators, matmul,
+                     matmul_into, reduce_rows_into, relu, residual_add, row_max, row_sum, softmax,
+                     softmax_rows_into, tensor, tensor_operators_artifact,
                      tensor_operators_capabilities)
 from .b200 import (MatmulMode, device_kernel_count, fill_synthetic_into, inspect_module, matmul_mode,
                    set_matmul_mode)

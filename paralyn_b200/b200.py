@@ -27,6 +27,10 @@ def _b200(lib):
             "pr_b200_buffer_export": (_c.c_int, [h, _c.c_void_p]),
             "pr_b200_buffer_import": (_c.c_int, [h, _c.c_void_p, ptr(h)]),
             "pr_b200_layer_norm_gather_f32": (_c.c_int, [h, h, _c.c_void_p, _c.c_void_p, u32, u64, ptr(h)]),
+            "pr_b200_buffer_write_async": (_c.c_int, [h, h, u64, _c.c_void_p, u64, ptr(h)]),
+            "pr_b200_buffer_read_async": (_c.c_int, [h, h, u64, _c.c_void_p, u64, ptr(h)]),
+            "pr_b200_host_register": (_c.c_int, [_c.c_void_p, u64]),
+            "pr_b200_host_unregister": (_c.c_int, [_c.c_void_p]),
             "pr_b200_marker": (_c.c_int, [h, ptr(h)]),
             "pr_b200_event_elapsed": (_c.c_int, [h, h, ptr(_c.c_double)]),
             "pr_b200_fill_synthetic_f32": (_c.c_int, [h, ptr(TensorDescRecord), u64, u64, u32,
@@ -106,6 +110,65 @@ def layer_norm_gather_into(queue, operators, x, gamma, beta, out, gathered, *, r
     lib.check(lib.api.pr_b200_layer_norm_gather_f32(queue.handle, operators.handle, _c.byref(record), array,
                                                     len(natives), row_offset, _c.byref(handle)))
     return Event._adopt(lib, handle.value) if handle.value else None
+
+
+def _host_range(host, nbytes):
+    """(address, bytes) of a numpy array, a ctypes object or a raw address + size."""
+    if isinstance(host, int):
+        if nbytes is None:
+            raise ValueError("a raw host address needs nbytes")
+        return host, int(nbytes)
+    if hasattr(host, "__array_interface__"):
+        import numpy as np
+        array = np.asarray(host)
+        if not array.flags.c_contiguous:
+            raise ValueError("host array must be C-contiguous")
+        return array.__array_interface__["data"][0], array.nbytes if nbytes is None else int(nbytes)
+    return _c.addressof(host), _c.sizeof(host) if nbytes is None else int(nbytes)
+
+
+def write_async(queue, buffer, source, *, offset=0, nbytes=None):
+    """Stream-ordered copy of host memory into buffer[offset:offset+nbytes]; returns
+    its Event (None for zero bytes). `source` must stay valid until the event completes."""
+    lib = _b200(queue._lib)
+    address, size = _host_range(source, nbytes)
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_buffer_write_async(queue.handle, buffer.handle, offset, address, size,
+                                                 _c.byref(handle)))
+    if not handle.value:
+        return None
+    event = Event._adopt(lib, handle.value)
+    event.host = source  # kept alive with the event
+    return event
+
+
+def read_async(queue, buffer, destination, *, offset=0, nbytes=None):
+    """Stream-ordered copy of buffer[offset:offset+nbytes] into host memory."""
+    lib = _b200(queue._lib)
+    address, size = _host_range(destination, nbytes)
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_buffer_read_async(queue.handle, buffer.handle, offset, address, size,
+                                                _c.byref(handle)))
+    if not handle.value:
+        return None
+    event = Event._adopt(lib, handle.value)
+    event.host = destination
+    return event
+
+
+def host_register(host, nbytes=None, library_path=None):
+    """Page-lock a host range (numpy array or address + nbytes) so copies overlap."""
+    from .native import library
+    lib = _b200(library(library_path))
+    address, size = _host_range(host, nbytes)
+    lib.check(lib.api.pr_b200_host_register(address, size))
+
+
+def host_unregister(host, library_path=None):
+    from .native import library
+    lib = _b200(library(library_path))
+    address, _ = _host_range(host, 0 if isinstance(host, int) else None)
+    lib.check(lib.api.pr_b200_host_unregister(address))
 
 
 def marker(queue):

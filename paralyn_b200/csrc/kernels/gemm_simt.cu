@@ -26,6 +26,9 @@ struct GemmArgs {
   int64_t m, n, k;       // m, n: extent computed; k: full depth
   int64_t lda, ldb, ldc; // row strides of the stored matrices
   bool vec_a, vec_b, vec_c;
+  // Batched launches (grid.z = batch): matrix z starts sa / sb / sc elements after
+  // matrix z-1; C's column stride may differ from 1.
+  int64_t sa = 0, sb = 0, sc = 0, c_col = 1;
 };
 
 template <int MODE> __device__ __forceinline__ float mac(float acc, float a, float b) {
@@ -121,7 +124,11 @@ template <bool TB> __device__ __forceinline__ void store_b(float (*sb)[BN], cons
 }
 
 template <int MODE, bool TA, bool TB>
-__global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs g) {
+__global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs batch) {
+  GemmArgs g = batch;
+  g.a += int64_t(blockIdx.z) * batch.sa;
+  g.b += int64_t(blockIdx.z) * batch.sb;
+  g.c += int64_t(blockIdx.z) * batch.sc;
   __shared__ __align__(16) float sa[2][BK][BM];
   __shared__ __align__(16) float sb[2][BK][BN];
   // Grouped raster: 8 tile-rows at a time, columns fastest within the group.
@@ -191,7 +198,12 @@ __global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs g) {
     for (int h = 0; h < 2; ++h) {
       const int64_t n = n0 + h * 64 + tx * 4;
       const float *v = &acc[i][4 * h];
-      if (g.vec_c && n + 3 < g.n) {
+      if (g.c_col != 1) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < g.n)
+            row[(n + j) * g.c_col] = v[j];
+      } else if (g.vec_c && n + 3 < g.n) {
         *reinterpret_cast<float4 *>(row + n) = make_float4(v[0], v[1], v[2], v[3]);
       } else {
 #pragma unroll
@@ -203,20 +215,44 @@ __global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs g) {
   }
 }
 
-template <int MODE, bool TA, bool TB> void run(const GemmArgs &g, cudaStream_t stream) {
+template <int MODE, bool TA, bool TB> void run(const GemmArgs &g, cudaStream_t stream, uint32_t batch) {
   const int64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + BN - 1) / BN);
-  gemm_simt<MODE, TA, TB><<<uint32_t(tiles), THREADS, 0, stream>>>(g);
+  gemm_simt<MODE, TA, TB><<<dim3(uint32_t(tiles), 1, batch), THREADS, 0, stream>>>(g);
 }
 
-template <int MODE> void dispatch(const GemmArgs &g, bool ta, bool tb, cudaStream_t stream) {
+template <int MODE> void dispatch(const GemmArgs &g, bool ta, bool tb, cudaStream_t stream, uint32_t batch = 1) {
   if (!ta && !tb)
-    run<MODE, false, false>(g, stream);
+    run<MODE, false, false>(g, stream, batch);
   else if (!ta && tb)
-    run<MODE, false, true>(g, stream);
+    run<MODE, false, true>(g, stream, batch);
   else if (ta && !tb)
-    run<MODE, true, false>(g, stream);
+    run<MODE, true, false>(g, stream, batch);
   else
-    run<MODE, true, true>(g, stream);
+    run<MODE, true, true>(g, stream, batch);
+}
+
+// Any strides: one output per thread, 16x16 threads per block, k in increasing order.
+template <int MODE>
+__global__ void __launch_bounds__(256) batched_generic(const float *a, const float *b, float *c, int64_t m,
+                                                       int64_t n, int64_t k, int64_t a0, int64_t a1, int64_t a2,
+                                                       int64_t b0, int64_t b1, int64_t b2, int64_t c0, int64_t c1,
+                                                       int64_t c2) {
+  const int64_t i = int64_t(blockIdx.y) * 16 + threadIdx.y, j = int64_t(blockIdx.x) * 16 + threadIdx.x;
+  if (i >= m || j >= n)
+    return;
+  const int64_t z = blockIdx.z;
+  const float *ar = a + z * a0 + i * a1, *bc = b + z * b0 + j * b2;
+  float sum = 0.0f;
+  for (int64_t p = 0; p < k; ++p)
+    sum = mac<MODE>(sum, ar[p * a2], bc[p * b1]);
+  c[z * c0 + i * c1 + j * c2] = sum;
+}
+
+__global__ void __launch_bounds__(256) batched_fill(float *c, int64_t m, int64_t n, int64_t c0, int64_t c1,
+                                                    int64_t c2, float value) {
+  const int64_t i = int64_t(blockIdx.y) * 16 + threadIdx.y, j = int64_t(blockIdx.x) * 16 + threadIdx.x;
+  if (i < m && j < n)
+    c[int64_t(blockIdx.z) * c0 + i * c1 + j * c2] = value;
 }
 
 bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
@@ -276,6 +312,122 @@ void launch_provider_matmul(Launch &L) {
     L.variant = "simt_ffma";
   }
   L.kernels = 1;
+}
+
+namespace {
+// Highest element index + 1 of a strided [d0, d1, d2] operand (all extents > 0).
+uint64_t extent(uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s0, uint64_t s1, uint64_t s2) {
+  return (d0 - 1) * s0 + (d1 - 1) * s1 + (d2 - 1) * s2 + 1;
+}
+// A strided [rows, cols] operand as a (leading dimension, transposed) pair, when one
+// of its two strides is 1 (or that dimension has extent 1, so its stride is never
+// used): element (r, c) at r*ld + c, or at c*ld + r when transposed.
+bool as_matrix(int64_t rows, int64_t cols, int64_t row_stride, int64_t col_stride, int64_t &ld, bool &transposed) {
+  if (col_stride == 1 || cols == 1) {
+    ld = row_stride;
+    transposed = false;
+    return true;
+  }
+  if (row_stride == 1 || rows == 1) {
+    ld = col_stride;
+    transposed = true;
+    return true;
+  }
+  return false;
+}
+} // namespace
+
+// (a, b, c, m, n, k, a_batch, a_row, a_col, b_batch, b_row, b_col, c_batch, c_row,
+//  c_col), grid (ceil(n/16), ceil(m/16), batch): C[z] = A[z] B[z] over element-strided
+// views, each output one accumulator over increasing k (reference
+// runtime/tensor.cpp:130-166). Operands whose strides make them row-major or
+// transposed matrices run on the tiled SIMT kernel with a batch grid dimension;
+// other layouts on a one-output-per-thread kernel.
+void launch_provider_batched_matmul(Launch &L) {
+  const auto &A = L.args;
+  const int64_t m = std::min<int64_t>(A[3].u32(), int64_t(L.grid.y) * 16);
+  const int64_t n = std::min<int64_t>(A[4].u32(), int64_t(L.grid.x) * 16);
+  const int64_t k = A[5].u32();
+  const uint64_t batch = L.grid.z;
+  const int64_t s[9] = {A[6].u32(), A[7].u32(), A[8].u32(), A[9].u32(), A[10].u32(),
+                        A[11].u32(), A[12].u32(), A[13].u32(), A[14].u32()};
+  if (!m || !n || !batch) {
+    L.variant = "empty";
+    return;
+  }
+  if (k) {
+    need_elements(A[0], extent(batch, m, k, s[0], s[1], s[2]), "a");
+    need_elements(A[1], extent(batch, k, n, s[3], s[4], s[5]), "b");
+  }
+  need_elements(A[2], extent(batch, m, n, s[6], s[7], s[8]), "c");
+  if (L.dry_run)
+    return;
+  const auto *a = static_cast<const float *>(A[0].ptr);
+  const auto *b = static_cast<const float *>(A[1].ptr);
+  auto *c = static_cast<float *>(A[2].ptr);
+  const bool reference = L.matmul_mode == matmul_reference;
+  L.kernels = 1;
+  if (!k) {
+    batched_fill<<<dim3(L.grid.x, L.grid.y, uint32_t(batch)), dim3(16, 16), 0, L.stream>>>(c, m, n, s[6], s[7], s[8],
+                                                                                           0.0f);
+    L.variant = "batched_fill";
+    return;
+  }
+  if (batch > 65535)
+    throw Failure(PR_UNSUPPORTED, "Batched matmul supports at most 65535 matrices per launch");
+  GemmArgs g;
+  bool ta = false, tb = false; // B's matrix form is [k, n]; transposed = stored [n, k]
+  if (as_matrix(m, k, s[1], s[2], g.lda, ta) && as_matrix(k, n, s[4], s[5], g.ldb, tb)) {
+    g.a = a;
+    g.b = b;
+    g.c = c;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    g.sa = s[0];
+    g.sb = s[3];
+    g.sc = s[6];
+    g.ldc = s[7]; // element (i, j) of C[z] at i*ldc + j*c_col
+    g.c_col = n == 1 ? 1 : s[8];
+    g.vec_a = aligned16(a) && g.lda % 4 == 0 && g.sa % 4 == 0;
+    g.vec_b = aligned16(b) && g.ldb % 4 == 0 && g.sb % 4 == 0;
+    g.vec_c = aligned16(c) && g.ldc % 4 == 0 && g.sc % 4 == 0 && g.c_col == 1;
+    if (reference)
+      dispatch<matmul_reference>(g, ta, tb, L.stream, uint32_t(batch));
+    else
+      dispatch<matmul_ffma>(g, ta, tb, L.stream, uint32_t(batch));
+    L.variant = reference ? "batched_simt_reference_order" : "batched_simt_ffma";
+    return;
+  }
+  const dim3 grid(L.grid.x, L.grid.y, uint32_t(batch)), block(16, 16);
+  if (reference)
+    batched_generic<matmul_reference><<<grid, block, 0, L.stream>>>(a, b, c, m, n, k, s[0], s[1], s[2], s[3], s[4],
+                                                                    s[5], s[6], s[7], s[8]);
+  else
+    batched_generic<matmul_ffma><<<grid, block, 0, L.stream>>>(a, b, c, m, n, k, s[0], s[1], s[2], s[3], s[4], s[5],
+                                                               s[6], s[7], s[8]);
+  L.variant = reference ? "batched_generic_reference_order" : "batched_generic_ffma";
+}
+
+// (c, m, n, c_batch, c_row, c_col, value), grid (ceil(n/16), ceil(m/16), batch).
+void launch_provider_batched_fill(Launch &L) {
+  const auto &A = L.args;
+  const int64_t m = std::min<int64_t>(A[1].u32(), int64_t(L.grid.y) * 16);
+  const int64_t n = std::min<int64_t>(A[2].u32(), int64_t(L.grid.x) * 16);
+  const uint64_t batch = L.grid.z;
+  if (!m || !n || !batch) {
+    L.variant = "empty";
+    return;
+  }
+  need_elements(A[0], extent(batch, m, n, A[3].u32(), A[4].u32(), A[5].u32()), "c");
+  if (batch > 65535)
+    throw Failure(PR_UNSUPPORTED, "Batched fill supports at most 65535 matrices per launch");
+  if (L.dry_run)
+    return;
+  batched_fill<<<dim3(L.grid.x, L.grid.y, uint32_t(batch)), dim3(16, 16), 0, L.stream>>>(
+      static_cast<float *>(A[0].ptr), m, n, A[3].u32(), A[4].u32(), A[5].u32(), A[6].f32());
+  L.kernels = 1;
+  L.variant = "batched_fill";
 }
 
 } // namespace pb

@@ -426,6 +426,28 @@ pr_event submit_command(pr_queue queue, const std::string &name, Launcher launch
                        std::move(args), std::move(retained));
 }
 
+pr_event submit_transfer(pr_queue queue, pr_buffer buffer, uint64_t offset, void *host,
+                         uint64_t bytes, bool to_device) {
+  auto q = get<QueueObj>(queue, HandleKind::queue);
+  auto b = get<BufferObj>(buffer, HandleKind::buffer);
+  require(b->owner == q->owner, PR_CONTEXT_MISMATCH, "Buffer and queue belong to different contexts");
+  require(host || !bytes, PR_INVALID_ARGUMENT,
+          to_device ? "Nonempty write requires a host pointer" : "Nonempty read requires a host pointer");
+  require(offset <= b->allocation->bytes && bytes <= b->allocation->bytes - offset, PR_OUT_OF_BOUNDS,
+          "Copy range exceeds buffer");
+  if (!bytes)
+    return 0;
+  auto event = std::make_shared<EventObj>(q->owner, nullptr);
+  const pr_handle handle = add(event);
+  try {
+    event->work = q->owner->engine->transfer(to_device, b->allocation, offset, host, bytes);
+  } catch (...) {
+    objects.erase(handle);
+    throw;
+  }
+  return handle;
+}
+
 pr_event submit_marker(pr_queue queue) {
   auto q = get<QueueObj>(queue, HandleKind::queue);
   auto event = std::make_shared<EventObj>(q->owner, nullptr);
@@ -745,6 +767,7 @@ PB_EXPORT pr_status pr_launch(pr_queue q, pr_kernel h, pr_dim3 grid, pr_dim3 blo
         require((view->access & p.access) == p.access, PR_INVALID_ARGUMENT,
                 "View access does not allow the kernel's reads/writes");
         bound[i].buffer = true;
+        bound[i].writes = (p.access & PR_WRITE) != 0;
         bound[i].ptr = static_cast<char *>(view->buffer->allocation->ptr) + view->offset;
         bound[i].bytes = view->size;
         retained.push_back(view->buffer->allocation);

@@ -41,6 +41,9 @@ pr_event submit_command(pr_queue queue, const std::string &name, Launcher launch
                         Dim3 block, std::vector<BoundArg> args,
                         std::vector<std::shared_ptr<Allocation>> retained);
 pr_event submit_marker(pr_queue queue);
+// A stream-ordered host copy of `queue` (0 and nothing enqueued when bytes == 0).
+pr_event submit_transfer(pr_queue queue, pr_buffer buffer, uint64_t offset, void *host,
+                         uint64_t bytes, bool to_device);
 double event_elapsed(pr_event first, pr_event second);
 pr_handle add_object(std::shared_ptr<void> object, HandleKind kind, const void *context);
 std::shared_ptr<void> get_object(pr_handle handle, HandleKind kind, const void **context);

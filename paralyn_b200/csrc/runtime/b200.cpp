@@ -87,6 +87,47 @@ PB_EXPORT pr_status pr_b200_buffer_import(pr_context context, const void *handle
   });
 }
 
+PB_EXPORT pr_status pr_b200_buffer_write_async(pr_queue queue, pr_buffer buffer, uint64_t offset,
+                                               const void *source, uint64_t bytes, pr_event *out) {
+  return api("b200_buffer_write_async", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    *out = submit_transfer(queue, buffer, offset, const_cast<void *>(source), bytes, true);
+  });
+}
+
+PB_EXPORT pr_status pr_b200_buffer_read_async(pr_queue queue, pr_buffer buffer, uint64_t offset,
+                                              void *destination, uint64_t bytes, pr_event *out) {
+  return api("b200_buffer_read_async", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    *out = submit_transfer(queue, buffer, offset, destination, bytes, false);
+  });
+}
+
+PB_EXPORT pr_status pr_b200_host_register(void *pointer, uint64_t bytes) {
+  return api("b200_host_register", [&] {
+    require(pointer && bytes, PR_INVALID_ARGUMENT, "Registering host memory needs a pointer and a size");
+    const cudaError_t e = cudaHostRegister(pointer, bytes, cudaHostRegisterPortable);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw Failure(e == cudaErrorHostMemoryAlreadyRegistered ? PR_INVALID_ARGUMENT : PR_DEVICE_UNAVAILABLE,
+                    std::string("cudaHostRegister failed: ") + cudaGetErrorString(e));
+    }
+  });
+}
+
+PB_EXPORT pr_status pr_b200_host_unregister(void *pointer) {
+  return api("b200_host_unregister", [&] {
+    require(pointer, PR_INVALID_ARGUMENT, "Missing host pointer");
+    const cudaError_t e = cudaHostUnregister(pointer);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw Failure(PR_INVALID_ARGUMENT, std::string("cudaHostUnregister failed: ") + cudaGetErrorString(e));
+    }
+  });
+}
+
 PB_EXPORT pr_status pr_b200_marker(pr_queue queue, pr_event *out) {
   return api("b200_marker", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");

@@ -15,6 +15,7 @@ namespace pb {
 
 struct BoundArg {
   bool buffer = false;
+  bool writes = true;     // the kernel may write the view (false: read-only parameter)
   void *ptr = nullptr;    // device address of the view's first byte
   uint64_t bytes = 0;     // view size
   uint32_t bits = 0;      // scalar payload
@@ -87,7 +88,10 @@ void launch_provider_layer_norm(Launch &);
 void launch_provider_matmul(Launch &);
 void launch_provider_bias_activation(Launch &);
 void launch_provider_activation(Launch &);
-void launch_unsupported(Launch &);
+void launch_provider_batched_matmul(Launch &);
+void launch_provider_batched_fill(Launch &);
+void launch_provider_reduce_rows(Launch &);
+void launch_provider_softmax_rows(Launch &);
 
 // Synthetic input streams (paralyn/b200.h pr_b200_fill_synthetic_f32).
 void launch_synthetic(cudaStream_t stream, float *out, uint64_t count, uint64_t seed,

@@ -1,8 +1,7 @@
 // Built-in kernel table. The provider entries keep the reference provider's
 // entry names, parameter names, types, buffer flags, access and required block
 // (runtime/tensor.cpp:322-371), because clients check that schema before use
-// (runtime/tensor.cpp:595-614). Entries without an sm_100a implementation in this
-// build keep their schema and fail with PR_UNSUPPORTED when launched.
+// (runtime/tensor.cpp:595-614).
 #include "builtin.hpp"
 
 namespace pb {
@@ -14,10 +13,6 @@ Param u32(const char *name) { return Param{name, Scalar::U32, false, PR_READ}; }
 Param f32(const char *name) { return Param{name, Scalar::F32, false, PR_READ}; }
 constexpr pr_access RW = PR_READ_WRITE;
 } // namespace
-
-void launch_unsupported(Launch &) {
-  throw Failure(PR_UNSUPPORTED, "This operator has no sm_100a implementation in this build");
-}
 
 const std::vector<Builtin> &provider_builtins() {
   static const std::vector<Builtin> table = {
@@ -36,16 +31,16 @@ const std::vector<Builtin> &provider_builtins() {
        {buf("a"), buf("b"), buf("c", RW), u32("m"), u32("n"), u32("k"), u32("a_batch"),
         u32("a_row"), u32("a_col"), u32("b_batch"), u32("b_row"), u32("b_col"), u32("c_batch"),
         u32("c_row"), u32("c_col")},
-       launch_unsupported},
+       launch_provider_batched_matmul},
       {"paralyn_batched_fill_f32", {16, 16, 1},
        {buf("c", RW), u32("m"), u32("n"), u32("c_batch"), u32("c_row"), u32("c_col"),
         f32("value")},
-       launch_unsupported},
+       launch_provider_batched_fill},
       {"paralyn_reduce_rows_f32", {256, 1, 1},
-       {buf("x"), buf("out", RW), u32("columns"), u32("op")}, launch_unsupported},
+       {buf("x"), buf("out", RW), u32("columns"), u32("op")}, launch_provider_reduce_rows},
       {"paralyn_softmax_rows_f32", {256, 1, 1},
        {buf("x"), buf("out", RW), u32("columns"), u32("rows"), u32("causal"), f32("scale")},
-       launch_unsupported},
+       launch_provider_softmax_rows},
       {"paralyn_layer_norm_f32", {256, 1, 1},
        {buf("x"), buf("gamma"), buf("beta"), buf("out", RW), u32("columns"), f32("epsilon")},
        launch_provider_layer_norm},

@@ -263,6 +263,8 @@ Engine::Engine(const DeviceRecord &device)
   std::memset(status_host_, 0, 64);
   cuda_check(cudaStreamCreateWithFlags(&side_stream_, cudaStreamNonBlocking),
              "cudaStreamCreate(side)");
+  for (auto &copy : copy_streams_)
+    cuda_check(cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking), "cudaStreamCreate(copy)");
   for (auto &event : side_events_)
     cuda_check(cudaEventCreateWithFlags(&event, cudaEventDisableTiming), "cudaEventCreate(side)");
   cuda_check(cudaHostGetDevicePointer(reinterpret_cast<void **>(&status_device_), status_host_, 0),
@@ -292,6 +294,9 @@ Engine::~Engine() {
       cudaStreamDestroy(stream_);
     if (side_stream_)
       cudaStreamDestroy(side_stream_);
+    for (auto copy : copy_streams_)
+      if (copy)
+        cudaStreamDestroy(copy);
     for (auto event : side_events_)
       if (event)
         cudaEventDestroy(event);
@@ -470,7 +475,8 @@ void Engine::recycle(Work &work) {
 
 std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher, Dim3 grid,
                                      Dim3 block, std::vector<BoundArg> args,
-                                     std::vector<std::shared_ptr<Allocation>> retained) {
+                                     std::vector<std::shared_ptr<Allocation>> retained,
+                                     bool barrier) {
   std::lock_guard<std::mutex> lock(mutex_);
   healthy();
   DeviceScope scope(device_.ordinal);
@@ -502,6 +508,12 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
   work->start = take_event();
   work->end = take_event();
   runtime_event("submission", "prepared", name, trace_id_, work->operation_id);
+  try {
+    order_after(0, launch.args, barrier);
+  } catch (...) {
+    recycle(*work);
+    throw;
+  }
   cudaError_t e = cudaEventRecord(work->start, stream_);
   if (e != cudaSuccess) {
     recycle(*work);
@@ -534,7 +546,128 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
     work->failure = text;
     throw Error(code_of(e), text);
   }
+  remember(0, launch.args, work);
   progress("Kernel: " + name + " (" + launch.variant + ")\n");
+  return work;
+}
+
+static bool overlaps(uintptr_t b0, uintptr_t e0, uintptr_t b1, uintptr_t e1) {
+  return b0 < e1 && b1 < e0;
+}
+
+void Engine::order_after(int lane, const std::vector<BoundArg> &accesses, bool barrier) {
+  const cudaStream_t stream = lane_stream(lane);
+  for (int other = 0; other < lanes; ++other) {
+    if (other == lane)
+      continue;
+    const auto &list = records_[other];
+    // Newest first; a finished command means every older one of its lane finished
+    // too (commands finish in submission order, and a lane runs in that order).
+    for (auto it = list.rbegin(); it != list.rend() && !it->work->recorded; ++it) {
+      bool conflict = barrier;
+      for (size_t i = 0; i < accesses.size() && !conflict; ++i) {
+        const auto &a = accesses[i];
+        if (!a.buffer || !a.bytes)
+          continue;
+        const auto begin = reinterpret_cast<uintptr_t>(a.ptr);
+        conflict = (a.writes || it->write) && overlaps(begin, begin + a.bytes, it->begin, it->end);
+      }
+      if (conflict) {
+        const cudaError_t e = cudaStreamWaitEvent(stream, it->work->end, 0);
+        if (e != cudaSuccess)
+          cuda_failure(e, "cudaStreamWaitEvent");
+        break;
+      }
+    }
+  }
+}
+
+void Engine::remember(int lane, const std::vector<BoundArg> &accesses,
+                      const std::shared_ptr<Work> &work) {
+  auto &list = records_[lane];
+  for (const auto &a : accesses)
+    if (a.buffer && a.bytes) {
+      const auto begin = reinterpret_cast<uintptr_t>(a.ptr);
+      list.push_back({begin, begin + a.bytes, a.writes, work});
+    }
+  if (list.size() > 256)
+    prune(lane);
+}
+
+// Drops the records of commands that the device has finished: the lane is in
+// order, so a binary search finds the newest finished one.
+void Engine::prune(int lane) {
+  auto &list = records_[lane];
+  auto finished = [](const Record &r) {
+    if (r.work->recorded)
+      return true;
+    const cudaError_t e = cudaEventQuery(r.work->end);
+    if (e == cudaErrorNotReady && cudaPeekAtLastError() == cudaErrorNotReady)
+      cudaGetLastError(); // not-ready is a state, not a failure for the next launch check
+    return e == cudaSuccess;
+  };
+  size_t lo = 0, hi = list.size(); // records [0, lo) finished; [hi, size) not
+  while (lo < hi) {
+    const size_t mid = lo + (hi - lo) / 2;
+    if (finished(list[mid]))
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  list.erase(list.begin(), list.begin() + lo);
+}
+
+std::shared_ptr<Work> Engine::transfer(bool to_device, const std::shared_ptr<Allocation> &allocation,
+                                       size_t offset, void *host, size_t bytes) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  healthy();
+  check_owner(*allocation);
+  copy_range(*allocation, offset, bytes);
+  if (!host || !bytes)
+    throw Error(Code::invalid_value, "An asynchronous copy needs a host pointer and a nonzero size");
+  DeviceScope scope(device_.ordinal);
+  const int lane = to_device ? 1 : 2;
+  const cudaStream_t stream = lane_stream(lane);
+  auto work = std::make_shared<Work>();
+  work->kernel = to_device ? "b200_buffer_write_async" : "b200_buffer_read_async";
+  work->variant = "copy_engine";
+  work->transfer = true;
+  work->to_device = to_device;
+  work->device = device_.ordinal;
+  work->retained.push_back(allocation);
+  work->operation_id = next_operation_++;
+  std::vector<BoundArg> access(1);
+  access[0].buffer = true;
+  access[0].writes = to_device;
+  access[0].ptr = static_cast<char *>(allocation->ptr) + offset;
+  access[0].bytes = bytes;
+  pending_.reserve(pending_.size() + 1);
+  work->start = take_event();
+  work->end = take_event();
+  order_after(lane, access, false);
+  cudaError_t e = cudaEventRecord(work->start, stream);
+  if (e == cudaSuccess)
+    e = to_device ? cudaMemcpyAsync(access[0].ptr, host, bytes, cudaMemcpyDefault, stream)
+                  : cudaMemcpyAsync(host, access[0].ptr, bytes, cudaMemcpyDefault, stream);
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(stream);
+    recycle(*work);
+    cuda_failure(e, to_device ? "cudaMemcpyAsync(host to device)" : "cudaMemcpyAsync(device to host)");
+  }
+  pending_.push_back(work);
+  e = cudaEventRecord(work->end, stream);
+  if (e != cudaSuccess) {
+    const std::string text = "CUDA cudaEventRecord after copy failed: " + text_of(e);
+    cudaStreamSynchronize(stream);
+    if (terminal_failure_.empty())
+      terminal_failure_ = text;
+    work->failure = text;
+    throw Error(code_of(e), text);
+  }
+  remember(lane, access, work);
+  (to_device ? counters_.h2d_bytes : counters_.d2h_bytes) += bytes;
+  runtime_event("transfer", "enqueued", to_device ? "host_to_device" : "device_to_host", trace_id_,
+                work->operation_id, bytes);
   return work;
 }
 
@@ -561,7 +694,7 @@ void Engine::finish(const std::shared_ptr<Work> &work) {
       else
         milliseconds = ms;
       // A kernel that gave up a bounded wait reports it through the status word.
-      const int status = __atomic_exchange_n(status_host_, 0, __ATOMIC_ACQ_REL);
+      const int status = work->transfer ? 0 : __atomic_exchange_n(status_host_, 0, __ATOMIC_ACQ_REL);
       if (status != 0 && failure.empty())
         failure = "Kernel " + work->kernel + " abandoned a bounded wait (status " +
                   std::to_string(status) + ")";
@@ -580,12 +713,17 @@ void Engine::finish(const std::shared_ptr<Work> &work) {
   if (completed && failure.empty()) {
     work->info.duration_valid = true;
     work->info.duration_seconds = milliseconds / 1000.0;
-    counters_.gpu_seconds += work->info.duration_seconds;
-    ++counters_.completed_launches;
-    counters_.device_kernels += work->kernels;
+    if (work->transfer) {
+      (work->to_device ? counters_.h2d_seconds : counters_.d2h_seconds) += work->info.duration_seconds;
+    } else {
+      counters_.gpu_seconds += work->info.duration_seconds;
+      ++counters_.completed_launches;
+      counters_.device_kernels += work->kernels;
+    }
   }
-  executions_.push_back({work->kernel, work->variant, failure, work->grid, work->block,
-                         work->kernels, work->info.duration_seconds, completed});
+  if (!work->transfer)
+    executions_.push_back({work->kernel, work->variant, failure, work->grid, work->block,
+                           work->kernels, work->info.duration_seconds, completed});
   if (!failure.empty() && terminal_failure_.empty())
     terminal_failure_ = failure;
   work->failure = failure;
@@ -600,6 +738,8 @@ void Engine::drain_locked() {
   for (const auto &work : pending_)
     finish(work);
   pending_.clear();
+  for (auto &list : records_)
+    list.clear();
   healthy();
 }
 
@@ -664,7 +804,7 @@ void *Engine::workspace_hook(void *self, size_t bytes) {
 }
 
 std::shared_ptr<Work> Engine::marker() {
-  auto work = submit("b200_marker", marker_launch, Dim3{}, Dim3{}, {}, {});
+  auto work = submit("b200_marker", marker_launch, Dim3{}, Dim3{}, {}, {}, true);
   std::lock_guard<std::mutex> lock(mutex_);
   work->keep_end = true;
   work->device = device_.ordinal;

@@ -11,6 +11,7 @@
 // time for sm_100a and launched through the CUDA runtime API.
 #pragma once
 #include "builtin.hpp"
+#include <deque>
 #include <memory>
 #include <mutex>
 
@@ -66,6 +67,8 @@ struct Work {
   uint64_t operation_id = 0;
   bool recorded = false;
   bool keep_end = false; // markers keep their end timestamp for elapsed-time queries
+  bool transfer = false; // a stream-ordered host copy (not a kernel launch)
+  bool to_device = false;
   int device = 0;
   EventInfo info;
   std::string failure;
@@ -97,9 +100,18 @@ public:
   // Runs `launcher` between two events on the context stream; retains the views.
   std::shared_ptr<Work> submit(const std::string &name, Launcher launcher, Dim3 grid, Dim3 block,
                                std::vector<BoundArg> args,
-                               std::vector<std::shared_ptr<Allocation>> retained);
+                               std::vector<std::shared_ptr<Allocation>> retained,
+                               bool barrier = false);
   EventInfo wait(const std::shared_ptr<Work> &work);
-  // An empty command that records a device timestamp (kept until the Work dies).
+  // A host <-> device copy enqueued as a command without blocking the caller. It runs
+  // on the copy lane of its direction after every earlier command that touches the
+  // same bytes (read-after-write, write-after-read, write-after-write), and commands
+  // submitted later order themselves after it the same way; commands on other bytes
+  // overlap it. `host` must stay valid until the Work completes.
+  std::shared_ptr<Work> transfer(bool to_device, const std::shared_ptr<Allocation> &allocation,
+                                 size_t offset, void *host, size_t bytes);
+  // An empty command that records a device timestamp (kept until the Work dies). It
+  // follows every earlier command, copies included.
   std::shared_ptr<Work> marker();
   // Device seconds between the completion of two markers of this engine.
   double elapsed(const std::shared_ptr<Work> &first, const std::shared_ptr<Work> &second);
@@ -126,6 +138,22 @@ private:
   cudaEvent_t take_event();
   void recycle(Work &work);
   static void *workspace_hook(void *self, size_t bytes);
+  // Cross-lane ordering. Lane 0 is the kernel stream, 1 host-to-device copies,
+  // 2 device-to-host copies; each lane is one in-order CUDA stream, so a command
+  // waits at most once per other lane: on the newest unfinished command there whose
+  // byte range overlaps one of its own with at least one of the two writing.
+  static constexpr int lanes = 3;
+  struct Record {
+    uintptr_t begin, end;
+    bool write;
+    std::shared_ptr<Work> work;
+  };
+  cudaStream_t lane_stream(int lane) const { return lane == 0 ? stream_ : copy_streams_[lane - 1]; }
+  void order_after(int lane, const std::vector<BoundArg> &accesses, bool barrier);
+  void remember(int lane, const std::vector<BoundArg> &accesses, const std::shared_ptr<Work> &work);
+  void prune(int lane);
+  std::deque<Record> records_[lanes];
+  cudaStream_t copy_streams_[2] = {};
   void *workspace_ = nullptr;
   size_t workspace_bytes_ = 0;
 

@@ -7,6 +7,7 @@
 // rejection follow runtime/tensor.cpp:448-1038, so callers see the same errors.
 // The entries run the sm_100a kernels of paralyn_b200/csrc/kernels.
 #include "abi_internal.hpp"
+#include <algorithm>
 #include <array>
 #include <cmath>
 #include <cstring>
@@ -14,6 +15,7 @@
 #include <limits>
 #include <mutex>
 #include <unordered_set>
+#include <vector>
 
 namespace pb {
 namespace {
@@ -133,6 +135,37 @@ Layout operand(const pr_tensor_desc_v1 *d, const char *label, uint32_t rank) {
   if (!layout.contiguous)
     fail(PR_UNSUPPORTED, std::string(label) + ": v1 operators require contiguous row-major layout");
   return layout;
+}
+
+// Strided operands (batched matmul only): any validated non-negative layout whose
+// extent fits 32-bit element indexing (reference runtime/tensor.cpp:506-515).
+Layout strided_operand(const pr_tensor_desc_v1 *d, const char *label, uint32_t rank) {
+  const Layout layout = validate(d, label);
+  if (d->rank != rank)
+    fail(PR_INVALID_ARGUMENT, std::string(label) + ": expected rank " + std::to_string(rank));
+  if (layout.bytes / 4 > max_elements)
+    fail(PR_UNSUPPORTED, std::string(label) + ": strided extent exceeds INT32_MAX elements");
+  return layout;
+}
+
+// A written layout must address each element at its own location. Sufficient test
+// (reference runtime/tensor.cpp:516-535): with the dimensions of extent > 1 sorted
+// by stride, each stride exceeds the largest offset the smaller ones reach.
+void injective(const pr_tensor_desc_v1 *d, const char *label) {
+  std::vector<std::pair<uint64_t, uint64_t>> dims; // (stride, extent)
+  for (uint32_t i = 0; i < d->rank; ++i) {
+    if (!d->shape[i])
+      return; // an empty tensor writes nothing
+    if (d->shape[i] > 1)
+      dims.emplace_back(uint64_t(d->strides[i]), d->shape[i]);
+  }
+  std::sort(dims.begin(), dims.end());
+  uint64_t reach = 0;
+  for (const auto &dim : dims) {
+    if (dim.first <= reach)
+      fail(PR_INVALID_ARGUMENT, std::string(label) + ": output layout overlaps itself");
+    reach += (dim.second - 1) * dim.first;
+  }
 }
 
 std::string shape_text(const pr_tensor_desc_v1 *d) {
@@ -338,12 +371,13 @@ PB_EXPORT pr_status pr_tensor_operators_capabilities(pr_tensor_operators_capabil
     pr_tensor_operators_capabilities_v1 caps{};
     caps.struct_size = sizeof(caps);
     caps.version = PR_TENSOR_VERSION_1;
-    caps.operations = PR_TENSOR_OP_MATMUL | PR_TENSOR_OP_BIAS_ACTIVATION | PR_TENSOR_OP_LAYER_NORM |
+    caps.operations = PR_TENSOR_OP_MATMUL | PR_TENSOR_OP_BIAS_ACTIVATION | PR_TENSOR_OP_BATCHED_MATMUL |
+                      PR_TENSOR_OP_REDUCE_ROWS | PR_TENSOR_OP_SOFTMAX_ROWS | PR_TENSOR_OP_LAYER_NORM |
                       PR_TENSOR_OP_ADD;
     caps.activations = PR_TENSOR_ACTIVATION_BIT(PR_ACTIVATION_NONE) |
                        PR_TENSOR_ACTIVATION_BIT(PR_ACTIVATION_RELU) |
                        PR_TENSOR_ACTIVATION_BIT(PR_ACTIVATION_GELU_TANH);
-    caps.reductions = 0;
+    caps.reductions = PR_TENSOR_REDUCE_BIT(PR_REDUCE_SUM) | PR_TENSOR_REDUCE_BIT(PR_REDUCE_MAX);
     caps.max_tensor_elements = max_elements;
     caps.max_row_operator_rows = max_rows;
     caps.max_layer_norm_columns = max_layer_norm_columns;
@@ -447,35 +481,124 @@ PB_EXPORT pr_status pr_bias_activation_f32(pr_queue queue, pr_module operators,
   });
 }
 
-// The remaining transformer-block operators keep their symbols and record checks;
-// their kernels are not part of this build.
-PB_EXPORT pr_status pr_batched_matmul_f32(pr_queue, pr_module, const pr_batched_matmul_v1 *op,
-                                          pr_event *out) {
+// Transformer-block operators (reference runtime/tensor.cpp:847-970): the same
+// record checks, validation order, zero-work rules and launch arguments.
+PB_EXPORT pr_status pr_batched_matmul_f32(pr_queue queue, pr_module operators,
+                                          const pr_batched_matmul_v1 *op, pr_event *out) {
   return boundary("batched_matmul_f32", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");
     *out = 0;
     header(op, "batched matmul");
-    fail(PR_UNSUPPORTED, "Batched matmul has no sm_100a implementation in this build");
+    require(op->a && op->b && op->c, PR_INVALID_ARGUMENT, "Missing batched matmul tensor");
+    const Layout a = strided_operand(op->a, "A", 3), b = strided_operand(op->b, "B", 3),
+                 c = strided_operand(op->c, "C", 3);
+    const uint64_t batch = op->batch, m = op->m, n = op->n, k = op->k;
+    require(batch <= max_elements && m <= max_elements && n <= max_elements && k <= max_elements,
+            PR_UNSUPPORTED, "Batched matmul dimensions must not exceed INT32_MAX");
+    expect_dims(op->a, "A [batch,m,k]", {batch, m, k});
+    expect_dims(op->b, "B [batch,k,n]", {batch, k, n});
+    expect_dims(op->c, "C [batch,m,n]", {batch, m, n});
+    injective(op->c, "C");
+    no_alias(op->c, c, op->a, a, "A");
+    no_alias(op->c, c, op->b, b, "B");
+    same_context(queue, operators, {{op->a, "A"}, {op->b, "B"}, {op->c, "C"}});
+    Owned fn;
+    kernel(operators, k ? "paralyn_batched_matmul_f32" : "paralyn_batched_fill_f32", fn);
+    if (!batch || !m || !n)
+      return; // no output elements: nothing is submitted and no event is invented
+    Owned cv;
+    view(op->c, c, PR_READ_WRITE, cv);
+    const pr_dim3 grid{uint32_t((n + tile - 1) / tile), uint32_t((m + tile - 1) / tile), uint32_t(batch)};
+    if (!k) { // the empty sum: +0.0 at every addressed output element
+      const std::array<pr_argument, 7> args{buffer(cv), u32(m), u32(n), u32(op->c->strides[0]),
+                                            u32(op->c->strides[1]), u32(op->c->strides[2]), f32(0.0f)};
+      call(pr_launch(queue, fn.handle, grid, {tile, tile, 1}, args.data(), 7, out));
+      return;
+    }
+    Owned av, bv;
+    view(op->a, a, PR_READ, av);
+    view(op->b, b, PR_READ, bv);
+    const std::array<pr_argument, 15> args{
+        buffer(av), buffer(bv), buffer(cv), u32(m), u32(n), u32(k),
+        u32(op->a->strides[0]), u32(op->a->strides[1]), u32(op->a->strides[2]),
+        u32(op->b->strides[0]), u32(op->b->strides[1]), u32(op->b->strides[2]),
+        u32(op->c->strides[0]), u32(op->c->strides[1]), u32(op->c->strides[2])};
+    call(pr_launch(queue, fn.handle, grid, {tile, tile, 1}, args.data(), 15, out));
   });
 }
 
-PB_EXPORT pr_status pr_reduce_rows_f32(pr_queue, pr_module, const pr_reduce_rows_v1 *op,
+PB_EXPORT pr_status pr_reduce_rows_f32(pr_queue queue, pr_module operators, const pr_reduce_rows_v1 *op,
                                        pr_event *out) {
   return boundary("reduce_rows_f32", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");
     *out = 0;
     header(op, "row reduction");
-    fail(PR_UNSUPPORTED, "Row reductions have no sm_100a implementation in this build");
+    require(op->op == PR_REDUCE_SUM || op->op == PR_REDUCE_MAX, PR_INVALID_ARGUMENT, "Unknown reduction");
+    require(op->reserved == 0, PR_INVALID_ARGUMENT, "Reserved field must be zero");
+    require(op->x && op->out, PR_INVALID_ARGUMENT, "Missing input or output tensor");
+    const Layout x = operand(op->x, "x", 2), o = operand(op->out, "out", 1);
+    const uint64_t rows = op->x->shape[0], columns = op->x->shape[1];
+    expect_dims(op->out, "out [rows]", {rows});
+    row_limit(rows, "row reduction");
+    no_alias(op->out, o, op->x, x, "x");
+    same_context(queue, operators, {{op->x, "x"}, {op->out, "out"}});
+    Owned fn;
+    kernel(operators, columns ? "paralyn_reduce_rows_f32" : "paralyn_fill_f32", fn);
+    if (!rows)
+      return;
+    Owned ov;
+    view(op->out, o, PR_READ_WRITE, ov);
+    if (!columns) { // empty rows: +0.0 (sum) or -inf (max), written on the GPU
+      const float identity = op->op == PR_REDUCE_MAX ? -std::numeric_limits<float>::infinity() : 0.0f;
+      const std::array<pr_argument, 3> args{buffer(ov), u32(rows), f32(identity)};
+      call(pr_launch(queue, fn.handle, linear(rows), {group, 1, 1}, args.data(), 3, out));
+      return;
+    }
+    Owned xv;
+    view(op->x, x, PR_READ, xv);
+    const std::array<pr_argument, 4> args{buffer(xv), buffer(ov), u32(columns), u32(op->op)};
+    call(pr_launch(queue, fn.handle, {uint32_t(rows), 1, 1}, {group, 1, 1}, args.data(), 4, out));
   });
 }
 
-PB_EXPORT pr_status pr_softmax_rows_f32(pr_queue, pr_module, const pr_softmax_rows_v1 *op,
+PB_EXPORT pr_status pr_softmax_rows_f32(pr_queue queue, pr_module operators, const pr_softmax_rows_v1 *op,
                                         pr_event *out) {
   return boundary("softmax_rows_f32", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");
     *out = 0;
     header(op, "softmax");
-    fail(PR_UNSUPPORTED, "Row softmax has no sm_100a implementation in this build");
+    require(op->causal <= 1, PR_INVALID_ARGUMENT, "causal must be 0 or 1");
+    require(std::isfinite(op->scale) && op->scale > 0.0f, PR_INVALID_ARGUMENT,
+            "scale must be finite and greater than zero");
+    require(op->x && op->out, PR_INVALID_ARGUMENT, "Missing input or output tensor");
+    const uint32_t rank = op->x->rank;
+    require(rank == 2 || rank == 3, PR_INVALID_ARGUMENT,
+            "x: softmax input must have rank 2 [rows,columns] or rank 3 [batch,rows,columns]");
+    const Layout x = operand(op->x, "x", rank), o = operand(op->out, "out", rank);
+    for (uint32_t i = 0; i < rank; ++i)
+      if (op->out->shape[i] != op->x->shape[i])
+        fail(PR_INVALID_ARGUMENT,
+             "out shape " + shape_text(op->out) + " does not match x shape " + shape_text(op->x));
+    const uint64_t columns = op->x->shape[rank - 1], rows = op->x->shape[rank - 2];
+    if (op->causal && columns < rows)
+      fail(PR_INVALID_ARGUMENT, "causal softmax requires columns >= rows (got " + shape_text(op->x) + ")");
+    uint64_t all_rows = rows; // batch * rows for rank 3 (validate already rejected overflow)
+    if (rank == 3 && !mul(all_rows, op->x->shape[0], all_rows))
+      all_rows = std::numeric_limits<uint64_t>::max();
+    row_limit(all_rows, "softmax (batch * rows)");
+    no_alias(op->out, o, op->x, x, "x");
+    same_context(queue, operators, {{op->x, "x"}, {op->out, "out"}});
+    Owned fn;
+    kernel(operators, "paralyn_softmax_rows_f32", fn);
+    if (!x.count)
+      return;
+    const uint64_t total_rows = x.count / columns;
+    Owned xv, ov;
+    view(op->x, x, PR_READ, xv);
+    view(op->out, o, PR_READ_WRITE, ov);
+    const std::array<pr_argument, 6> args{buffer(xv), buffer(ov), u32(columns), u32(rows), u32(op->causal),
+                                          f32(op->scale)};
+    call(pr_launch(queue, fn.handle, {uint32_t(total_rows), 1, 1}, {group, 1, 1}, args.data(), 6, out));
   });
 }
 

@@ -107,6 +107,41 @@ class ChainShard:
                                              self.yd, gathered.targets, row_offset=self.r0, epsilon=self.epsilon)
         return mm, ln
 
+    def step_from_host(self, x_host, y_host, slices=8, gathered=None):
+        """One step with the input X and the output Y in host memory, pipelined.
+
+        x_host / y_host are addresses of this shard's [local_rows, k] and
+        [local_rows, n] float32 host arrays (page-locked, or the copies do not
+        overlap). The rows are cut into `slices` slices (multiples of 128 rows, the
+        GEMM tile height); per slice the queue gets an upload of the X rows, Z = X W,
+        Y = LayerNorm(Z) and a download of the Y rows, all enqueued at once. The
+        copies are stream-ordered (pr_b200_buffer_write_async / read_async), so the
+        upload of slice i+1 and the download of slice i-1 run on the copy engines
+        while slice i computes. Returns the events in submission order; the host
+        arrays must stay valid until the last one completes.
+        """
+        m, k, n = self.local_rows, self.k, self.n
+        tile = 128
+        cuts = sorted({min(m, -(-m * i // slices) // tile * tile) for i in range(1, slices)} | {0, m})
+        events = []
+        for lo, hi in zip(cuts, cuts[1:]):
+            rows = hi - lo
+            xo, yo = 4 * lo * k, 4 * lo * n
+            events.append(b200.write_async(self.queue, self.x, x_host + xo, offset=xo, nbytes=4 * rows * k))
+            zd = TensorDescriptor(self.z, (rows, n), yo)
+            yd = TensorDescriptor(self.y, (rows, n), yo)
+            events.append(matmul_into(self.queue, self.resources.module, TensorDescriptor(self.x, (rows, k), xo),
+                                      self.wd, zd, m=rows, n=n, k=k))
+            if gathered is None:
+                events.append(layer_norm_into(self.queue, self.resources.module, zd, self.gd, self.bd, yd,
+                                              epsilon=self.epsilon))
+            else:
+                events.append(b200.layer_norm_gather_into(self.queue, self.resources.module, zd, self.gd, self.bd,
+                                                          yd, gathered.targets, row_offset=self.r0 + lo,
+                                                          epsilon=self.epsilon))
+            events.append(b200.read_async(self.queue, self.y, y_host + yo, offset=yo, nbytes=4 * rows * n))
+        return [e for e in events if e is not None]
+
     def flops(self):
         return 2 * self.local_rows * self.n * self.k
 

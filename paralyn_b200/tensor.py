@@ -52,6 +52,22 @@ class BiasActivationRecord(_c.Structure):
                 ("reserved", _c.c_uint32), ("x", _DESC), ("bias", _DESC), ("out", _DESC)]
 
 
+class BatchedMatmulRecord(_c.Structure):
+    _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32), ("batch", _c.c_uint64),
+                ("m", _c.c_uint64), ("n", _c.c_uint64), ("k", _c.c_uint64), ("a", _DESC), ("b", _DESC),
+                ("c", _DESC)]
+
+
+class ReduceRowsRecord(_c.Structure):
+    _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32), ("op", _c.c_int),
+                ("reserved", _c.c_uint32), ("x", _DESC), ("out", _DESC)]
+
+
+class SoftmaxRowsRecord(_c.Structure):
+    _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32), ("causal", _c.c_uint32),
+                ("scale", _c.c_float), ("x", _DESC), ("out", _DESC)]
+
+
 class LayerNormRecord(_c.Structure):
     _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32), ("epsilon", _c.c_float),
                 ("reserved", _c.c_uint32), ("x", _DESC), ("gamma", _DESC), ("beta", _DESC),
@@ -81,6 +97,9 @@ def _api(lib):
             "pr_matmul_f32": (_c.c_int, [h, h, ptr(MatmulRecord), ptr(h)]),
             "pr_bias_activation_f32": (_c.c_int, [h, h, ptr(BiasActivationRecord), ptr(h)]),
             "pr_layer_norm_f32": (_c.c_int, [h, h, ptr(LayerNormRecord), ptr(h)]),
+            "pr_batched_matmul_f32": (_c.c_int, [h, h, ptr(BatchedMatmulRecord), ptr(h)]),
+            "pr_reduce_rows_f32": (_c.c_int, [h, h, ptr(ReduceRowsRecord), ptr(h)]),
+            "pr_softmax_rows_f32": (_c.c_int, [h, h, ptr(SoftmaxRowsRecord), ptr(h)]),
             "pr_add_f32": (_c.c_int, [h, h, ptr(AddRecord), ptr(h)]),
             "pr_tensor_operators_capabilities": (_c.c_int, [ptr(CapabilitiesRecord)]),
         }
@@ -119,14 +138,21 @@ class TensorDescriptor:
         if len(shape) > MAX_RANK:
             raise ValueError(f"rank exceeds {MAX_RANK}")
         desc = TensorDescRecord()
-        dims = (_c.c_uint64 * max(1, len(shape)))(*shape)
-        lib.check(lib.api.pr_tensor_desc_contiguous(self.buffer.handle, self.byte_offset, Type.F32,
-                                                    len(shape), dims, _c.byref(desc)))
-        if self.strides is not None:
-            if len(self.strides) != len(shape):
-                raise ValueError("strides must have one entry per dimension")
-            for index, stride in enumerate(self.strides):
-                desc.strides[index] = _int(stride, -(1 << 63), (1 << 63) - 1, "stride")
+        if self.strides is None:
+            dims = (_c.c_uint64 * max(1, len(shape)))(*shape)
+            lib.check(lib.api.pr_tensor_desc_contiguous(self.buffer.handle, self.byte_offset, Type.F32,
+                                                        len(shape), dims, _c.byref(desc)))
+            return desc
+        if len(self.strides) != len(shape):
+            raise ValueError("strides must have one entry per dimension")
+        # A strided view may reach past the contiguous extent of its shape, so the
+        # record is filled directly; the operators validate it against the buffer.
+        desc.struct_size, desc.version = _c.sizeof(TensorDescRecord), TENSOR_VERSION_1
+        desc.buffer, desc.byte_offset = self.buffer.handle, _int(self.byte_offset, 0, (1 << 64) - 1, "byte_offset")
+        desc.dtype, desc.rank = Type.F32, len(shape)
+        for index, (extent, stride) in enumerate(zip(shape, self.strides)):
+            desc.shape[index] = _int(extent, 0, (1 << 64) - 1, "shape")
+            desc.strides[index] = _int(stride, -(1 << 63), (1 << 63) - 1, "stride")
         return desc
 
     def required_bytes(self):
@@ -224,6 +250,32 @@ def bias_activation_into(queue, operators, x, bias, out, *, activation=Activatio
                                   int(Activation(activation)), 0, _c.pointer(xd),
                                   _c.pointer(bd) if bd is not None else None, _c.pointer(od))
     return _submit(queue, operators, "pr_bias_activation_f32", record)
+
+
+def batched_matmul_into(queue, operators, a, b, c, *, batch, m, n, k):
+    """C[z] = A[z] B[z] for rank-3 (possibly strided) descriptors [batch,m,k] x [batch,k,n]."""
+    descs = [x._native() for x in (a, b, c)]
+    record = BatchedMatmulRecord(_c.sizeof(BatchedMatmulRecord), TENSOR_VERSION_1,
+                                 *(_int(v, 0, (1 << 64) - 1, label) for v, label in
+                                   ((batch, "batch"), (m, "m"), (n, "n"), (k, "k"))),
+                                 *(_c.pointer(d) for d in descs))
+    return _submit(queue, operators, "pr_batched_matmul_f32", record)
+
+
+def reduce_rows_into(queue, operators, x, out, *, op=Reduce.SUM):
+    """out[i] = sum or max of row i of x [rows, columns] in the fixed 256-lane order."""
+    xd, od = x._native(), out._native()
+    record = ReduceRowsRecord(_c.sizeof(ReduceRowsRecord), TENSOR_VERSION_1, int(Reduce(op)), 0,
+                              _c.pointer(xd), _c.pointer(od))
+    return _submit(queue, operators, "pr_reduce_rows_f32", record)
+
+
+def softmax_rows_into(queue, operators, x, out, *, scale=1.0, causal=False):
+    """Row softmax of scale*x over the last dimension of a rank-2 or rank-3 descriptor."""
+    xd, od = x._native(), out._native()
+    record = SoftmaxRowsRecord(_c.sizeof(SoftmaxRowsRecord), TENSOR_VERSION_1, _flag(causal, "causal"),
+                               _real(scale, "scale"), _c.pointer(xd), _c.pointer(od))
+    return _submit(queue, operators, "pr_softmax_rows_f32", record)
 
 
 def layer_norm_into(queue, operators, x, gamma, beta, out, *, epsilon=1e-5):
@@ -465,6 +517,47 @@ def gelu(x):
 
 def bias_gelu(x, bias):
     return _bias_activation(x, bias, Activation.GELU_TANH)
+
+
+def batched_matmul(a, b):
+    """C[i] = A[i] B[i] for contiguous rank-3 tensors [batch,m,k] x [batch,k,n]."""
+    context = _same_context(a, b)
+    if a.ndim != 3 or b.ndim != 3:
+        raise ValueError("batched_matmul requires rank-3 tensors")
+    batch, m, k = a.shape
+    if b.shape[0] != batch or b.shape[1] != k:
+        raise ValueError(f"batched_matmul shapes differ: {a.shape} x {b.shape}")
+    n = b.shape[2]
+    resources = operators_of(context)
+    return _output(context, (batch, m, n), a.device, lambda c: batched_matmul_into(
+        resources.queue, resources.module, a.descriptor(), b.descriptor(), c, batch=batch, m=m, n=n, k=k))
+
+
+def _reduce(x, op):
+    context = _same_context(x)
+    if x.ndim != 2:
+        raise ValueError("row reductions require rank-2 tensors")
+    resources = operators_of(context)
+    return _output(context, (x.shape[0],), x.device, lambda out: reduce_rows_into(
+        resources.queue, resources.module, x.descriptor(), out, op=op))
+
+
+def row_sum(x):
+    """Row sums of a rank-2 tensor in the fixed 256-lane order."""
+    return _reduce(x, Reduce.SUM)
+
+
+def row_max(x):
+    """Row maxima (NaN-propagating, +0.0 preferred over -0.0, -inf for empty rows)."""
+    return _reduce(x, Reduce.MAX)
+
+
+def softmax(x, *, scale=1.0, causal=False):
+    """Numerically stable row softmax of scale*x over the last dimension."""
+    context = _same_context(x)
+    resources = operators_of(context)
+    return _output(context, x.shape, x.device, lambda out: softmax_rows_into(
+        resources.queue, resources.module, x.descriptor(), out, scale=scale, causal=causal))
 
 
 def layer_norm(x, gamma, beta, *, epsilon=1e-5):

@@ -12,6 +12,15 @@ Contents (inputs are seeded synthetic data from paralyn_b200.synthetic):
                               the reference's float64 LayerNorm bound layer_norm_row
                               (same header :133-147) on the LayerNorm test shapes of
                               tests/native/transformer_ops_tests.cpp:397-400
+  tmax_<n>                    the reference's tree_max_f32 of the same tree inputs (:182-191)
+  tmax_special_{x,max}        tree_max_f32 of the NaN / signed-zero / infinity rows of
+                              tests/native/transformer_ops_tests.cpp:277-283
+  sm_<b>x<r>x<c>_{x,value,error,meta}
+                              the reference's float64 softmax_row bound (same header
+                              :122-132) on the softmax test shapes of
+                              tests/native/transformer_ops_tests.cpp:341-350 (columns
+                              <= 1000); meta = (scale, causal)
+  dot_<k>_{a,b,value,error}   the reference's float64 dot bound (same header :101-111)
   prk_emit_cuda_sha256        SHA-256 of the CUDA the reference's codegen emits for
                               paralyn_b200.prk.operators() (must equal the reference's
                               reviewed goldens tests/cuda/golden/array_{add,affine}.cu)
@@ -36,6 +45,14 @@ TREE_LENGTHS = (1, 7, 255, 256, 257, 1000, 4096, 100003)
 LN_CASES = ((1, 1, 0.0, 1.0, 1e-5), (3, 17, 0.5, 2.0, 1e-5), (4, 256, 0.0, 1.0, 1e-5),
             (2, 257, -3.0, 4.0, 1e-6), (5, 1000, 0.0, 1.0, 1e-5), (3, 64, 1000.0, 1.0, 1e-5),
             (2, 48, 0.0, 1e-3, 1e-2))
+
+
+# (batch, rows, columns, scale, magnitude, causal) of the reference softmax cases with
+# at most 1000 columns.
+SOFTMAX_CASES = ((1, 1, 1, 1.0, 4.0, False), (1, 3, 17, 1.0, 4.0, False), (1, 5, 256, 0.125, 16.0, False),
+                 (1, 2, 1000, 1.0, 8.0, False), (4, 9, 9, 0.35355339, 8.0, True), (2, 5, 12, 1.0, 8.0, True),
+                 (3, 7, 7, 3.0, 4.0, False), (1, 1, 300, 1.0, 100.0, True), (1, 17, 17, 1.0, 60.0, True))
+DOT_LENGTHS = (1, 5, 16, 47, 257, 300)
 
 
 def main():
@@ -67,6 +84,33 @@ def main():
         out[key + "_gamma"], out[key + "_beta"] = g, b
         out[key + "_value"], out[key + "_error"] = value, error
         out[key + "_eps"] = np.array([eps], np.float32)
+    for i, n in enumerate(TREE_LENGTHS):
+        x = synthetic.uniform(100 + i, 0, n, 4.0)
+        out[f"tmax_{n}"] = np.array([ref.ref_tree_max_f32(x, n)], np.float32)
+    nan, inf = np.float32(np.nan), np.float32(np.inf)
+    special = np.array([[1, nan, -2, 3], [-0.0, 0.0, -0.0, -1], [-0.0, -0.0, -3, -1], [inf, -inf, 1, 2],
+                        [-inf, -inf, -inf, -inf], [inf, 1, inf, 0]], np.float32)
+    out["tmax_special_x"] = special
+    out["tmax_special_max"] = np.array([ref.ref_tree_max_f32(np.ascontiguousarray(r), 4) for r in special],
+                                       np.float32)
+    for i, (batch, rows, cols, scale, magnitude, causal) in enumerate(SOFTMAX_CASES):
+        x = synthetic.uniform(500 + i, 0, batch * rows * cols, magnitude).reshape(batch * rows, cols)
+        value = np.empty_like(x, dtype=np.float64)
+        error = np.empty_like(x, dtype=np.float64)
+        for r in range(batch * rows):
+            visible = (r % rows) + (cols - rows) + 1 if causal else cols
+            ref.ref_softmax_row(np.ascontiguousarray(x[r]), cols, float(np.float32(scale)), visible, value[r], error[r])
+        key = f"sm_{batch}x{rows}x{cols}"
+        out[key + "_x"], out[key + "_value"], out[key + "_error"] = x, value, error
+        out[key + "_meta"] = np.array([np.float32(scale), float(causal)], np.float64)
+    for i, k in enumerate(DOT_LENGTHS):
+        a = synthetic.uniform(600 + i, 0, k, 2.0)
+        b = synthetic.uniform(700 + i, 0, k, 3.0)
+        v, e = ctypes.c_double(), ctypes.c_double()
+        ref.ref_dot(a, b, k, ctypes.byref(v), ctypes.byref(e))
+        out[f"dot_{k}_a"], out[f"dot_{k}_b"] = a, b
+        out[f"dot_{k}_value"] = np.array([v.value])
+        out[f"dot_{k}_error"] = np.array([e.value])
     data = prk.serialize(prk.operators()[:2])
     text = ctypes.create_string_buffer(1 << 16)
     if ref.ref_prk_emit_cuda(data, len(data), text, len(text)) != 0:

@@ -168,3 +168,69 @@ def test_reference_sources_reproduce_fixture(reference_checkout):
         pytest.skip("oracle/_ref not built")
     x = synthetic.uniform(100 + 7, 0, 100003, 4.0)
     assert np.float32(ref.ref_tree_sum_f32(x, x.size)).tobytes() == GOLDEN["tree_100003_sum"].tobytes()
+
+
+# ---- transformer-block row operators and the batched matmul ----
+SM_KEYS = sorted({k.rsplit("_", 1)[0] for k in GOLDEN.files if k.startswith("sm_")})
+DOT_LENGTHS = sorted(int(k.split("_")[1]) for k in GOLDEN.files if k.startswith("dot_") and k.endswith("_a"))
+
+
+@pytest.mark.parametrize("index,n", list(enumerate(TREE_LENGTHS)))
+def test_tree_max_matches_reference_bitwise(index, n):
+    x = synthetic.uniform(100 + index, 0, n, 4.0)
+    got = oracle.reduce_rows(x.reshape(1, n), 1)
+    assert got.tobytes() == GOLDEN[f"tmax_{n}"].tobytes()
+
+
+def test_reduce_specials_match_reference():
+    x = GOLDEN["tmax_special_x"]
+    got = oracle.reduce_rows(x, 1)
+    want = GOLDEN["tmax_special_max"]
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    finite = ~np.isnan(want)
+    assert got[finite].tobytes() == want[finite].tobytes()  # signed zeros included
+    sums = oracle.reduce_rows(x, 0)  # reference expectations, transformer_ops_tests.cpp:293-298
+    assert np.isnan(sums[0]) and sums[1] == -1.0 and sums[2] == -4.0 and np.isnan(sums[3])
+    assert sums[4] == -np.inf and sums[5] == np.inf
+    assert oracle.reduce_rows(np.zeros((3, 0), np.float32), 0).tobytes() == np.zeros(3, np.float32).tobytes()
+    assert np.all(oracle.reduce_rows(np.zeros((2, 0), np.float32), 1) == -np.inf)
+
+
+@pytest.mark.parametrize("key", SM_KEYS)
+def test_softmax_bound_restatement_matches_reference(key):
+    x = GOLDEN[key + "_x"]
+    scale, causal = GOLDEN[key + "_meta"]
+    batch, rows, cols = (int(v) for v in key[3:].split("x"))
+    value, error = oracle.softmax_bound(x.reshape(batch, rows, cols), np.float32(scale), bool(causal))
+    np.testing.assert_allclose(value.reshape(x.shape), GOLDEN[key + "_value"], rtol=1e-13, atol=0)
+    np.testing.assert_allclose(error.reshape(x.shape), GOLDEN[key + "_error"], rtol=1e-12, atol=0)
+
+
+@pytest.mark.parametrize("k", DOT_LENGTHS)
+def test_dot_bound_matches_reference(k):
+    a, b = GOLDEN[f"dot_{k}_a"], GOLDEN[f"dot_{k}_b"]
+    value, error = oracle.batched_dot_bound(a, (0, (0, 0, 1)), b, (0, (0, 1, 0)), 1, 1, 1, k)
+    np.testing.assert_allclose(value.ravel(), GOLDEN[f"dot_{k}_value"], rtol=1e-13, atol=0)
+    np.testing.assert_allclose(error.ravel(), GOLDEN[f"dot_{k}_error"], rtol=1e-12, atol=0)
+
+
+def test_batched_matmul_strided_views_follow_the_sequential_order():
+    # attention-style head split (tests/native/transformer_ops_tests.cpp:194-206): Q_h and
+    # K_h^T are strided views into one [T, 3HD] storage.
+    T_, H, D = 19, 3, 7
+    W = 3 * H * D
+    qkv = synthetic.uniform(77, 0, T_ * W, 1.0)
+    c = np.full(H * T_ * T_, 12345.0, np.float32)
+    oracle.batched_matmul(qkv, (0, (D, W, 1)), qkv, (H * D, (D, 1, W)), c, (0, (T_ * T_, T_, 1)), H, T_, T_, D)
+    q = qkv.reshape(T_, 3, H, D)[:, 0].transpose(1, 0, 2)  # [H, T, D]
+    k = qkv.reshape(T_, 3, H, D)[:, 1].transpose(1, 0, 2)
+    for h in range(H):
+        want = oracle.matmul(np.ascontiguousarray(q[h]), np.ascontiguousarray(k[h]), T_, T_, D, transpose_b=True)
+        assert c.reshape(H, T_, T_)[h].tobytes() == want.tobytes()
+    # a strided output writes only the addressed elements
+    out = np.full(80, 12345.0, np.float32)
+    oracle.batched_matmul(np.zeros(1, np.float32), (0, (0, 0, 1)), np.zeros(1, np.float32), (0, (0, 1, 0)), out,
+                          (1, (40, 10, 2)), 2, 3, 4, 0)
+    addressed = {1 + z * 40 + i * 10 + j * 2 for z in range(2) for i in range(3) for j in range(4)}
+    for idx in range(80):
+        assert out[idx] == (0.0 if idx in addressed else 12345.0)

@@ -64,6 +64,7 @@ def lib():
                                               _size]),
             "orc_batched_dot_bound": (None, [_f32p, _View, _f32p, _View, _size, _size, _size, _size, _f64p,
                                              _f64p]),
+            "orc_gelu_bound": (None, [_f32p, _size, _f64p, _f64p]),
         }
         for name, (restype, argtypes) in sig.items():
             f = getattr(_lib, name)
@@ -210,6 +211,15 @@ def batched_dot_bound(a, a_view, b, b_view, batch, m, n, k):
     return value, error
 
 
+def gelu_bound(x):
+    """(value, error) float64 arrays of the tanh-form GELU of the FP32 inputs x."""
+    x = _f32(x)
+    value = np.empty(x.shape, np.float64)
+    error = np.empty(x.shape, np.float64)
+    lib().orc_gelu_bound(x, x.size, value, error)
+    return value, error
+
+
 def within(gpu, value, error):
     """The reference's acceptance rule: |gpu - value| <= error + 2^-45 |value| + 2^-126; NaN fails."""
     gpu = np.asarray(gpu, np.float64)
@@ -242,4 +252,6 @@ def reference():
         _ref.ref_softmax_row.argtypes = [_f32p, _c.c_size_t, _c.c_double, _c.c_size_t, _f64p, _f64p]
         _ref.ref_dot.restype = None
         _ref.ref_dot.argtypes = [_f32p, _f32p, _c.c_size_t, _c.POINTER(_c.c_double), _c.POINTER(_c.c_double)]
+        _ref.ref_gelu.restype = None
+        _ref.ref_gelu.argtypes = [_f32p, _c.c_size_t, _f64p, _f64p]
     return _ref

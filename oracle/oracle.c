@@ -36,6 +36,8 @@
  *                          tests/native/transformer_ops_tests.cpp:129-169
  *   orc_batched_dot_bound  float64 dot bound of the same checker (gamma_k,
  *                          examples/native/transformer_reference.hpp:100-111)
+ *   orc_gelu_bound         float64 bound of the tanh-form GELU with the FP32
+ *                          constants, same header :74-80 (tanh at 5 ulp), :113-121
  *
  * Threaded (_mt) variants split rows or ranges across OpenMP threads; each
  * output element is still computed in the reference order, so they are
@@ -461,4 +463,29 @@ void orc_batched_dot_bound(const float *a, orc_view av, const float *b, orc_view
         value[o] = v;
         error[o] = gamma_n((double)k) * magnitude + (double)k * ORC_TINY;
       }
+}
+
+static orc_b b_tanh(orc_b a) {
+  orc_b r;
+  r.v = tanh(a.v);
+  const double lower = fabs(a.v) - a.e > 0.0 ? fabs(a.v) - a.e : 0.0;
+  const double t = tanh(lower);
+  const double e0 = (1.0 - t * t) * a.e; /* sech^2 decreases in |x| */
+  r.e = e0 + rounded(fabs(r.v) + e0, 5.0 * 2.0 * ORC_U);
+  return r;
+}
+
+/* gelu(x) = (0.5 x)(1 + tanh(c0 (x + c1 ((x x) x)))) with c0, c1 the FP32 constants. */
+void orc_gelu_bound(const float *x, size_t n, double *value, double *error) {
+  const orc_b c0 = {(double)0.7978845608028654f, 0.0}, c1 = {(double)0.044715f, 0.0};
+  const orc_b half = {0.5, 0.0}, one = {1.0, 0.0};
+  for (size_t i = 0; i < n; ++i) {
+    const orc_b v = {(double)x[i], 0.0};
+    const orc_b cube = b_mul(b_mul(v, v), v);
+    const orc_b inner = b_add(v, b_mul(c1, cube));
+    const orc_b t = b_tanh(b_mul(c0, inner));
+    const orc_b y = b_mul(b_mul(half, v), b_add(one, t));
+    value[i] = y.v;
+    error[i] = y.e;
+  }
 }

@@ -11,6 +11,7 @@
 //   ref_tree_max_f32    tree_max_f32 (same header :182-191)
 //   ref_softmax_row     softmax_row float64 bound (same header :122-132)
 //   ref_dot             dot float64 bound (same header :101-111)
+//   ref_gelu            gelu float64 bound (same header :113-121)
 #include "paralyn/artifact.hpp"
 #include "paralyn/cuda_codegen.hpp"
 #include "transformer_reference.hpp"
@@ -65,5 +66,13 @@ void ref_dot(const float *a, const float *b, size_t k, double *value, double *er
   const auto d = r::dot(r::exact_values(std::vector<float>(a, a + k)), r::exact_values(std::vector<float>(b, b + k)));
   *value = d.v;
   *error = d.e;
+}
+void ref_gelu(const float *x, size_t n, double *value, double *error) {
+  namespace r = paralyn_reference;
+  for (size_t i = 0; i < n; ++i) {
+    const auto y = r::gelu(r::exact(double(x[i])));
+    value[i] = y.v;
+    error[i] = y.e;
+  }
 }
 }

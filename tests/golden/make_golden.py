@@ -21,6 +21,9 @@ Contents (inputs are seeded synthetic data from paralyn_b200.synthetic):
                               tests/native/transformer_ops_tests.cpp:341-350 (columns
                               <= 1000); meta = (scale, causal)
   dot_<k>_{a,b,value,error}   the reference's float64 dot bound (same header :101-111)
+  gelu_{x,value,error}        the reference's float64 GELU bound (same header :113-121) on
+                              synthetic.uniform(900, 0, 1000, 8) and the saturation and
+                              special points of tests/native/transformer_ops_tests.cpp:482-499
   prk_emit_cuda_sha256        SHA-256 of the CUDA the reference's codegen emits for
                               paralyn_b200.prk.operators() (must equal the reference's
                               reviewed goldens tests/cuda/golden/array_{add,affine}.cu)
@@ -111,6 +114,11 @@ def main():
         out[f"dot_{k}_a"], out[f"dot_{k}_b"] = a, b
         out[f"dot_{k}_value"] = np.array([v.value])
         out[f"dot_{k}_error"] = np.array([e.value])
+    gx = np.concatenate([synthetic.uniform(900, 0, 1000, 8.0),
+                         np.array([30, -30, 0, -0.0, 1e-20, -1e-3, 5.5, -5.5], np.float32)]).astype(np.float32)
+    gv, ge = np.empty(gx.size, np.float64), np.empty(gx.size, np.float64)
+    ref.ref_gelu(gx, gx.size, gv, ge)
+    out["gelu_x"], out["gelu_value"], out["gelu_error"] = gx, gv, ge
     data = prk.serialize(prk.operators()[:2])
     text = ctypes.create_string_buffer(1 << 16)
     if ref.ref_prk_emit_cuda(data, len(data), text, len(text)) != 0:

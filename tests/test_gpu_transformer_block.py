@@ -1,0 +1,220 @@
+"""GELU and the reference's pre-LN encoder block on the GPU.
+
+GELU (tanh form, FP32 constants) is checked against the reference's float64 bound
+(tanh budgeted at 5 ulp) on the cases of tests/native/transformer_ops_tests.cpp:448-499,
+with the documented exact results for NaN, +-inf, +-0 and +-1e20.
+
+The block follows docs/transformer-operators.md:195-258: T=24 tokens, d=48, 4
+heads of 12, d_ff=192, eps 1e-5, softmax scale fl32(1/sqrt(12)), causal and
+bidirectional, sizes not multiples of 16. It runs as exactly the reference's 15
+launches through the tensor provider, with the heads as strided views of the fused
+QKV output (no copies) and the attention output written through C strides into the
+concatenated [T, d] buffer. Every stage is read back and checked locally against the
+oracle on the GPU's own inputs to that stage: LayerNorm, bias adds and residual
+adds bit for bit, GEMMs within the float64 dot bound, softmax and GELU within the
+reference's float64 bounds. The reference's published block hashes depend on Metal's
+exp/tanh and are not reproducible on any other device, so they are not used.
+"""
+import importlib
+import json
+
+import numpy as np
+import pytest
+
+import oracle
+import paralyn_b200 as p
+from paralyn_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+T = importlib.import_module("paralyn_b200.tensor")
+
+
+def run_activation(context, x, bias=None, x_offset=0, out_offset=0):
+    ops = T.operators_of(context)
+    rows, cols = x.shape
+    xb = context.buffer(4 * (x_offset + x.size) + 16)
+    xb.write(np.concatenate([np.full(x_offset, 5.0, np.float32), x.ravel()]))
+    ob = context.buffer(4 * (out_offset + x.size) + 16)
+    ob.write(np.full(out_offset + x.size, 12345.0, np.float32))
+    bb = None
+    try:
+        bd = None
+        if bias is not None:
+            bb = context.buffer(4 * bias.size)
+            bb.write(bias)
+            bd = T.TensorDescriptor(bb, (cols,))
+        event = T.bias_activation_into(ops.queue, ops.module, T.TensorDescriptor(xb, (rows, cols), 4 * x_offset), bd,
+                                       T.TensorDescriptor(ob, (rows, cols), 4 * out_offset),
+                                       activation=p.Activation.GELU_TANH)
+        event.wait()
+        event.close()
+        got = np.frombuffer(ob.read(), np.float32)[:out_offset + x.size]
+        assert np.all(got[:out_offset] == 12345.0)
+        return got[out_offset:].reshape(rows, cols)
+    finally:
+        for buf in (xb, ob, bb):
+            if buf is not None:
+                buf.close()
+
+
+@pytest.mark.parametrize("count", [1, 255, 1000, 100003])
+def test_gelu_within_reference_bound(context, count):
+    x = synthetic.uniform(900 + count, 0, count, 8.0).reshape(1, count)
+    for offsets in ((0, 0), (3, 1)):
+        got = run_activation(context, x, None, *offsets)
+        value, error = oracle.gelu_bound(x)
+        assert np.all(oracle.within(got, value, error))
+
+
+def test_bias_gelu_within_reference_bound(context):
+    rows, cols = 33, 70
+    x = synthetic.uniform(950, 0, rows * cols, 4.0).reshape(rows, cols)
+    bias = synthetic.uniform(951, 0, cols, 2.0)
+    got = run_activation(context, x, bias)
+    summed = (x + bias[None, :]).astype(np.float32)  # fl(x + bias), one rounding
+    value, error = oracle.gelu_bound(summed)
+    assert np.all(oracle.within(got, value, error))
+
+
+def test_gelu_specials(context):
+    special = np.array([[np.nan, np.inf, -np.inf, 1e20, -1e20, 0.0, -0.0, 30.0, -30.0]], np.float32)
+    got = run_activation(context, special)[0]
+    assert np.isnan(got[0]) and got[1] == np.inf and np.isnan(got[2])
+    assert got[3] == np.float32(1e20)
+    assert got[4] == 0.0 and np.signbit(got[4])
+    assert got[5] == 0.0 and not np.signbit(got[5]) and got[6] == 0.0 and np.signbit(got[6])
+    value, error = oracle.gelu_bound(special[0, 7:])
+    assert np.all(oracle.within(got[7:], value, error))
+
+
+# ---------------------------------------------------------------- the encoder block
+TOKENS, D, HEADS, DFF = 24, 48, 4, 192
+DH = D // HEADS
+
+
+class Block:
+    """Device buffers of one block and the 15 launches, in the reference's order."""
+
+    def __init__(self, context, causal, seed=2026):
+        self.ctx, self.causal = context, causal
+        self.ops = T.operators_of(context)
+        g = synthetic.uniform
+        self.host = {
+            "x": g(seed, 0, TOKENS * D, 1.0).reshape(TOKENS, D),
+            "gamma1": (1 + g(seed + 1, 0, D, 0.25)).astype(np.float32), "beta1": g(seed + 2, 0, D, 0.25),
+            "w_qkv": g(seed + 3, 0, D * 3 * D, 0.125).reshape(D, 3 * D), "b_qkv": g(seed + 4, 0, 3 * D, 0.25),
+            "w_o": g(seed + 5, 0, D * D, 0.125).reshape(D, D), "b_o": g(seed + 6, 0, D, 0.25),
+            "gamma2": (1 + g(seed + 7, 0, D, 0.25)).astype(np.float32), "beta2": g(seed + 8, 0, D, 0.25),
+            "w_1": g(seed + 9, 0, D * DFF, 0.125).reshape(D, DFF), "b_1": g(seed + 10, 0, DFF, 0.25),
+            "w_2": g(seed + 11, 0, DFF * D, 0.0625).reshape(DFF, D), "b_2": g(seed + 12, 0, D, 0.25),
+        }
+        shapes = {"ln1": (TOKENS, D), "qkv": (TOKENS, 3 * D), "qkv_b": (TOKENS, 3 * D),
+                  "scores": (HEADS, TOKENS, TOKENS), "probs": (HEADS, TOKENS, TOKENS), "attn": (TOKENS, D),
+                  "proj": (TOKENS, D), "proj_b": (TOKENS, D), "h1": (TOKENS, D), "ln2": (TOKENS, D),
+                  "ff1": (TOKENS, DFF), "ff1_g": (TOKENS, DFF), "ff2": (TOKENS, D), "ff2_b": (TOKENS, D),
+                  "out": (TOKENS, D)}
+        self.shapes = {**{k: v.shape for k, v in self.host.items()}, **shapes}
+        self.buf = {}
+        for name, shape in self.shapes.items():
+            self.buf[name] = context.buffer(4 * int(np.prod(shape)))
+            if name in self.host:
+                self.buf[name].write(np.ascontiguousarray(self.host[name], np.float32))
+
+    def d(self, name, shape=None, offset=0, strides=None):
+        return T.TensorDescriptor(self.buf[name], shape or self.shapes[name], offset, strides)
+
+    def run(self):
+        q, m = self.ops.queue, self.ops.module
+        d = self.d
+        events = [
+            T.layer_norm_into(q, m, d("x"), d("gamma1"), d("beta1"), d("ln1")),
+            T.matmul_into(q, m, d("ln1"), d("w_qkv"), d("qkv"), m=TOKENS, n=3 * D, k=D),
+            T.bias_activation_into(q, m, d("qkv"), d("b_qkv"), d("qkv_b")),
+            # Q_h [H,T,Dh] strides [Dh, 3d, 1]; K_h^T [H,Dh,T] strides [Dh, 1, 3d] at column d
+            T.batched_matmul_into(q, m, d("qkv_b", (HEADS, TOKENS, DH), 0, (DH, 3 * D, 1)),
+                                  d("qkv_b", (HEADS, DH, TOKENS), 4 * D, (DH, 1, 3 * D)), d("scores"),
+                                  batch=HEADS, m=TOKENS, n=TOKENS, k=DH),
+            T.softmax_rows_into(q, m, d("scores"), d("probs"), scale=float(np.float32(1 / np.sqrt(12.0))),
+                                causal=self.causal),
+            # P_h V_h with V_h at column 2d, written into the concatenated [T, d] output
+            T.batched_matmul_into(q, m, d("probs"), d("qkv_b", (HEADS, TOKENS, DH), 8 * D, (DH, 3 * D, 1)),
+                                  d("attn", (HEADS, TOKENS, DH), 0, (DH, D, 1)), batch=HEADS, m=TOKENS, n=DH,
+                                  k=TOKENS),
+            T.matmul_into(q, m, d("attn"), d("w_o"), d("proj"), m=TOKENS, n=D, k=D),
+            T.bias_activation_into(q, m, d("proj"), d("b_o"), d("proj_b")),
+            T.add_into(q, m, d("x"), d("proj_b"), d("h1")),
+            T.layer_norm_into(q, m, d("h1"), d("gamma2"), d("beta2"), d("ln2")),
+            T.matmul_into(q, m, d("ln2"), d("w_1"), d("ff1"), m=TOKENS, n=DFF, k=D),
+            T.bias_activation_into(q, m, d("ff1"), d("b_1"), d("ff1_g"), activation=p.Activation.GELU_TANH),
+            T.matmul_into(q, m, d("ff1_g"), d("w_2"), d("ff2"), m=TOKENS, n=D, k=DFF),
+            T.bias_activation_into(q, m, d("ff2"), d("b_2"), d("ff2_b")),
+            T.add_into(q, m, d("h1"), d("ff2_b"), d("out")),
+        ]
+        events[-1].wait()
+        for e in events:
+            e.close()
+        return len(events)
+
+    def read(self, name):
+        return np.frombuffer(self.buf[name].read(), np.float32).reshape(self.shapes[name]).copy()
+
+    def close(self):
+        for b in self.buf.values():
+            b.close()
+
+
+def check_gemm(a, b, got, a_view, b_view, batch, m, n, k):
+    value, error = oracle.batched_dot_bound(a, a_view, b, b_view, batch, m, n, k)
+    assert np.all(oracle.within(got.reshape(value.shape), value, error))
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_encoder_block_stage_local(context, tmp_path, causal):
+    block = Block(context, causal)
+    try:
+        before = len(json.loads(_evidence(context, tmp_path / "before"))["launches"])
+        assert block.run() == 15
+        launches = json.loads(_evidence(context, tmp_path / "after"))["launches"][before:]
+        assert [l["kernel"] for l in launches] == [
+            "paralyn_layer_norm_f32", "paralyn_matmul_f32", "paralyn_bias_activation_f32",
+            "paralyn_batched_matmul_f32", "paralyn_softmax_rows_f32", "paralyn_batched_matmul_f32",
+            "paralyn_matmul_f32", "paralyn_bias_activation_f32", "paralyn_add_f32", "paralyn_layer_norm_f32",
+            "paralyn_matmul_f32", "paralyn_bias_activation_f32", "paralyn_matmul_f32",
+            "paralyn_bias_activation_f32", "paralyn_add_f32"]
+        h, r = block.host, block.read
+        eps = np.float32(1e-5)
+        # LayerNorms, bias adds and residual adds: bit for bit on the GPU's own inputs
+        assert r("ln1").tobytes() == oracle.layer_norm(h["x"], h["gamma1"], h["beta1"], eps).tobytes()
+        qkv = r("qkv")
+        check_gemm(r("ln1"), h["w_qkv"], qkv, (0, (0, D, 1)), (0, (0, 3 * D, 1)), 1, TOKENS, 3 * D, D)
+        assert r("qkv_b").tobytes() == oracle.bias_activation(qkv, h["b_qkv"], 0).tobytes()
+        qkv_b = r("qkv_b").ravel()
+        check_gemm(qkv_b, qkv_b, r("scores"), (0, (DH, 3 * D, 1)), (D, (DH, 1, 3 * D)), HEADS, TOKENS, TOKENS, DH)
+        scale = np.float32(1 / np.sqrt(12.0))
+        value, error = oracle.softmax_bound(r("scores"), scale, causal)
+        probs = r("probs")
+        assert np.all(oracle.within(probs, value, error))
+        check_gemm(probs.ravel(), qkv_b, r("attn").reshape(TOKENS, HEADS, DH).transpose(1, 0, 2),
+                   (0, (TOKENS * TOKENS, TOKENS, 1)), (2 * D, (DH, 3 * D, 1)), HEADS, TOKENS, DH, TOKENS)
+        proj = r("proj")
+        check_gemm(r("attn"), h["w_o"], proj, (0, (0, D, 1)), (0, (0, D, 1)), 1, TOKENS, D, D)
+        assert r("proj_b").tobytes() == oracle.bias_activation(proj, h["b_o"], 0).tobytes()
+        assert r("h1").tobytes() == oracle.add(h["x"], r("proj_b")).tobytes()
+        assert r("ln2").tobytes() == oracle.layer_norm(r("h1"), h["gamma2"], h["beta2"], eps).tobytes()
+        ff1 = r("ff1")
+        check_gemm(r("ln2"), h["w_1"], ff1, (0, (0, D, 1)), (0, (0, DFF, 1)), 1, TOKENS, DFF, D)
+        value, error = oracle.gelu_bound((ff1 + h["b_1"][None, :]).astype(np.float32))
+        assert np.all(oracle.within(r("ff1_g"), value, error))
+        ff2 = r("ff2")
+        check_gemm(r("ff1_g"), h["w_2"], ff2, (0, (0, DFF, 1)), (0, (0, D, 1)), 1, TOKENS, D, DFF)
+        assert r("ff2_b").tobytes() == oracle.bias_activation(ff2, h["b_2"], 0).tobytes()
+        assert r("out").tobytes() == oracle.add(r("h1"), r("ff2_b")).tobytes()
+        if causal:  # the first query row attends to itself only
+            assert np.all(probs[:, 0, 1:] == 0.0) and np.all(probs[:, 0, 0] == 1.0)
+    finally:
+        block.close()
+
+
+def _evidence(context, directory):
+    context.write_evidence(str(directory))
+    return (directory / "execution.json").read_text()

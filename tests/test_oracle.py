@@ -234,3 +234,10 @@ def test_batched_matmul_strided_views_follow_the_sequential_order():
     addressed = {1 + z * 40 + i * 10 + j * 2 for z in range(2) for i in range(3) for j in range(4)}
     for idx in range(80):
         assert out[idx] == (0.0 if idx in addressed else 12345.0)
+
+
+def test_gelu_bound_matches_reference():
+    x = GOLDEN["gelu_x"]
+    value, error = oracle.gelu_bound(x)
+    np.testing.assert_allclose(value, GOLDEN["gelu_value"], rtol=1e-13, atol=1e-300)
+    np.testing.assert_allclose(error, GOLDEN["gelu_error"], rtol=1e-12, atol=1e-300)

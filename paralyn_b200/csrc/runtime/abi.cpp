@@ -8,6 +8,7 @@
 // once and not repeated by cleanup (:332-352). An atexit handler drains every
 // context and terminates with status 1 if a failure was never observed (:91-146).
 #include "abi_internal.hpp"
+#include "jit.hpp"
 #include "paralyn/b200.h"
 #include <atomic>
 #include <cstdio>
@@ -246,7 +247,7 @@ std::shared_ptr<ModuleObj> load(const std::shared_ptr<ContextObj> &ctx, const vo
                          "verified IR modules only");
   if (is_provider_artifact(data, n)) {
     for (const auto &b : provider_builtins())
-      module->entries.push_back(Entry{b.name, b.params, &b});
+      module->entries.push_back(Entry{b.name, b.params, &b, nullptr});
     return module;
   }
   std::vector<IrKernel> kernels;
@@ -261,13 +262,15 @@ std::shared_ptr<ModuleObj> load(const std::shared_ptr<ContextObj> &ctx, const vo
     if (k.params.size() > 31)
       fail(PR_UNSUPPORTED, "Kernel exceeds the portable 31-parameter limit");
     const std::string name = match_ir(k);
-    if (name.empty())
-      fail(PR_UNSUPPORTED, "Kernel " + k.name +
-                               ": this build runs only IR it implements natively for sm_100a "
-                               "(elementwise add/affine); it has no run-time compiler");
     Entry entry;
     entry.name = k.name;
-    entry.builtin = find_builtin(name);
+    if (name.empty()) { // no native kernel: compile the IR for sm_100a now
+      entry.jit = compile_ir(k);
+      entry.builtin = &jit_builtin();
+      runtime_event("compilation", "completed", k.name, 0);
+    } else {
+      entry.builtin = find_builtin(name);
+    }
     for (size_t i = 0; i < k.params.size(); ++i)
       entry.params.push_back(Param{k.params[i].name, scalar_of(k.params[i].type),
                                    k.params[i].buffer, ir_access(k, i)});
@@ -311,12 +314,13 @@ std::shared_ptr<ContextObj> context_of(const Object &o) {
 
 pr_event submit_locked(const std::shared_ptr<QueueObj> &queue, const std::string &name,
                        Launcher launcher, Dim3 grid, Dim3 block, std::vector<BoundArg> args,
-                       std::vector<std::shared_ptr<Allocation>> retained) {
+                       std::vector<std::shared_ptr<Allocation>> retained,
+                       std::shared_ptr<const void> entry_data = nullptr) {
   auto event = std::make_shared<EventObj>(queue->owner, nullptr);
   const pr_handle handle = add(event);
   try {
     event->work = queue->owner->engine->submit(name, launcher, grid, block, std::move(args),
-                                               std::move(retained));
+                                               std::move(retained), false, std::move(entry_data));
   } catch (...) {
     objects.erase(handle);
     throw;
@@ -788,7 +792,8 @@ PB_EXPORT pr_status pr_launch(pr_queue q, pr_kernel h, pr_dim3 grid, pr_dim3 blo
               PR_INVALID_ARGUMENT, "Launch block does not match the entry's required block");
     const Dim3 g{grid.x, grid.y, grid.z}, bl{block.x, block.y, block.z};
     queue->owner->engine->check_geometry(g, bl);
-    *out = submit_locked(queue, entry.name, b.launch, g, bl, std::move(bound), std::move(retained));
+    *out = submit_locked(queue, entry.name, b.launch, g, bl, std::move(bound), std::move(retained),
+                         entry.jit);
   });
 }
 

@@ -1,5 +1,6 @@
 // Additive entry points declared in paralyn/b200.h.
 #include "abi_internal.hpp"
+#include "jit.hpp"
 #include "paralyn/b200.h"
 #include <cstring>
 #include <limits>
@@ -164,9 +165,11 @@ PB_EXPORT pr_status pr_b200_module_inspect(const void *data, uint64_t bytes, cha
         fail(PR_COMPILATION_FAILED, std::string("ParalynError: ") + e.what());
       }
       for (const auto &k : kernels) {
-        const std::string name = match_ir(k);
-        if (name.empty())
-          fail(PR_UNSUPPORTED, "Kernel " + k.name + ": no native sm_100a implementation of this IR");
+        std::string name = match_ir(k);
+        if (name.empty()) { // compiled at load time; compiling here reports compiler errors
+          compile_ir(k);
+          name = "nvrtc_sm_100a";
+        }
         text += k.name + "=" + name + ";";
       }
     }

@@ -57,6 +57,7 @@ struct Launch {
   // must make `stream` wait for everything it put on `side_stream`.
   cudaStream_t side_stream = nullptr;
   cudaEvent_t side_events[4] = {};
+  const void *entry_data = nullptr; // per-entry state (run-time compiled kernels)
   bool dry_run = false;        // validate and plan only; enqueue nothing
   uint32_t kernels = 0;        // device kernels enqueued (filled by the launcher)
   std::string variant;         // which implementation ran (filled by the launcher)

@@ -1,4 +1,5 @@
 #include "engine.hpp"
+#include "jit.hpp"
 #include <algorithm>
 #include <atomic>
 #include <chrono>
@@ -476,7 +477,7 @@ void Engine::recycle(Work &work) {
 std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher, Dim3 grid,
                                      Dim3 block, std::vector<BoundArg> args,
                                      std::vector<std::shared_ptr<Allocation>> retained,
-                                     bool barrier) {
+                                     bool barrier, std::shared_ptr<const void> entry_data) {
   std::lock_guard<std::mutex> lock(mutex_);
   healthy();
   DeviceScope scope(device_.ordinal);
@@ -486,7 +487,9 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
   work->block = block;
   work->retained = std::move(retained);
   work->operation_id = next_operation_++;
+  work->entry_owner = std::move(entry_data);
   Launch launch;
+  launch.entry_data = work->entry_owner.get();
   launch.stream = stream_;
   launch.device = device_.ordinal;
   launch.sm_count = device_.sm_count;
@@ -695,7 +698,10 @@ void Engine::finish(const std::shared_ptr<Work> &work) {
         milliseconds = ms;
       // A kernel that gave up a bounded wait reports it through the status word.
       const int status = work->transfer ? 0 : __atomic_exchange_n(status_host_, 0, __ATOMIC_ACQ_REL);
-      if (status != 0 && failure.empty())
+      if (status == status_out_of_view && failure.empty())
+        failure = "Kernel " + work->kernel + " addressed elements outside its bound views; those "
+                  "loads read 0 and those stores were skipped";
+      else if (status != 0 && failure.empty())
         failure = "Kernel " + work->kernel + " abandoned a bounded wait (status " +
                   std::to_string(status) + ")";
     }
@@ -729,6 +735,7 @@ void Engine::finish(const std::shared_ptr<Work> &work) {
   work->failure = failure;
   work->recorded = true;
   work->retained.clear();
+  work->entry_owner.reset();
   runtime_event("completion", failure.empty() ? "completed" : "failed",
                 failure.empty() ? work->kernel : failure, trace_id_, work->operation_id);
 }

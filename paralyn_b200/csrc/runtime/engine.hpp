@@ -61,6 +61,7 @@ struct EventInfo {
 struct Work {
   cudaEvent_t start = nullptr, end = nullptr;
   std::vector<std::shared_ptr<Allocation>> retained;
+  std::shared_ptr<const void> entry_owner; // keeps a run-time compiled kernel loaded
   std::string kernel, variant;
   Dim3 grid, block;
   uint32_t kernels = 0;
@@ -101,7 +102,7 @@ public:
   std::shared_ptr<Work> submit(const std::string &name, Launcher launcher, Dim3 grid, Dim3 block,
                                std::vector<BoundArg> args,
                                std::vector<std::shared_ptr<Allocation>> retained,
-                               bool barrier = false);
+                               bool barrier = false, std::shared_ptr<const void> entry_data = nullptr);
   EventInfo wait(const std::shared_ptr<Work> &work);
   // A host <-> device copy enqueued as a command without blocking the caller. It runs
   // on the copy lane of its direction after every earlier command that touches the

@@ -56,11 +56,13 @@ pr_access ir_access(const IrKernel &kernel, size_t index);
 const std::vector<unsigned char> &provider_artifact();
 bool is_provider_artifact(const void *data, size_t size);
 
+struct JitKernel;
 // One entry of a loaded module, as pr_module_kernel/pr_kernel_parameter see it.
 struct Entry {
   std::string name;
   std::vector<Param> params;
   const Builtin *builtin = nullptr;
+  std::shared_ptr<JitKernel> jit; // set for IR compiled at run time
 };
 
 } // namespace pb

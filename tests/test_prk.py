@@ -92,12 +92,13 @@ def test_commuted_operands_still_match():
     assert inspect(prk.serialize([k])) == {"swapped": "ir.affine.u32"}
 
 
-def test_other_verified_ir_is_unsupported():
+def test_other_verified_ir_is_compiled_at_run_time():
     k = prk.elementwise(
         "array_mul", [("a", prk.F32, True, True), ("b", prk.F32, True, True), ("out", prk.F32, True, False),
                       ("n", prk.U32, False, False)],
         lambda i: prk.binary("*", prk.F32, prk.load("a", i), prk.load("b", i)))
-    assert status_of(prk.serialize([k])) == p.Status.UNSUPPORTED
+    assert status_of(prk.serialize([k])) == p.Status.SUCCESS
+    assert inspect(prk.serialize([k])) == {"array_mul": "nvrtc_sm_100a"}
 
 
 def test_malformed_containers_fail_compilation():

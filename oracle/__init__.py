@@ -63,7 +63,7 @@ def lib():
             "orc_batched_matmul_f32": (None, [_f32p, _View, _f32p, _View, _f32p, _View, _size, _size, _size,
                                               _size]),
             "orc_batched_dot_bound": (None, [_f32p, _View, _f32p, _View, _size, _size, _size, _size, _f64p,
-                                             _f64p]),
+                                             _f64p, _f64p]),
             "orc_gelu_bound": (None, [_f32p, _size, _f64p, _f64p]),
         }
         for name, (restype, argtypes) in sig.items():
@@ -201,14 +201,16 @@ def batched_matmul(a, a_view, b, b_view, c, c_view, batch, m, n, k):
     return c
 
 
-def batched_dot_bound(a, a_view, b, b_view, batch, m, n, k):
-    """(value, error) float64 [batch, m, n] for the same products."""
+def batched_dot_bound(a, a_view, b, b_view, batch, m, n, k, magnitude=False):
+    """(value, error) float64 [batch, m, n] for the same products; with magnitude=True
+    also sum |a*b| per output (for the FP32 GEMM contract 2*k*2^-24*sum|a||b|)."""
     a, b = _f32(a), _f32(b)
     value = np.empty((batch, m, n), np.float64)
     error = np.empty((batch, m, n), np.float64)
+    mag = np.empty((batch, m, n), np.float64)
     va, vb = (_View(off, *strides) for off, strides in (a_view, b_view))
-    lib().orc_batched_dot_bound(a, va, b, vb, batch, m, n, k, value, error)
-    return value, error
+    lib().orc_batched_dot_bound(a, va, b, vb, batch, m, n, k, value, error, mag)
+    return (value, error, mag) if magnitude else (value, error)
 
 
 def gelu_bound(x):

@@ -446,9 +446,9 @@ void orc_batched_matmul_f32(const float *a, orc_view av, const float *b, orc_vie
       }
 }
 
-/* value/error per output, in [batch][m][n] order. */
+/* value/error per output, in [batch][m][n] order; magnitude (sum |a*b|) when not NULL. */
 void orc_batched_dot_bound(const float *a, orc_view av, const float *b, orc_view bv, size_t batch,
-                           size_t m, size_t n, size_t k, double *value, double *error) {
+                           size_t m, size_t n, size_t k, double *value, double *error, double *magnitude_out) {
   for (size_t z = 0; z < batch; ++z)
     for (size_t i = 0; i < m; ++i)
       for (size_t j = 0; j < n; ++j) {
@@ -462,6 +462,8 @@ void orc_batched_dot_bound(const float *a, orc_view av, const float *b, orc_view
         const size_t o = (z * m + i) * n + j;
         value[o] = v;
         error[o] = gamma_n((double)k) * magnitude + (double)k * ORC_TINY;
+        if (magnitude_out)
+          magnitude_out[o] = magnitude;
       }
 }
 

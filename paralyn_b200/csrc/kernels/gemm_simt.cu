@@ -261,6 +261,9 @@ bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
 
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n,
                         int64_t k, int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb);
+bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
+                           int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
+                           int64_t ldc, int64_t sc);
 
 // (a, b, c, m, n, k, transpose_a, transpose_b) with a 16x16 block per 16x16 output
 // tile: the grid bounds the computed region to min(m, 16*grid.y) x min(n, 16*grid.x).
@@ -341,8 +344,9 @@ bool as_matrix(int64_t rows, int64_t cols, int64_t row_stride, int64_t col_strid
 //  c_col), grid (ceil(n/16), ceil(m/16), batch): C[z] = A[z] B[z] over element-strided
 // views, each output one accumulator over increasing k (reference
 // runtime/tensor.cpp:130-166). Operands whose strides make them row-major or
-// transposed matrices run on the tiled SIMT kernel with a batch grid dimension;
-// other layouts on a one-output-per-thread kernel.
+// transposed matrices run on the 3xTF32 tensor-core kernel (AUTO or TF32X3 mode, when
+// C's columns are contiguous and the shape is large enough) or on the tiled SIMT
+// kernel with a batch grid dimension; other layouts on a one-output-per-thread kernel.
 void launch_provider_batched_matmul(Launch &L) {
   const auto &A = L.args;
   const int64_t m = std::min<int64_t>(A[3].u32(), int64_t(L.grid.y) * 16);
@@ -392,6 +396,9 @@ void launch_provider_batched_matmul(Launch &L) {
     g.vec_a = aligned16(a) && g.lda % 4 == 0 && g.sa % 4 == 0;
     g.vec_b = aligned16(b) && g.ldb % 4 == 0 && g.sb % 4 == 0;
     g.vec_c = aligned16(c) && g.ldc % 4 == 0 && g.sc % 4 == 0 && g.c_col == 1;
+    if ((L.matmul_mode == matmul_auto || L.matmul_mode == matmul_tf32x3) && g.c_col == 1 &&
+        launch_tf32x3_batched(L, a, b, c, int64_t(batch), m, n, k, g.lda, ta, g.sa, g.ldb, tb, g.sb, g.ldc, g.sc))
+      return;
     if (reference)
       dispatch<matmul_reference>(g, ta, tb, L.stream, uint32_t(batch));
     else

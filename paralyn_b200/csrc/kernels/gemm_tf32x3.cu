@@ -134,10 +134,16 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 // hi/lo split of op(X) into [rows_pad][k_pad] (K contiguous), zero padded.
 // Element (r, k) of op(X) is x[r*ld + k], or x[k*ld + r] when `transposed`.
+// Batched (grid.z > 1): matrix z starts x_batch elements after matrix z-1 and is
+// written rows_pad rows after it.
 __global__ void __launch_bounds__(256) split_tf32(const float *__restrict__ x, int64_t ld, int transposed,
                                                   int64_t rows, int64_t k, float *__restrict__ hi,
-                                                  float *__restrict__ lo, int64_t k_pad) {
+                                                  float *__restrict__ lo, int64_t k_pad, int64_t x_batch,
+                                                  int64_t rows_pad) {
   __shared__ float tile[32][33];
+  x += int64_t(blockIdx.z) * x_batch;
+  hi += int64_t(blockIdx.z) * rows_pad * k_pad;
+  lo += int64_t(blockIdx.z) * rows_pad * k_pad;
   const int64_t r0 = int64_t(blockIdx.y) * 32, k0 = int64_t(blockIdx.x) * 32;
   const int tx = threadIdx.x % 32, ty = threadIdx.x / 32; // 32 x 8
 #pragma unroll
@@ -169,6 +175,11 @@ struct TileArgs {
   int64_t m, n, ldc;
   int k_blocks, tiles_m, tiles_n;
   int *status;
+  // Batched launches: tiles_m * tiles_n CTAs per matrix; matrix z reads the split
+  // rows z*a_rows.. of A and z*b_rows.. of B (0: shared by all) and writes C at
+  // c + z*c_batch. Zero tiles_per_batch means one matrix.
+  int tiles_per_batch = 0, a_rows = 0, b_rows = 0;
+  int64_t c_batch = 0;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -186,13 +197,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
+  const int z = blockIdx.x / per_batch;
   // Grouped raster: 8 tile-rows at a time so consecutive CTAs share B tiles in L2.
-  const int id = blockIdx.x, group = 8, per_group = group * args.tiles_n;
+  const int id = blockIdx.x % per_batch, group = 8, per_group = group * args.tiles_n;
   const int first_m = (id / per_group) * group;
   const int rows_in_group = min(group, args.tiles_m - first_m);
   const int tm = first_m + (id % per_group) % rows_in_group;
   const int tn = (id % per_group) / rows_in_group;
   const int m0 = tm * TM, n0 = tn * TN;
+  const int a_y = z * args.a_rows + m0, b_y = z * args.b_rows + n0; // rows of the split operands
+  float *const c_base = args.c + int64_t(z) * args.c_batch;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -231,10 +246,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         uint8_t *stage = smem + s * STAGE_BYTES;
         mbar_expect_tx(&full[s], STAGE_BYTES);
-        tma_load_2d(stage, &a_hi, &full[s], kb * TK, m0);
-        tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, m0);
-        tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, n0);
-        tma_load_2d(stage + 2 * A_BYTES + B_BYTES, &b_lo, &full[s], kb * TK, n0);
+        tma_load_2d(stage, &a_hi, &full[s], kb * TK, a_y);
+        tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, a_y);
+        tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, b_y);
+        tma_load_2d(stage + 2 * A_BYTES + B_BYTES, &b_lo, &full[s], kb * TK, b_y);
         *issued = kb + 1;
       }
     }
@@ -281,8 +296,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (!*abort_flag) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int64_t row = int64_t(m0) + 32 * sub + lane;
-      float *crow = args.c + row * args.ldc;
-      const bool vec = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 15u) == 0);
+      float *crow = c_base + row * args.ldc;
+      const bool vec = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
       for (int col = 0; col < TN; col += 32) {
         float v[32];
@@ -392,13 +407,70 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   }
   // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi,
-                                                                                    alo, k_pad);
+                                                                                    alo, k_pad, 0, m_pad);
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi,
-                                                                                    blo, k_pad);
+                                                                                    blo, k_pad, 0, n_pad);
   TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
   gemm_tf32x3<<<uint32_t(tiles_m * tiles_n), THREADS, SMEM_BYTES, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
   L.kernels = 3;
   L.variant = "tcgen05_tf32x3";
+  return true;
+}
+
+// Batched form: C[z] = op(A[z]) op(B[z]) for z < batch, matrix z of A at a + z*sa,
+// of B at b + z*sb (sb = 0: one B shared by all), of C at c + z*sc (row stride
+// ldc, column stride 1). Same split and GEMM kernels with a batch grid dimension
+// (split) and batch-major CTA numbering (GEMM); the split operands of all
+// matrices are stacked row-wise, so no tile crosses a matrix boundary.
+bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
+                           int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
+                           int64_t ldc, int64_t sc) {
+  if (k < 16 || m < 1 || n < 1 || batch < 1 || batch > 65535)
+    return false;
+  if (L.matmul_mode == matmul_auto && (k < 64 || m * n * batch < 128 * 256 * 4))
+    return false;
+  if (!encoder() || !L.workspace)
+    return false;
+  const int64_t k_pad = round_up(k, 32), m_pad = round_up(m, TM), n_pad = round_up(n, TN);
+  const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / TN, batch_b = sb ? batch : 1;
+  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 ||
+      n_pad / 32 > 65535 || batch * m_pad > INT32_MAX || batch_b * n_pad > INT32_MAX)
+    return false; // grid limits and 32-bit TMA row coordinates
+  const size_t bytes = size_t(8) * size_t(k_pad) * size_t(batch * m_pad + batch_b * n_pad);
+  if (L.dry_run)
+    return true;
+  auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
+  if (!scratch)
+    return false;
+  float *ahi = scratch, *alo = ahi + batch * m_pad * k_pad, *bhi = alo + batch * m_pad * k_pad,
+        *blo = bhi + batch_b * n_pad * k_pad;
+  CUtensorMap maps[4];
+  if (!make_map(&maps[0], ahi, batch * m_pad, k_pad, TM) || !make_map(&maps[1], alo, batch * m_pad, k_pad, TM) ||
+      !make_map(&maps[2], bhi, batch_b * n_pad, k_pad, TN) || !make_map(&maps[3], blo, batch_b * n_pad, k_pad, TN))
+    return false;
+  static bool configured[64] = {};
+  if (L.device < 0 || L.device >= 64)
+    return false;
+  if (!configured[L.device]) {
+    if (cudaFuncSetAttribute(gemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    configured[L.device] = true;
+  }
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
+      a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, m_pad);
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
+      b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, n_pad);
+  TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
+  t.tiles_per_batch = int(tiles_m * tiles_n);
+  t.a_rows = int(m_pad);
+  t.b_rows = sb ? int(n_pad) : 0;
+  t.c_batch = sc;
+  gemm_tf32x3<<<uint32_t(tiles_m * tiles_n * batch), THREADS, SMEM_BYTES, L.stream>>>(maps[0], maps[1], maps[2],
+                                                                                      maps[3], t);
+  L.kernels = 3;
+  L.variant = "batched_tcgen05_tf32x3";
   return true;
 }
 
@@ -496,9 +568,11 @@ PB_EXPORT pr_status pr_b200_matmul_tf32x3_static_f32(const float *a, const float
   // The split writes every element of the four operand blocks the GEMM reads
   // (padding included), so the previous call's contents are never read.
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, s>>>(a, int64_t(lda), transpose_a ? 1 : 0,
-                                                                              int64_t(m), int64_t(k), ahi, alo, k_pad);
+                                                                              int64_t(m), int64_t(k), ahi, alo, k_pad,
+                                                                              0, m_pad);
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, s>>>(b, int64_t(ldb), transpose_b ? 0 : 1,
-                                                                              int64_t(n), int64_t(k), bhi, blo, k_pad);
+                                                                              int64_t(n), int64_t(k), bhi, blo, k_pad,
+                                                                              0, n_pad);
   TileArgs t{c, int64_t(m), int64_t(n), int64_t(ldc), int(k_pad / TK), int(m_pad / TM), int(n_pad / TN),
              status ? status : static_status_ptr[device]};
   gemm_tf32x3<<<uint32_t((m_pad / TM) * (n_pad / TN)), THREADS, SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], maps[3], t);

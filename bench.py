@@ -12,6 +12,10 @@ benchmark configurations; one "step" is one pass of the path over one batch):
   layernorm  X[16384 x 4096] ~ N(0,1), gamma ~ N(1,.02), beta ~ N(0,.02), seed 2; rows sharded
   affine     y = 1.5 x - 0.25, n = 2^26, x ~ U[-4,4), seed 1 (replica per rank)
   add        c = a + b, n = 2^20, a, b ~ U[-1,1), seed 0 (replica per rank, 16 rotating sets)
+  softmax    causal row softmax of x [32, 1024, 1024] ~ U[-8,8), scale 1/8, seed 5 (replica per rank)
+  reduce     row sums of x [65536 x 1024] ~ U[-4,4), seed 6 (replica per rank)
+  attention  batched Q K^T: Q, K [32 heads, 2048, 128] ~ U[-1,1), seed 7, K^T as a strided view
+             (replica per rank)
 `value` is device time (CUDA events on the library's context stream between two
 queue markers, max over ranks); `e2e` times the same steps through the public API
 with pinned host inputs copied in and results copied out every step. Under
@@ -41,7 +45,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="chain", choices=("chain", "gemm", "layernorm", "affine", "add"))
+    ap.add_argument("--workload", default="chain",
+                    choices=("chain", "gemm", "layernorm", "affine", "add", "softmax", "reduce", "attention"))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -52,7 +57,16 @@ def parse():
 
 # Sized so the timed region lasts about a second (the clock sampler needs several
 # 200 ms samples inside it).
-DEFAULT_STEPS = {"chain": 100, "gemm": 1500, "layernorm": 8000, "affine": 8000, "add": 20000}
+DEFAULT_STEPS = {"chain": 100, "gemm": 1500, "layernorm": 8000, "affine": 8000, "add": 20000, "softmax": 20000,
+                 "reduce": 20000, "attention": 5000}
+METRICS = {"chain": "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)",
+           "gemm": "FP32 GEMM TFLOP/s (4096^3, rows sharded)",
+           "layernorm": "FP32 row LayerNorm HBM GB/s (16384x4096, rows sharded)",
+           "affine": "FP32 affine y = 1.5x - 0.25 HBM GB/s (n = 2^26)",
+           "add": "FP32 vector add HBM GB/s (n = 2^20)",
+           "softmax": "FP32 causal row softmax HBM GB/s ([32, 1024, 1024])",
+           "reduce": "FP32 row sum HBM GB/s (65536 x 1024)",
+           "attention": "FP32 batched matmul TFLOP/s (32 x 2048x2048x128, Q K^T)"}
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -272,6 +286,49 @@ class Workload:
                            "l2": "16 rotating buffer sets (192 MiB) exceed L2"}
             self.h2d, self.d2h = 8 * self.count, 4 * self.count
             self.turn = 0
+        elif name in ("softmax", "reduce"):
+            D = self.T.TensorDescriptor
+            if name == "softmax":
+                self.shape = (32, 1024, 1024)
+                count = 32 * 1024 * 1024
+                self.units_local = 8 * count
+                self.config = {"workload": "softmax: causal row softmax of x [32, 1024, 1024] ~ U[-8,8), scale 1/8, "
+                                           "seed 5", "parallelism": f"replica{world}", "l2": "inputs larger than L2 (128 MiB)"}
+                self.h2d = self.d2h = 4 * count
+            else:
+                self.shape = (65536, 1024)
+                count = 65536 * 1024
+                self.units_local = 4 * count + 4 * 65536
+                self.config = {"workload": "reduce: row sums of x [65536 x 1024] ~ U[-4,4), seed 6",
+                               "parallelism": f"replica{world}", "l2": "inputs larger than L2 (256 MiB)"}
+                self.h2d, self.d2h = 4 * count, 4 * 65536
+            self.x = ctx.buffer(4 * count)
+            self.y = ctx.buffer(self.d2h)
+            e = b200.fill_synthetic_into(self.queue, D(self.x, (count,)), seed=5 if name == "softmax" else 6,
+                                         p0=8.0 if name == "softmax" else 4.0)
+            e.wait()
+            e.close()
+            self.units_total = self.units_local * world
+            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
+            self.metric = METRICS[name]
+        elif name == "attention":
+            D = self.T.TensorDescriptor
+            self.heads, self.seq, self.dh = 32, 2048, 128
+            count = self.heads * self.seq * self.dh
+            self.q, self.kmat = ctx.buffer(4 * count), ctx.buffer(4 * count)
+            self.c = ctx.buffer(4 * self.heads * self.seq * self.seq)
+            for buf, first in ((self.q, 0), (self.kmat, count)):
+                e = b200.fill_synthetic_into(self.queue, D(buf, (count,)), seed=7, first_draw=first)
+                e.wait()
+                e.close()
+            self.units_local = 2 * self.heads * self.seq * self.seq * self.dh
+            self.units_total = self.units_local * world
+            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "weak"
+            self.metric = METRICS[name]
+            self.config = {"workload": "attention: S = Q K^T per head, Q, K [32, 2048, 128] ~ U[-1,1), seed 7; "
+                                       "K^T is a strided view (no copy)", "batch": 32, "m": 2048, "n": 2048, "k": 128,
+                           "parallelism": f"replica{world}", "l2": "output 512 MiB exceeds L2"}
+            self.h2d, self.d2h = 8 * count, 4 * self.heads * self.seq * self.seq
         self.ctx.synchronize()
 
     def step(self):
@@ -294,6 +351,22 @@ class Workload:
         if self.name == "affine":
             e = self.queue.launch(self.kernel, [self.xv, self.yv, p.u32(self.count), p.f32(1.5), p.f32(-0.25)],
                                   grid=((self.count + 255) // 256, 1, 1), block=(256, 1, 1))
+            return [e], e
+        if self.name in ("softmax", "reduce"):
+            D = self.T.TensorDescriptor
+            if self.name == "softmax":
+                e = self.T.softmax_rows_into(self.queue, self.res.module, D(self.x, self.shape), D(self.y, self.shape),
+                                             scale=0.125, causal=True)
+            else:
+                e = self.T.reduce_rows_into(self.queue, self.res.module, D(self.x, self.shape),
+                                            D(self.y, (self.shape[0],)))
+            return [e], e
+        if self.name == "attention":
+            D = self.T.TensorDescriptor
+            H, S, K = self.heads, self.seq, self.dh
+            e = self.T.batched_matmul_into(self.queue, self.res.module, D(self.q, (H, S, K)),
+                                           D(self.kmat, (H, K, S), 0, (S * K, 1, K)), D(self.c, (H, S, S)),
+                                           batch=H, m=S, n=S, k=K)
             return [e], e
         a, b, c, av, bv, cv = self.bufs[self.turn % self.sets]
         self.turn += 1
@@ -334,6 +407,13 @@ class Workload:
                                                          D(self.y, (n_rows, self.cols), oo), epsilon=1e-5))
                 events.append(b200.read_async(self.queue, dst, host_out + oo, offset=oo, nbytes=4 * n_rows * width_out))
             return events
+        if self.name in ("softmax", "reduce", "attention"):  # one slice: upload, step, download
+            ins, (out, out_bytes) = self.io_buffers()
+            for (buf, nbytes), host in zip(ins, host_in):
+                events.append(b200.write_async(self.queue, buf, host, nbytes=nbytes))
+            events += self.step()[0]
+            events.append(b200.read_async(self.queue, out, host_out, nbytes=out_bytes))
+            return events
         if self.name == "affine":
             ins, out = [self.x], self.y
         else:
@@ -363,6 +443,10 @@ class Workload:
             return [(self.x, self.h2d)], (self.y, self.d2h)
         if self.name == "affine":
             return [(self.x, self.h2d)], (self.y, self.d2h)
+        if self.name in ("softmax", "reduce"):
+            return [(self.x, self.h2d)], (self.y, self.d2h)
+        if self.name == "attention":
+            return [(self.q, self.h2d // 2), (self.kmat, self.h2d // 2)], (self.c, self.d2h)
         a, b, c = self.bufs[0][:3]
         return [(a, 4 * self.count), (b, 4 * self.count)], (c, self.d2h)
 
@@ -425,7 +509,9 @@ def run_ours(args, group):
 
 
 DOMINANT_ENTRY = {"chain": "paralyn_matmul_f32", "gemm": "paralyn_matmul_f32",
-                  "layernorm": "paralyn_layer_norm_f32", "affine": "array_affine_scalar", "add": "array_add"}
+                  "layernorm": "paralyn_layer_norm_f32", "affine": "array_affine_scalar", "add": "array_add",
+                  "softmax": "paralyn_softmax_rows_f32", "reduce": "paralyn_reduce_rows_f32",
+                  "attention": "paralyn_batched_matmul_f32"}
 
 
 def last_variant(ctx, workload):
@@ -513,13 +599,14 @@ def roofline_for(w, seconds, variant, region_seconds):
     shorter ones with the burst figure."""
     peaks, basis = measured_peaks()
     traffic = load_traffic().get(w.name)
-    if w.name in ("layernorm", "affine", "add"):
+    if w.name in ("layernorm", "affine", "add", "softmax", "reduce"):
         per_launch = w.units_local
         achieved = per_launch / seconds / 1e9
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                 "peak_basis": f"{basis} STREAM-style copy"}
-    flops = 2 * (w.chain.local_rows if w.name == "chain" else w.m_local) * w.n * w.k
+    flops = w.units_local if w.name == "attention" else 2 * (
+        w.chain.local_rows if w.name == "chain" else w.m_local) * w.n * w.k
     achieved = flops / seconds / 1e12
     if variant and "tf32x3" in variant:
         sustained = region_seconds >= 0.5 and "bf16_tflops_sustained" in peaks
@@ -583,6 +670,33 @@ def cpu_sample(workload, budget_seconds):
             reps += 1
         t = time.perf_counter() - t0
         return reps * (2 * rows * cols * 4 + 2 * cols * 4) / t * 1e-9, "GB/s", f"{reps} x 4096 rows x 4096"
+    if workload in ("softmax", "reduce"):
+        shape = (8, 1024, 1024) if workload == "softmax" else (16384, 1024)
+        x = synthetic.uniform(5, 0, int(np.prod(shape)), 8.0).reshape(shape)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < budget_seconds or reps == 0:
+            if workload == "softmax":
+                oracle.softmax_rows(x, np.float32(0.125), causal=True)
+            else:
+                oracle.reduce_rows(x, 0, threaded=True)
+            reps += 1
+        t = time.perf_counter() - t0
+        per = 8 * x.size if workload == "softmax" else 4 * x.size + 4 * shape[0]
+        return reps * per / t * 1e-9, "GB/s", f"{reps} passes over x {list(shape)}"
+    if workload == "attention":
+        S, K = 2048, 128
+        q, kk = synthetic.uniform(7, 0, S * K), synthetic.uniform(7, 1, S * K)
+        rows = max(8, oracle.threads())
+        while True:  # grow the sample (at most one head's 2048 query rows) to about a quarter of the budget
+            c = np.zeros(rows * S, np.float32)
+            t0 = time.perf_counter()
+            oracle.batched_matmul_threaded(q, (0, (0, K, 1)), kk, (0, (0, 1, K)), c, (0, (0, S, 1)), 1, rows, S, K)
+            t = time.perf_counter() - t0
+            if t >= budget_seconds / 4 or rows == S:
+                break
+            rows = min(S, rows * 2)
+        return 2 * rows * S * K / t * 1e-12, "TFLOP/s", f"{rows} query rows of one head x 2048 keys x 128"
     count = 1 << 26 if workload == "affine" else 1 << 20
     x = synthetic.uniform(1, 0, count, 4.0)
     y = synthetic.uniform(0, count, count)
@@ -621,12 +735,7 @@ def run_reference(args, group):
         v, unit, sample = cpu_sample(args.workload, budget)
         values.append(v)
     value = sorted(values)[len(values) // 2]
-    names = {"chain": "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)",
-             "gemm": "FP32 GEMM TFLOP/s (4096^3, rows sharded)",
-             "layernorm": "FP32 row LayerNorm HBM GB/s (16384x4096, rows sharded)",
-             "affine": "FP32 affine y = 1.5x - 0.25 HBM GB/s (n = 2^26)",
-             "add": "FP32 vector add HBM GB/s (n = 2^20)"}
-    return {"impl": "reference", "metric": names[args.workload], "value": round(value, 4), "unit": unit,
+    return {"impl": "reference", "metric": METRICS[args.workload], "value": round(value, 4), "unit": unit,
             "n_gpus": group.world, "steps": steps, "warmup": args.warmup, "higher_is_better": True,
             "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload, "sample": sample},
             "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",

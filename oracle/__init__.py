@@ -65,6 +65,10 @@ def lib():
             "orc_batched_dot_bound": (None, [_f32p, _View, _f32p, _View, _size, _size, _size, _size, _f64p,
                                              _f64p, _f64p]),
             "orc_gelu_bound": (None, [_f32p, _size, _f64p, _f64p]),
+            "orc_softmax_rows_f32_mt": (None, [_f32p, _f32p, _size, _size, _size, _c.c_int, _c.c_float]),
+            "orc_reduce_rows_f32_mt": (None, [_f32p, _f32p, _size, _size, _c.c_int]),
+            "orc_batched_matmul_f32_mt": (None, [_f32p, _View, _f32p, _View, _f32p, _View, _size, _size, _size,
+                                                 _size]),
         }
         for name, (restype, argtypes) in sig.items():
             f = getattr(_lib, name)
@@ -164,12 +168,23 @@ def bias_activation(x, bias, activation):
     return out
 
 
-def reduce_rows(x, op):
+def reduce_rows(x, op, threaded=False):
     """Row sums (op 0) or maxima (op 1) of x [rows, columns] in the reference's fixed order."""
     x = _f32(x)
     rows, columns = x.shape
     out = np.empty(rows, np.float32)
-    lib().orc_reduce_rows_f32(x, out, rows, columns, int(op))
+    (lib().orc_reduce_rows_f32_mt if threaded else lib().orc_reduce_rows_f32)(x, out, rows, columns, int(op))
+    return out
+
+
+def softmax_rows(x, scale, causal=False):
+    """FP32 row softmax in the reference's order with the C library's expf (all threads;
+    a timing baseline: parity checks use softmax_bound)."""
+    x = _f32(x)
+    rows, columns = x.shape[-2], x.shape[-1]
+    out = np.empty_like(x)
+    lib().orc_softmax_rows_f32_mt(x, out, int(np.prod(x.shape[:-1])), rows, columns, int(bool(causal)),
+                                  float(scale))
     return out
 
 
@@ -198,6 +213,14 @@ def batched_matmul(a, a_view, b, b_view, c, c_view, batch, m, n, k):
     assert c.dtype == np.float32 and c.flags.c_contiguous
     views = [_View(off, *strides) for off, strides in (a_view, b_view, c_view)]
     lib().orc_batched_matmul_f32(a, views[0], b, views[1], c, views[2], batch, m, n, k)
+    return c
+
+
+def batched_matmul_threaded(a, a_view, b, b_view, c, c_view, batch, m, n, k):
+    """batched_matmul over all host threads (same per-element order)."""
+    a, b = _f32(a), _f32(b)
+    views = [_View(off, *strides) for off, strides in (a_view, b_view, c_view)]
+    lib().orc_batched_matmul_f32_mt(a, views[0], b, views[1], c, views[2], batch, m, n, k)
     return c
 
 

@@ -27,6 +27,8 @@
  *                          +0.0 / max from -inf, then the 256-lane tree; the max
  *                          rule of :184-191); emulation as in
  *                          examples/native/transformer_reference.hpp:165-191
+ *   orc_softmax_rows_f32   runtime/tensor.cpp:248-272 in FP32 with the C library's
+ *                          expf (a timing baseline; checks use the bound below)
  *   orc_softmax_bound      float64 running bound of softmax_row,
  *                          examples/native/transformer_reference.hpp:70-73, :122-132
  *                          (exp budgeted at 4 ulp, division at 2.5 ulp)
@@ -490,4 +492,61 @@ void orc_gelu_bound(const float *x, size_t n, double *value, double *error) {
     value[i] = y.v;
     error[i] = y.e;
   }
+}
+
+static float tree_sum_of(float *p) { return tree_sum_256(p); }
+
+static void softmax_row(const float *x, float *out, size_t columns, size_t visible, float scale) {
+  float p[ORC_LANES];
+  for (unsigned t = 0; t < ORC_LANES; ++t) {
+    float m = -INFINITY;
+    for (size_t j = t; j < visible; j += ORC_LANES)
+      m = max2(m, scale * x[j]);
+    p[t] = m;
+  }
+  for (unsigned w = ORC_LANES / 2; w > 0; w >>= 1)
+    for (unsigned t = 0; t < w; ++t)
+      p[t] = max2(p[t], p[t + w]);
+  const float m = p[0];
+  for (unsigned t = 0; t < ORC_LANES; ++t) {
+    float s = 0.0f;
+    for (size_t j = t; j < visible; j += ORC_LANES)
+      s = s + expf(scale * x[j] - m);
+    p[t] = s;
+  }
+  const float s = tree_sum_of(p);
+  for (size_t j = 0; j < columns; ++j)
+    out[j] = j < visible ? expf(scale * x[j] - m) / s : 0.0f;
+}
+
+void orc_softmax_rows_f32_mt(const float *x, float *out, size_t all_rows, size_t rows, size_t columns,
+                             int causal, float scale) {
+#pragma omp parallel for schedule(static)
+  for (long long r = 0; r < (long long)all_rows; ++r) {
+    const size_t visible = causal ? ((size_t)r % rows) + (columns - rows) + 1 : columns;
+    softmax_row(x + (size_t)r * columns, out + (size_t)r * columns, columns, visible, scale);
+  }
+}
+
+void orc_reduce_rows_f32_mt(const float *x, float *out, size_t rows, size_t columns, int op) {
+#pragma omp parallel for schedule(static)
+  for (long long r = 0; r < (long long)rows; ++r)
+    out[r] = op == 1 ? tree_max_f32(x + (size_t)r * columns, columns)
+                     : orc_tree_sum_f32(x + (size_t)r * columns, columns);
+}
+
+void orc_batched_matmul_f32_mt(const float *a, orc_view av, const float *b, orc_view bv, float *c, orc_view cv,
+                               size_t batch, size_t m, size_t n, size_t k) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (long long z = 0; z < (long long)batch; ++z)
+    for (long long i = 0; i < (long long)m; ++i)
+      for (size_t j = 0; j < n; ++j) {
+        float sum = 0.0f;
+        for (size_t p = 0; p < k; ++p) {
+          const float product = a[av.offset + z * av.s0 + i * av.s1 + p * av.s2] *
+                                b[bv.offset + z * bv.s0 + p * bv.s1 + j * bv.s2];
+          sum = sum + product;
+        }
+        c[cv.offset + z * cv.s0 + i * cv.s1 + j * cv.s2] = sum;
+      }
 }

@@ -10,10 +10,11 @@
 // enter neither m nor s. Row r of a batch of `rows` rows sees
 // r % rows + (columns - rows) + 1 leading columns when causal.
 //
-// Sums, maxima and the division round exactly as the reference's (__fadd_rn,
-// __fmul_rn, __fsub_rn, __fdiv_rn), so reductions are bit-identical to the
-// reference order; exp is CUDA's expf (full-range error within 2 ulp), inside the
-// reference's own 4-ulp budget for exp.
+// Sums and maxima round exactly as the reference's (__fadd_rn, __fmul_rn,
+// __fsub_rn), so reductions are bit-identical to the reference order. exp is
+// CUDA's expf (full-range error within 2 ulp), inside the reference's 4-ulp budget
+// for exp; e / s is e times the correctly rounded reciprocal of s (two roundings,
+// within about 1 ulp), inside its 2.5-ulp budget for the division.
 //
 // Fast paths (16-byte aligned rows, columns % 4 == 0) use the lane mapping of the
 // LayerNorm kernels: one warp per row, thread L holds the reference lanes
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(256) softmax_warp_rows(const float *__restrict
           v[i][h][c] = expf(__fsub_rn(v[i][h][c], m));
           s[4 * h + c] = __fadd_rn(s[4 * h + c], v[i][h][c]);
         }
-  const float sum = warp_tree<Sum>(s);
+  const float rinv = __frcp_rn(warp_tree<Sum>(s));
 #pragma unroll
   for (int i = 0; i < R; ++i)
 #pragma unroll
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(256) softmax_warp_rows(const float *__restrict
         float y[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          y[c] = col + c < visible ? __fdiv_rn(v[i][h][c], sum) : 0.0f;
+          y[c] = col + c < visible ? __fmul_rn(v[i][h][c], rinv) : 0.0f;
         __stcs(reinterpret_cast<float4 *>(yr + col), make_float4(y[0], y[1], y[2], y[3]));
       }
     }
@@ -249,9 +250,9 @@ __global__ void __launch_bounds__(256) softmax_block_rows(const float *x, float 
   float s = 0.0f;
   for (uint32_t j = threadIdx.x; j < visible; j += 256)
     s = __fadd_rn(s, expf(__fsub_rn(__fmul_rn(scale, xr[j]), m)));
-  s = block_tree<Sum>(s, scratch);
+  const float rinv = __frcp_rn(block_tree<Sum>(s, scratch));
   for (uint32_t j = threadIdx.x; j < columns; j += 256)
-    yr[j] = j < visible ? __fdiv_rn(expf(__fsub_rn(__fmul_rn(scale, xr[j]), m)), s) : 0.0f;
+    yr[j] = j < visible ? __fmul_rn(expf(__fsub_rn(__fmul_rn(scale, xr[j]), m)), rinv) : 0.0f;
 }
 
 bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }

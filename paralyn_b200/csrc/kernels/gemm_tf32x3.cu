@@ -180,6 +180,7 @@ struct TileArgs {
   // c + z*c_batch. Zero tiles_per_batch means one matrix.
   int tiles_per_batch = 0, a_rows = 0, b_rows = 0;
   int64_t c_batch = 0;
+  int tiles_total = 0; // persistent kernel: tiles of all matrices
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -333,6 +334,213 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+
+// Persistent form: one CTA per SM walks the tiles blockIdx.x, + gridDim.x, ...
+// The shared-memory ring runs continuously across tiles (one k-slice counter
+// for producer and MMA), and the accumulator is double-buffered in TMEM (2 x 256
+// of the 512 columns): the MMA thread computes tile j into buffer j % 2 while
+// the epilogue warps drain tile j - 1 from the other buffer, so stores of C
+// overlap the tensor-core work instead of following it.
+//   tmem_full[b]  MMA -> epilogue: all MMAs of the buffer's current tile are done
+//                 (tcgen05.commit); phase u = the u-th tile that used buffer b
+//   tmem_empty[b] epilogue -> MMA: the four epilogue warps have read buffer b
+//                 (one elected lane per warp arrives; count 4)
+// Every wait is bounded as in the one-tile kernel; before TMEM is freed the MMA
+// thread's final commit guarantees no MMA is still writing it.
+// Epilogue stores are coalesced: each warp passes its 32x32 accumulator chunk
+// (thread = row) through a padded shared-memory tile and writes it back one row
+// per instruction (thread = column), 128 contiguous bytes per store.
+constexpr int EPI_TILE_FLOATS = 32 * 33;
+constexpr int SMEM_BYTES_PERSISTENT = SMEM_BYTES + 4 * EPI_TILE_FLOATS * 4;
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                           const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                           const TileArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tmem_full = empty + STAGES;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint64_t *drained = tmem_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *issued = abort_flag + 1;   // k-slices the producer has requested
+  volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received
+  float *epi_tiles = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + 256);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
+  auto locate = [&](int tile, int &a_y, int &b_y, int &m0, int &n0, int &z) {
+    z = tile / per_batch;
+    const int id = tile % per_batch, group = 8, per_group = group * args.tiles_n;
+    const int first_m = (id / per_group) * group;
+    const int rows_in_group = min(group, args.tiles_m - first_m);
+    m0 = (first_m + (id % per_group) % rows_in_group) * TM;
+    n0 = ((id % per_group) / rows_in_group) * TN;
+    a_y = z * args.a_rows + m0;
+    b_y = z * args.b_rows + n0;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 4);
+    }
+    mbar_init(drained, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * TMEM_COLUMNS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) { // TMA producer
+      int g = 0;
+      for (int tile = blockIdx.x; tile < args.tiles_total && !*abort_flag; tile += gridDim.x) {
+        int a_y, b_y, m0, n0, z;
+        locate(tile, a_y, b_y, m0, n0, z);
+        for (int kb = 0; kb < args.k_blocks; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t round = g / STAGES;
+          if (g >= STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
+            atomicExch(args.status, STATUS_TIMEOUT_PRODUCER);
+            *abort_flag = 1;
+          }
+          if (*abort_flag)
+            break;
+          uint8_t *stage = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(stage, &a_hi, &full[s], kb * TK, a_y);
+          tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, a_y);
+          tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, b_y);
+          tma_load_2d(stage + 2 * A_BYTES + B_BYTES, &b_lo, &full[s], kb * TK, b_y);
+          *issued = g + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) { // MMA issuer
+      int g = 0, j = 0;
+      for (int tile = blockIdx.x; tile < args.tiles_total && !*abort_flag; tile += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1)) {
+          atomicExch(args.status, STATUS_TIMEOUT_MMA);
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS;
+        for (int kb = 0; kb < args.k_blocks; ++kb, ++g) {
+          const int s = g % STAGES;
+          if (!mbar_wait(&full[s], (g / STAGES) & 1)) {
+            atomicExch(args.status, STATUS_TIMEOUT_MMA);
+            *abort_flag = 1;
+            break;
+          }
+          *consumed = g + 1;
+          if (*abort_flag)
+            break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t stage = smem_u32(smem + s * STAGE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TK / 8; ++kk) {
+            const uint32_t step = kk * 32;
+            const uint64_t ah = desc_k_sw64(stage + step), al = desc_k_sw64(stage + A_BYTES + step);
+            const uint64_t bh = desc_k_sw64(stage + 2 * A_BYTES + step);
+            const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + B_BYTES + step);
+            mma_tf32(acc, ah, bh, (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_tf32(acc, ah, bl, 1u);
+            mma_tf32(acc, al, bh, 1u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (*abort_flag)
+          break;
+        mma_commit(&tmem_full[b]);
+      }
+      // Fires once every MMA issued above has finished (TMEM quiet before it is freed).
+      mma_commit(drained);
+    }
+  } else { // epilogue warps 2..5: TMEM lanes 32*(warp % 4) ..
+    const int sub = warp % 4;
+    int j = 0;
+    for (int tile = blockIdx.x; tile < args.tiles_total; tile += gridDim.x, ++j) {
+      const int b = j & 1;
+      bool ready = mbar_try_wait(&tmem_full[b], (j >> 1) & 1);
+      const long long start = clock64(), budget = WAIT_CYCLES + 100000ll * args.k_blocks;
+      while (!ready && !*abort_flag && clock64() - start < budget)
+        ready = mbar_try_wait(&tmem_full[b], (j >> 1) & 1);
+      if (!ready || *abort_flag) {
+        if (!ready && !*abort_flag)
+          atomicExch(args.status, STATUS_TIMEOUT_EPILOGUE);
+        *abort_flag = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int a_y, b_y, m0, n0, z;
+      locate(tile, a_y, b_y, m0, n0, z);
+      float *const c_base = args.c + int64_t(z) * args.c_batch;
+      const int64_t row0 = int64_t(m0) + 32 * sub; // this warp's 32 rows
+      const int64_t left = args.m - row0;
+      const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
+      float *tile_s = epi_tiles + sub * EPI_TILE_FLOATS;
+      const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS + (uint32_t(32 * sub) << 16);
+#pragma unroll 1
+      for (int col = 0; col < TN; col += 32) {
+        float v[32];
+        tmem_load_32(acc + uint32_t(col), v); // thread = row 32*sub + lane, 32 columns
+        const int64_t column = int64_t(n0) + col + lane;
+        if (int64_t(n0) + col >= args.n)
+          break; // the remaining columns of the tile are past n
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          tile_s[lane * 33 + q] = v[q];
+        __syncwarp();
+        if (column < args.n) {
+          float *cptr = c_base + row0 * args.ldc + column;
+          for (int r = 0; r < rows_here; ++r) // thread = column: one 128-byte row segment per store
+            cptr[r * args.ldc] = tile_s[r * 33 + lane];
+        }
+        __syncwarp();
+      }
+      // The buffer's loads are complete (tcgen05.wait::ld in tmem_load_32): hand it back.
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&tmem_empty[b])) : "memory");
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (*abort_flag) // copies requested but never consumed must land before shared memory is released
+      for (int g = *consumed; g < *issued; ++g)
+        (void)mbar_wait(&full[g % STAGES], (g / STAGES) & 1);
+    (void)mbar_wait(drained, 0); // bounded: every MMA has finished writing TMEM
+  }
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TMEM_COLUMNS)
+                 : "memory");
+  }
+}
+
 // ---- host side ----
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
@@ -368,6 +576,30 @@ bool make_map(CUtensorMap *map, float *base, int64_t rows_pad, int64_t k_pad, ui
 
 int64_t round_up(int64_t v, int64_t to) { return (v + to - 1) / to * to; }
 
+// Shared-memory limit of the persistent kernel, set once per device (the
+// attribute belongs to the device's context).
+bool configure_persistent(int device) {
+  static bool configured[64] = {};
+  if (device < 0 || device >= 64)
+    return false;
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES_PERSISTENT) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    configured[device] = true;
+  }
+  return true;
+}
+
+void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles) {
+  t.tiles_total = int(tiles);
+  const uint32_t ctas = uint32_t(std::min<int64_t>(tiles, std::max(1, L.sm_count)));
+  gemm_tf32x3_persistent<<<ctas, THREADS, SMEM_BYTES_PERSISTENT, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+}
+
 } // namespace
 
 // Plans and enqueues the 3xTF32 GEMM; returns false (nothing enqueued) when the
@@ -395,23 +627,15 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   if (!make_map(&maps[0], ahi, m_pad, k_pad, TM) || !make_map(&maps[1], alo, m_pad, k_pad, TM) ||
       !make_map(&maps[2], bhi, n_pad, k_pad, TN) || !make_map(&maps[3], blo, n_pad, k_pad, TN))
     return false;
-  static bool configured[64] = {};
-  if (L.device < 0 || L.device >= 64)
+  if (!configure_persistent(L.device))
     return false;
-  if (!configured[L.device]) { // per device: the attribute belongs to the device's context
-    if (cudaFuncSetAttribute(gemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    configured[L.device] = true;
-  }
   // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi,
                                                                                     alo, k_pad, 0, m_pad);
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi,
                                                                                     blo, k_pad, 0, n_pad);
   TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
-  gemm_tf32x3<<<uint32_t(tiles_m * tiles_n), THREADS, SMEM_BYTES, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+  launch_persistent(L, maps, t, tiles_m * tiles_n);
   L.kernels = 3;
   L.variant = "tcgen05_tf32x3";
   return true;
@@ -448,16 +672,8 @@ bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, 
   if (!make_map(&maps[0], ahi, batch * m_pad, k_pad, TM) || !make_map(&maps[1], alo, batch * m_pad, k_pad, TM) ||
       !make_map(&maps[2], bhi, batch_b * n_pad, k_pad, TN) || !make_map(&maps[3], blo, batch_b * n_pad, k_pad, TN))
     return false;
-  static bool configured[64] = {};
-  if (L.device < 0 || L.device >= 64)
+  if (!configure_persistent(L.device))
     return false;
-  if (!configured[L.device]) {
-    if (cudaFuncSetAttribute(gemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    configured[L.device] = true;
-  }
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
       a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, m_pad);
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
@@ -467,8 +683,7 @@ bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, 
   t.a_rows = int(m_pad);
   t.b_rows = sb ? int(n_pad) : 0;
   t.c_batch = sc;
-  gemm_tf32x3<<<uint32_t(tiles_m * tiles_n * batch), THREADS, SMEM_BYTES, L.stream>>>(maps[0], maps[1], maps[2],
-                                                                                      maps[3], t);
+  launch_persistent(L, maps, t, tiles_m * tiles_n * batch);
   L.kernels = 3;
   L.variant = "batched_tcgen05_tf32x3";
   return true;

@@ -171,7 +171,7 @@ __device__ __forceinline__ uint32_t visible_columns(uint64_t row, uint32_t rows,
 }
 
 template <int R>
-__global__ void __launch_bounds__(256) softmax_warp_rows(const float *__restrict__ x, float *__restrict__ out,
+__global__ void __launch_bounds__(256, R <= 4 ? 3 : 1) softmax_warp_rows(const float *__restrict__ x, float *__restrict__ out,
                                                          uint32_t all_rows, uint32_t rows, uint32_t columns,
                                                          uint32_t causal, float scale) {
   const uint32_t lane = threadIdx.x & 31u;
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(256) softmax_warp_rows(const float *__restrict
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t col = 256u * i + 128u * h + 4u * lane;
-      const float4 q = col < columns ? __ldcs(reinterpret_cast<const float4 *>(xr + col))
+      const float4 q = col < visible ? __ldcs(reinterpret_cast<const float4 *>(xr + col)) // masked: not read
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
       unpack(q, v[i][h]);
 #pragma unroll

@@ -348,9 +348,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Every wait is bounded as in the one-tile kernel; before TMEM is freed the MMA
 // thread's final commit guarantees no MMA is still writing it.
 // Epilogue stores are coalesced: each warp passes its 32x32 accumulator chunk
-// (thread = row) through a padded shared-memory tile and writes it back one row
-// per instruction (thread = column), 128 contiguous bytes per store.
-constexpr int EPI_TILE_FLOATS = 32 * 33;
+// (thread = row) through a shared-memory tile with 36-float rows (16-byte aligned,
+// bank-conflict-free for 128-bit accesses by each quarter warp) and writes it
+// back with 128-bit stores, eight threads per 128-byte row segment, four rows per
+// instruction.
+constexpr int EPI_PITCH = 36;
+constexpr int EPI_TILE_FLOATS = 32 * EPI_PITCH;
 constexpr int SMEM_BYTES_PERSISTENT = SMEM_BYTES + 4 * EPI_TILE_FLOATS * 4;
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
@@ -501,21 +504,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
       float *tile_s = epi_tiles + sub * EPI_TILE_FLOATS;
       const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS + (uint32_t(32 * sub) << 16);
+      const bool vec_c = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
       for (int col = 0; col < TN; col += 32) {
         float v[32];
         tmem_load_32(acc + uint32_t(col), v); // thread = row 32*sub + lane, 32 columns
-        const int64_t column = int64_t(n0) + col + lane;
-        if (int64_t(n0) + col >= args.n)
+        const int64_t first = int64_t(n0) + col;
+        if (first >= args.n)
           break; // the remaining columns of the tile are past n
 #pragma unroll
-        for (int q = 0; q < 32; ++q)
-          tile_s[lane * 33 + q] = v[q];
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH + q]) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         __syncwarp();
-        if (column < args.n) {
-          float *cptr = c_base + row0 * args.ldc + column;
-          for (int r = 0; r < rows_here; ++r) // thread = column: one 128-byte row segment per store
-            cptr[r * args.ldc] = tile_s[r * 33 + lane];
+        if (vec_c && rows_here == 32 && first + 31 < args.n) {
+          const int r_in = lane / 8, c4 = 4 * (lane % 8); // 4 rows x 8 float4 per instruction
+          float4 w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            w[i] = *reinterpret_cast<const float4 *>(&tile_s[(4 * i + r_in) * EPI_PITCH + c4]);
+          float *cptr = c_base + (row0 + r_in) * args.ldc + first + c4;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4 *>(cptr + int64_t(4 * i) * args.ldc) = w[i];
+        } else {
+          const int64_t column = first + lane; // thread = column: one row segment per store
+          if (column < args.n) {
+            float *cptr = c_base + row0 * args.ldc + column;
+            for (int r = 0; r < rows_here; ++r)
+              cptr[r * args.ldc] = tile_s[r * EPI_PITCH + lane];
+          }
         }
         __syncwarp();
       }

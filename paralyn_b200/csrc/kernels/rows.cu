@@ -22,7 +22,9 @@
 // 256i + 128 + 4L of chunk i. The tree then runs w = 128 inside the thread,
 // w = 64..4 as shuffles with thread L + 16..1 and w = 2, 1 inside the thread.
 //   reduce_warp_rows     streams chunks (any column count), 8 rows per block
-//   softmax_warp_rows<R> keeps the row in registers (columns <= 256 R, R <= 8)
+//   softmax_warp_rows<R> keeps the row in registers (columns <= 256 R, R <= 8),
+//                        skips masked columns and takes the row maximum with
+//                        max.NaN (same softmax values; see max_nan)
 // Other rows take one 256-thread block per row with thread t = lane t.
 #include "../runtime/builtin.hpp"
 #include <algorithm>
@@ -170,6 +172,23 @@ __device__ __forceinline__ uint32_t visible_columns(uint64_t row, uint32_t rows,
   return causal ? uint32_t(row % rows) + (columns - rows) + 1u : columns;
 }
 
+// NaN-propagating maximum (max.NaN). For softmax only the value of the row
+// maximum matters: exp(v - m) is the same for m = +0.0 and m = -0.0, and any NaN
+// makes the whole row NaN, so this one instruction gives the reference's results
+// where Max::apply (its exact total order) takes several.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+struct MaxValue {
+  static __device__ __forceinline__ float identity() { return -__int_as_float(0x7f800000); }
+  static __device__ __forceinline__ float apply(float a, float b) { return max_nan(a, b); }
+};
+
+// Row in registers. Columns past `visible` (causal mask) are neither read nor
+// computed: whole float4 groups are skipped, only the group holding the mask edge
+// checks each element.
 template <int R>
 __global__ void __launch_bounds__(256, R <= 4 ? 3 : 1) softmax_warp_rows(const float *__restrict__ x, float *__restrict__ out,
                                                          uint32_t all_rows, uint32_t rows, uint32_t columns,
@@ -182,44 +201,49 @@ __global__ void __launch_bounds__(256, R <= 4 ? 3 : 1) softmax_warp_rows(const f
   float *yr = out + row * columns;
   const uint32_t visible = visible_columns(row, rows, columns, causal != 0);
   float v[R][2][4];
+  float s[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    s[c] = MaxValue::identity();
 #pragma unroll
   for (int i = 0; i < R; ++i)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t col = 256u * i + 128u * h + 4u * lane;
-      const float4 q = col < visible ? __ldcs(reinterpret_cast<const float4 *>(xr + col)) // masked: not read
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      unpack(q, v[i][h]);
+      if (col < visible) { // masked groups are not read
+        unpack(__ldcs(reinterpret_cast<const float4 *>(xr + col)), v[i][h]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        v[i][h][c] = __fmul_rn(scale, v[i][h][c]);
+        for (int c = 0; c < 4; ++c) {
+          v[i][h][c] = __fmul_rn(scale, v[i][h][c]);
+          if (col + 4 <= visible || col + c < visible)
+            s[4 * h + c] = MaxValue::apply(s[4 * h + c], v[i][h][c]);
+        }
+      }
     }
-  float s[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-    s[c] = Max::identity();
-#pragma unroll
-  for (int i = 0; i < R; ++i)
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (256u * i + 128u * h + 4u * lane + c < visible)
-          s[4 * h + c] = Max::apply(s[4 * h + c], v[i][h][c]);
-  const float m = warp_tree<Max>(s);
+  const float m = warp_tree<MaxValue>(s);
 #pragma unroll
   for (int c = 0; c < 8; ++c)
     s[c] = 0.0f;
 #pragma unroll
   for (int i = 0; i < R; ++i)
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t col = 256u * i + 128u * h + 4u * lane;
+      if (col + 4 <= visible) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (256u * i + 128u * h + 4u * lane + c < visible) {
+        for (int c = 0; c < 4; ++c) {
           v[i][h][c] = expf(__fsub_rn(v[i][h][c], m));
           s[4 * h + c] = __fadd_rn(s[4 * h + c], v[i][h][c]);
         }
+      } else if (col < visible) { // the group holding the mask edge
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (col + c < visible) {
+            v[i][h][c] = expf(__fsub_rn(v[i][h][c], m));
+            s[4 * h + c] = __fadd_rn(s[4 * h + c], v[i][h][c]);
+          }
+      }
+    }
   const float rinv = __frcp_rn(warp_tree<Sum>(s));
 #pragma unroll
   for (int i = 0; i < R; ++i)

@@ -736,7 +736,7 @@ def run_reference(args, group):
         values.append(v)
     value = sorted(values)[len(values) // 2]
     return {"impl": "reference", "metric": METRICS[args.workload], "value": round(value, 4), "unit": unit,
-            "n_gpus": group.world, "steps": steps, "warmup": args.warmup, "higher_is_better": True,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", args.gpus)), "steps": steps, "warmup": args.warmup, "higher_is_better": True,
             "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload, "sample": sample},
             "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
                              "sample": sample},

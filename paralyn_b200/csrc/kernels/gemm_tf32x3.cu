@@ -181,6 +181,11 @@ struct TileArgs {
   int tiles_per_batch = 0, a_rows = 0, b_rows = 0;
   int64_t c_batch = 0;
   int tiles_total = 0; // persistent kernel: tiles of all matrices
+  // Persistent kernel work units: units [0, full_units) are whole tiles; after them
+  // every remaining tile is cut into `split` k-ranges whose partial sums go to
+  // `partials` (one 128x256 tile each) and are added by split_fixup.
+  int units_total = 0, full_units = 0, split = 1;
+  float *partials = nullptr;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -384,6 +389,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     a_y = z * args.a_rows + m0;
     b_y = z * args.b_rows + n0;
   };
+  // Unit -> tile and k-slice range [kb0, kb1).
+  auto unit = [&](int u, int &tile, int &kb0, int &kb1) {
+    if (u < args.full_units) {
+      tile = u;
+      kb0 = 0;
+      kb1 = args.k_blocks;
+    } else {
+      const int v = u - args.full_units, part = v % args.split;
+      tile = args.full_units + v / args.split;
+      kb0 = part * args.k_blocks / args.split;
+      kb1 = (part + 1) * args.k_blocks / args.split;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -415,10 +433,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     if (lane == 0) { // TMA producer
       int g = 0;
-      for (int tile = blockIdx.x; tile < args.tiles_total && !*abort_flag; tile += gridDim.x) {
-        int a_y, b_y, m0, n0, z;
+      for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x) {
+        int tile, kb0, kb1, a_y, b_y, m0, n0, z;
+        unit(u, tile, kb0, kb1);
         locate(tile, a_y, b_y, m0, n0, z);
-        for (int kb = 0; kb < args.k_blocks; ++kb, ++g) {
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % STAGES;
           const uint32_t round = g / STAGES;
           if (g >= STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
@@ -440,7 +459,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) { // MMA issuer
       int g = 0, j = 0;
-      for (int tile = blockIdx.x; tile < args.tiles_total && !*abort_flag; tile += gridDim.x, ++j) {
+      for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x, ++j) {
+        int tile, kb0, kb1;
+        unit(u, tile, kb0, kb1);
         const int b = j & 1;
         if (j >= 2 && !mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1)) {
           atomicExch(args.status, STATUS_TIMEOUT_MMA);
@@ -449,7 +470,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS;
-        for (int kb = 0; kb < args.k_blocks; ++kb, ++g) {
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % STAGES;
           if (!mbar_wait(&full[s], (g / STAGES) & 1)) {
             atomicExch(args.status, STATUS_TIMEOUT_MMA);
@@ -467,7 +488,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t ah = desc_k_sw64(stage + step), al = desc_k_sw64(stage + A_BYTES + step);
             const uint64_t bh = desc_k_sw64(stage + 2 * A_BYTES + step);
             const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + B_BYTES + step);
-            mma_tf32(acc, ah, bh, (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_tf32(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
             mma_tf32(acc, ah, bl, 1u);
             mma_tf32(acc, al, bh, 1u);
           }
@@ -483,7 +504,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else { // epilogue warps 2..5: TMEM lanes 32*(warp % 4) ..
     const int sub = warp % 4;
     int j = 0;
-    for (int tile = blockIdx.x; tile < args.tiles_total; tile += gridDim.x, ++j) {
+    for (int u = blockIdx.x; u < args.units_total; u += gridDim.x, ++j) {
+      int tile, kb0, kb1;
+      unit(u, tile, kb0, kb1);
       const int b = j & 1;
       bool ready = mbar_try_wait(&tmem_full[b], (j >> 1) & 1);
       const long long start = clock64(), budget = WAIT_CYCLES + 100000ll * args.k_blocks;
@@ -498,40 +521,46 @@ __global__ void __launch_bounds__(THREADS, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       int a_y, b_y, m0, n0, z;
       locate(tile, a_y, b_y, m0, n0, z);
-      float *const c_base = args.c + int64_t(z) * args.c_batch;
-      const int64_t row0 = int64_t(m0) + 32 * sub; // this warp's 32 rows
-      const int64_t left = args.m - row0;
+      // Whole tiles go to C; the k-range parts of split tiles go to their own
+      // 128x256 partial tile (row stride 256), all of it written.
+      const bool whole = u < args.full_units;
+      float *const c_base = whole ? args.c + int64_t(z) * args.c_batch
+                                  : args.partials + int64_t(u - args.full_units) * (TM * TN);
+      const int64_t ldc = whole ? args.ldc : TN, m_lim = whole ? args.m : TM, n_lim = whole ? args.n : TN;
+      const int64_t row0 = (whole ? int64_t(m0) : 0) + 32 * sub; // this warp's 32 rows
+      const int64_t col0 = whole ? int64_t(n0) : 0;
+      const int64_t left = m_lim - row0;
       const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
       float *tile_s = epi_tiles + sub * EPI_TILE_FLOATS;
       const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS + (uint32_t(32 * sub) << 16);
-      const bool vec_c = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
+      const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
       for (int col = 0; col < TN; col += 32) {
         float v[32];
         tmem_load_32(acc + uint32_t(col), v); // thread = row 32*sub + lane, 32 columns
-        const int64_t first = int64_t(n0) + col;
-        if (first >= args.n)
+        const int64_t first = col0 + col;
+        if (first >= n_lim)
           break; // the remaining columns of the tile are past n
 #pragma unroll
         for (int q = 0; q < 32; q += 4)
           *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH + q]) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         __syncwarp();
-        if (vec_c && rows_here == 32 && first + 31 < args.n) {
+        if (vec_c && rows_here == 32 && first + 31 < n_lim) {
           const int r_in = lane / 8, c4 = 4 * (lane % 8); // 4 rows x 8 float4 per instruction
           float4 w[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             w[i] = *reinterpret_cast<const float4 *>(&tile_s[(4 * i + r_in) * EPI_PITCH + c4]);
-          float *cptr = c_base + (row0 + r_in) * args.ldc + first + c4;
+          float *cptr = c_base + (row0 + r_in) * ldc + first + c4;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4 *>(cptr + int64_t(4 * i) * args.ldc) = w[i];
+            *reinterpret_cast<float4 *>(cptr + int64_t(4 * i) * ldc) = w[i];
         } else {
           const int64_t column = first + lane; // thread = column: one row segment per store
-          if (column < args.n) {
-            float *cptr = c_base + row0 * args.ldc + column;
+          if (column < n_lim) {
+            float *cptr = c_base + row0 * ldc + column;
             for (int r = 0; r < rows_here; ++r)
-              cptr[r * args.ldc] = tile_s[r * EPI_PITCH + lane];
+              cptr[r * ldc] = tile_s[r * EPI_PITCH + lane];
           }
         }
         __syncwarp();
@@ -556,6 +585,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TMEM_COLUMNS)
                  : "memory");
   }
+}
+
+// C of every split tile = its partial tiles added in k order (one thread per
+// element, 256 columns per block, one block per tile row).
+__global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
+  const int t = blockIdx.y, i = blockIdx.x, j = threadIdx.x; // remaining tile, row, column in tile
+  const int tile = args.full_units + t;
+  const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
+  const int z = tile / per_batch, id = tile % per_batch, group = 8, per_group = group * args.tiles_n;
+  const int first_m = (id / per_group) * group;
+  const int rows_in_group = min(group, args.tiles_m - first_m);
+  const int64_t row = int64_t(first_m + (id % per_group) % rows_in_group) * TM + i;
+  const int64_t col = int64_t((id % per_group) / rows_in_group) * TN + j;
+  if (row >= args.m || col >= args.n)
+    return;
+  const float *p = args.partials + int64_t(t) * args.split * (TM * TN) + i * TN + j;
+  float sum = p[0];
+  for (int q = 1; q < args.split; ++q)
+    sum = __fadd_rn(sum, p[int64_t(q) * (TM * TN)]);
+  args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = sum;
 }
 
 // ---- host side ----
@@ -611,10 +660,42 @@ bool configure_persistent(int device) {
   return true;
 }
 
-void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles) {
+// Work units of the persistent kernel. With G CTAs, tiles = R*G + r: when the last
+// round would keep fewer than half of the SMs busy, its r tiles are cut into
+// s = min(G / r, 4) k-ranges so that round ends about s times sooner.
+struct UnitPlan {
+  int ctas, full_units, split, units, remaining;
+  size_t partial_bytes;
+};
+UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks) {
+  UnitPlan p{};
+  p.ctas = int(std::min<int64_t>(tiles, std::max(1, sm_count)));
+  const int64_t r = tiles % p.ctas;
+  p.split = 1;
+  if (r > 0 && 2 * r <= p.ctas)
+    p.split = int(std::min<int64_t>({p.ctas / r, 4, k_blocks / 2}));
+  if (p.split < 2)
+    p.split = 1;
+  p.remaining = p.split > 1 ? int(r) : 0;
+  p.full_units = int(tiles - p.remaining);
+  p.units = p.full_units + p.remaining * p.split;
+  p.partial_bytes = size_t(p.remaining) * p.split * TM * TN * sizeof(float);
+  return p;
+}
+
+void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
+                       float *partials) {
   t.tiles_total = int(tiles);
-  const uint32_t ctas = uint32_t(std::min<int64_t>(tiles, std::max(1, L.sm_count)));
-  gemm_tf32x3_persistent<<<ctas, THREADS, SMEM_BYTES_PERSISTENT, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+  t.units_total = plan.units;
+  t.full_units = plan.full_units;
+  t.split = plan.split;
+  t.partials = partials;
+  gemm_tf32x3_persistent<<<uint32_t(plan.ctas), THREADS, SMEM_BYTES_PERSISTENT, L.stream>>>(maps[0], maps[1],
+                                                                                            maps[2], maps[3], t);
+  if (plan.remaining) {
+    split_fixup<<<dim3(TM, uint32_t(plan.remaining)), TN, 0, L.stream>>>(t);
+    ++L.kernels;
+  }
 }
 
 } // namespace
@@ -633,13 +714,16 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / TN;
   if (tiles_m * tiles_n > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 || n_pad / 32 > 65535)
     return false; // split-kernel grid.y limit
-  const size_t bytes = size_t(8) * size_t(k_pad) * size_t(m_pad + n_pad);
+  const UnitPlan plan = plan_units(tiles_m * tiles_n, L.sm_count, int(k_pad / TK));
+  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(m_pad + n_pad);
+  const size_t bytes = split_bytes + plan.partial_bytes;
   if (L.dry_run)
     return true;
   auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
   if (!scratch)
     return false;
   float *ahi = scratch, *alo = ahi + m_pad * k_pad, *bhi = alo + m_pad * k_pad, *blo = bhi + n_pad * k_pad;
+  float *partials = scratch + split_bytes / sizeof(float);
   CUtensorMap maps[4];
   if (!make_map(&maps[0], ahi, m_pad, k_pad, TM) || !make_map(&maps[1], alo, m_pad, k_pad, TM) ||
       !make_map(&maps[2], bhi, n_pad, k_pad, TN) || !make_map(&maps[3], blo, n_pad, k_pad, TN))
@@ -652,8 +736,8 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi,
                                                                                     blo, k_pad, 0, n_pad);
   TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
-  launch_persistent(L, maps, t, tiles_m * tiles_n);
   L.kernels = 3;
+  launch_persistent(L, maps, t, tiles_m * tiles_n, plan, partials);
   L.variant = "tcgen05_tf32x3";
   return true;
 }
@@ -677,12 +761,15 @@ bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, 
   if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 ||
       n_pad / 32 > 65535 || batch * m_pad > INT32_MAX || batch_b * n_pad > INT32_MAX)
     return false; // grid limits and 32-bit TMA row coordinates
-  const size_t bytes = size_t(8) * size_t(k_pad) * size_t(batch * m_pad + batch_b * n_pad);
+  const UnitPlan plan = plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK));
+  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(batch * m_pad + batch_b * n_pad);
+  const size_t bytes = split_bytes + plan.partial_bytes;
   if (L.dry_run)
     return true;
   auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
   if (!scratch)
     return false;
+  float *partials = scratch + split_bytes / sizeof(float);
   float *ahi = scratch, *alo = ahi + batch * m_pad * k_pad, *bhi = alo + batch * m_pad * k_pad,
         *blo = bhi + batch_b * n_pad * k_pad;
   CUtensorMap maps[4];
@@ -700,8 +787,8 @@ bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, 
   t.a_rows = int(m_pad);
   t.b_rows = sb ? int(n_pad) : 0;
   t.c_batch = sc;
-  launch_persistent(L, maps, t, tiles_m * tiles_n * batch);
   L.kernels = 3;
+  launch_persistent(L, maps, t, tiles_m * tiles_n * batch, plan, partials);
   L.variant = "batched_tcgen05_tf32x3";
   return true;
 }

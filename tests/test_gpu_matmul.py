@@ -130,3 +130,22 @@ def test_matmul_validation(context):
     assert error.value.code in (p.Status.UNSUPPORTED, p.Status.INVALID_ARGUMENT)
     c.close()
     buf.close()
+
+
+@pytest.mark.parametrize("m,n,k", [(2432, 2048, 1024), (4096, 4096, 256), (4096, 4096, 40), (128 * 150, 256, 96)])
+def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
+    # Tile counts just above a multiple of the 148 persistent CTAs: the tiles of the
+    # last, mostly idle round are cut into k-ranges whose partial sums are added by a
+    # second kernel. Rows sampled from every tile row, all columns checked.
+    p.set_matmul_mode(context, p.MatmulMode.TF32X3)
+    try:
+        a = synthetic.uniform(7000 + k, 0, m * k)
+        b = synthetic.uniform(8000 + k, 0, k * n)
+        with p.tensor(a, shape=(m, k), context=context) as ta, p.tensor(b, shape=(k, n), context=context) as tb, \
+                p.matmul(ta, tb) as tc:
+            c = np.asarray(tc.to_host(), np.float32).reshape(m, n)
+        rows = np.unique(np.concatenate([np.arange(0, m, 128), np.arange(127, m, 128), [m - 1]]))
+        exact, magnitude = oracle.matmul_exact(a.reshape(m, k)[rows].ravel(), b, len(rows), n, k)
+        assert np.all(np.abs(c[rows].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)

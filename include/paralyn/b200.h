@@ -88,6 +88,15 @@ pr_status pr_b200_buffer_read_async(pr_queue queue, pr_buffer buffer, uint64_t o
 pr_status pr_b200_host_register(void *pointer, uint64_t bytes);
 pr_status pr_b200_host_unregister(void *pointer);
 
+/* Failure-path probe (no counterpart in the reference). Enqueues a one-thread
+ * kernel that waits on a shared-memory barrier nothing completes and gives up after
+ * `cycles` SM clock cycles (1 .. 4e9), exactly as the library's TMA and tensor-core
+ * kernels give up a stalled wait: it records a status code in the context's status
+ * word and returns, and the command fails with PR_EXECUTION_FAILED ("abandoned a
+ * bounded wait"). The context's failure is then sticky, as after any failed command.
+ * The GPU itself is left healthy. */
+pr_status pr_b200_selftest_bounded_wait(pr_queue queue, uint64_t cycles, pr_event *event);
+
 /* Enqueues an empty command whose only effect is a device timestamp on the
  * context queue; it follows every earlier command, copies included.
  * pr_b200_event_elapsed returns the device time between the

@@ -32,6 +32,7 @@ def _b200(lib):
             "pr_b200_host_register": (_c.c_int, [_c.c_void_p, u64]),
             "pr_b200_host_unregister": (_c.c_int, [_c.c_void_p]),
             "pr_b200_marker": (_c.c_int, [h, ptr(h)]),
+            "pr_b200_selftest_bounded_wait": (_c.c_int, [h, u64, ptr(h)]),
             "pr_b200_event_elapsed": (_c.c_int, [h, h, ptr(_c.c_double)]),
             "pr_b200_fill_synthetic_f32": (_c.c_int, [h, ptr(TensorDescRecord), u64, u64, u32,
                                                       _c.c_float, _c.c_float, ptr(h)]),
@@ -169,6 +170,15 @@ def host_unregister(host, library_path=None):
     lib = _b200(library(library_path))
     address, _ = _host_range(host, 0 if isinstance(host, int) else None)
     lib.check(lib.api.pr_b200_host_unregister(address))
+
+
+def selftest_bounded_wait(queue, cycles):
+    """Enqueue the bounded-wait probe (a wait that gives up after `cycles` SM cycles);
+    waiting on the returned event raises the command's failure."""
+    lib = _b200(queue._lib)
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_selftest_bounded_wait(queue.handle, int(cycles), _c.byref(handle)))
+    return Event._adopt(lib, handle.value)
 
 
 def marker(queue):

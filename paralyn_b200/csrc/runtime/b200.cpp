@@ -129,6 +129,23 @@ PB_EXPORT pr_status pr_b200_host_unregister(void *pointer) {
   });
 }
 
+namespace pb {
+void launch_selftest_bounded_wait(Launch &);
+}
+
+PB_EXPORT pr_status pr_b200_selftest_bounded_wait(pr_queue queue, uint64_t cycles, pr_event *out) {
+  return api("b200_selftest_bounded_wait", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    require(cycles >= 1 && cycles <= 4000000000ull, PR_INVALID_ARGUMENT, "cycles must be in [1, 4e9]");
+    std::vector<BoundArg> args(2);
+    args[0].bits = uint32_t(cycles);
+    args[1].bits = uint32_t(cycles >> 32);
+    *out = submit_command(queue, "b200_selftest_bounded_wait", launch_selftest_bounded_wait, Dim3{}, Dim3{},
+                          std::move(args), {});
+  });
+}
+
 PB_EXPORT pr_status pr_b200_marker(pr_queue queue, pr_event *out) {
   return api("b200_marker", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");

@@ -108,3 +108,23 @@ def test_device_kernel_count_advances(context):
     with p.asarray(np.ones(4096, np.float32), context=context) as a, p.add(a, a) as b:
         b.wait()
     assert p.device_kernel_count(context) == before + 1
+
+
+def test_bounded_wait_failure_path():
+    # A wait nothing completes gives up after ~1 ms of SM cycles: the kernel records
+    # its status and returns, the command fails and the GPU stays healthy (a new
+    # context works). A context of its own: the failure is sticky.
+    with p.Context("cuda:0") as ctx:
+        queue = ctx.queue()
+        event = p.b200.selftest_bounded_wait(queue, 2_000_000)
+        with pytest.raises(p.Error) as error:
+            event.wait()
+        assert error.value.code == p.Status.EXECUTION_FAILED
+        assert "abandoned a bounded wait" in str(error.value)
+        for obj in (event, queue):
+            try:
+                obj.close()
+            except p.Error:
+                pass
+    with p.Context("cuda:0") as ctx, p.asarray(np.ones(1000, np.float32), context=ctx) as a, p.add(a, a) as b:
+        assert np.all(np.asarray(b.to_host(), np.float32) == 2.0)

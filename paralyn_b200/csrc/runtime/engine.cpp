@@ -4,6 +4,8 @@
 #include <atomic>
 #include <chrono>
 #include <cmath>
+#include <condition_variable>
+#include <cstring>
 #include <cstdio>
 #include <cstdlib>
 #include <filesystem>
@@ -12,6 +14,7 @@
 #include <limits>
 #include <sstream>
 #include <sys/utsname.h>
+#include <thread>
 #include <unistd.h>
 
 namespace pb {
@@ -295,6 +298,12 @@ Engine::~Engine() {
       cudaStreamDestroy(stream_);
     if (side_stream_)
       cudaStreamDestroy(side_stream_);
+    for (int i = 0; i < staging_slots; ++i) {
+      if (staging_[i])
+        cudaFreeHost(staging_[i]);
+      if (staging_events_[i])
+        cudaEventDestroy(staging_events_[i]);
+    }
     for (auto copy : copy_streams_)
       if (copy)
         cudaStreamDestroy(copy);
@@ -386,6 +395,148 @@ static void copy_range(const Allocation &a, size_t offset, size_t bytes) {
     throw Error(Code::invalid_value, "Copy range exceeds allocation");
 }
 
+// Host-side copy split over a few worker threads (a pageable source or destination
+// is read or written at more than one core's memory bandwidth). The pool lives for
+// the process; its threads wait on a condition variable between copies.
+namespace {
+class CopyPool {
+public:
+  static CopyPool &get() {
+    static CopyPool *pool = new CopyPool(); // never destroyed: workers outlive static teardown
+    return *pool;
+  }
+  void copy(char *dst, const char *src, size_t bytes) {
+    const size_t parts = workers_ + 1, piece = ((bytes + parts - 1) / parts + 63) & ~size_t(63);
+    if (bytes < (size_t(1) << 20) || !workers_) {
+      std::memcpy(dst, src, bytes);
+      return;
+    }
+    {
+      std::lock_guard<std::mutex> lock(mutex_);
+      dst_ = dst;
+      src_ = src;
+      bytes_ = bytes;
+      piece_ = piece;
+      pending_ = workers_;
+      ++generation_;
+    }
+    wake_.notify_all();
+    const size_t mine = std::min(piece, bytes); // the caller copies part 0
+    std::memcpy(dst, src, mine);
+    std::unique_lock<std::mutex> lock(mutex_);
+    done_.wait(lock, [&] { return pending_ == 0; });
+  }
+
+private:
+  CopyPool() {
+    const unsigned hw = std::thread::hardware_concurrency();
+    workers_ = hw >= 8 ? 5 : (hw >= 4 ? hw / 2 : 0);
+    for (unsigned i = 0; i < workers_; ++i)
+      std::thread([this, i] { run(i + 1); }).detach();
+  }
+  void run(unsigned part) {
+    uint64_t seen = 0;
+    for (;;) {
+      char *dst;
+      const char *src;
+      size_t bytes, piece;
+      {
+        std::unique_lock<std::mutex> lock(mutex_);
+        wake_.wait(lock, [&] { return generation_ != seen; });
+        seen = generation_;
+        dst = dst_, src = src_, bytes = bytes_, piece = piece_;
+      }
+      const size_t begin = std::min(bytes, part * piece), end = std::min(bytes, begin + piece);
+      if (end > begin)
+        std::memcpy(dst + begin, src + begin, end - begin);
+      std::lock_guard<std::mutex> lock(mutex_);
+      if (--pending_ == 0)
+        done_.notify_one();
+    }
+  }
+  unsigned workers_ = 0;
+  std::mutex mutex_;
+  std::condition_variable wake_, done_;
+  char *dst_ = nullptr;
+  const char *src_ = nullptr;
+  size_t bytes_ = 0, piece_ = 0;
+  unsigned pending_ = 0;
+  uint64_t generation_ = 0;
+};
+
+bool pageable(const void *p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false; // unknown: let the direct copy decide
+  }
+  return a.type == cudaMemoryTypeUnregistered;
+}
+} // namespace
+
+// Slot i of the ring is reused only after the event recorded behind its last DMA.
+bool Engine::staged_copy(bool to_device, char *device, void *host, size_t bytes) {
+  if (bytes < (size_t(4) << 20) || !pageable(host))
+    return false;
+  if (!staging_[0]) {
+    for (int i = 0; i < staging_slots; ++i) {
+      if (cudaHostAlloc(reinterpret_cast<void **>(&staging_[i]), staging_slot_bytes, cudaHostAllocPortable) !=
+              cudaSuccess ||
+          cudaEventCreateWithFlags(&staging_events_[i], cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        for (int j = 0; j <= i; ++j) {
+          if (staging_[j])
+            cudaFreeHost(staging_[j]);
+          if (staging_events_[j])
+            cudaEventDestroy(staging_events_[j]);
+          staging_[j] = nullptr;
+          staging_events_[j] = nullptr;
+        }
+        return false; // no pinned memory: the direct copy still works
+      }
+    }
+  }
+  auto &pool = CopyPool::get();
+  auto *h = static_cast<char *>(host);
+  const size_t chunks = (bytes + staging_slot_bytes - 1) / staging_slot_bytes;
+  auto check = [&](cudaError_t e, const char *what) {
+    if (e != cudaSuccess)
+      cuda_failure(e, what);
+  };
+  if (to_device) {
+    for (size_t c = 0; c < chunks; ++c) {
+      const int slot = int(c % staging_slots);
+      const size_t off = c * staging_slot_bytes, len = std::min(staging_slot_bytes, bytes - off);
+      if (c >= size_t(staging_slots))
+        check(cudaEventSynchronize(staging_events_[slot]), "cudaEventSynchronize(staging)");
+      pool.copy(staging_[slot], h + off, len);
+      check(cudaMemcpyAsync(device + off, staging_[slot], len, cudaMemcpyHostToDevice, stream_),
+            "cudaMemcpyAsync(host to device, staged)");
+      check(cudaEventRecord(staging_events_[slot], stream_), "cudaEventRecord(staging)");
+    }
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    return true;
+  }
+  auto issue = [&](size_t c) {
+    const int slot = int(c % staging_slots);
+    const size_t off = c * staging_slot_bytes, len = std::min(staging_slot_bytes, bytes - off);
+    check(cudaMemcpyAsync(staging_[slot], device + off, len, cudaMemcpyDeviceToHost, stream_),
+          "cudaMemcpyAsync(device to host, staged)");
+    check(cudaEventRecord(staging_events_[slot], stream_), "cudaEventRecord(staging)");
+  };
+  for (size_t c = 0; c < chunks && c < size_t(staging_slots); ++c)
+    issue(c);
+  for (size_t c = 0; c < chunks; ++c) {
+    const int slot = int(c % staging_slots);
+    const size_t off = c * staging_slot_bytes, len = std::min(staging_slot_bytes, bytes - off);
+    check(cudaEventSynchronize(staging_events_[slot]), "cudaEventSynchronize(staging)");
+    pool.copy(h + off, staging_[slot], len);
+    if (c + staging_slots < chunks)
+      issue(c + staging_slots);
+  }
+  return true;
+}
+
 // Host pointers may be pageable or pinned; any UVA address (including device
 // memory of this process) is accepted because the copy kind is inferred.
 void Engine::write(const std::shared_ptr<Allocation> &allocation, size_t offset,
@@ -399,8 +550,14 @@ void Engine::write(const std::shared_ptr<Allocation> &allocation, size_t offset,
   const auto start = std::chrono::steady_clock::now();
   if (bytes) {
     DeviceScope scope(device_.ordinal);
-    cudaError_t e = cudaMemcpyAsync(static_cast<char *>(allocation->ptr) + offset, source, bytes,
-                                    cudaMemcpyDefault, stream_);
+    char *device = static_cast<char *>(allocation->ptr) + offset;
+    if (staged_copy(true, device, const_cast<void *>(source), bytes)) {
+      counters_.h2d_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+      counters_.h2d_bytes += bytes;
+      runtime_event("transfer", "completed", "host_to_device", trace_id_, 0, bytes);
+      return;
+    }
+    cudaError_t e = cudaMemcpyAsync(device, source, bytes, cudaMemcpyDefault, stream_);
     if (e == cudaSuccess)
       e = cudaStreamSynchronize(stream_);
     if (e != cudaSuccess)
@@ -423,8 +580,14 @@ void Engine::read(const std::shared_ptr<Allocation> &allocation, size_t offset, 
   const auto start = std::chrono::steady_clock::now();
   if (bytes) {
     DeviceScope scope(device_.ordinal);
-    cudaError_t e = cudaMemcpyAsync(destination, static_cast<const char *>(allocation->ptr) + offset,
-                                    bytes, cudaMemcpyDefault, stream_);
+    char *device = static_cast<char *>(allocation->ptr) + offset;
+    if (staged_copy(false, device, destination, bytes)) {
+      counters_.d2h_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+      counters_.d2h_bytes += bytes;
+      runtime_event("transfer", "completed", "device_to_host", trace_id_, 0, bytes);
+      return;
+    }
+    cudaError_t e = cudaMemcpyAsync(destination, device, bytes, cudaMemcpyDefault, stream_);
     if (e == cudaSuccess)
       e = cudaStreamSynchronize(stream_);
     if (e != cudaSuccess)

@@ -155,6 +155,14 @@ private:
   void prune(int lane);
   std::deque<Record> records_[lanes];
   cudaStream_t copy_streams_[2] = {};
+  // Blocking copies from or to pageable host memory go through a ring of pinned
+  // staging slots (allocated on first use): host-side memcpy of one slot (several
+  // threads) overlaps the DMA of the previous one.
+  static constexpr int staging_slots = 4;
+  static constexpr size_t staging_slot_bytes = size_t(16) << 20;
+  bool staged_copy(bool to_device, char *device, void *host, size_t bytes);
+  char *staging_[staging_slots] = {};
+  cudaEvent_t staging_events_[staging_slots] = {};
   void *workspace_ = nullptr;
   size_t workspace_bytes_ = 0;
 

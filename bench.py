@@ -79,7 +79,7 @@ class Group:
         if world > 1 or (int(os.environ.get("WORLD_SIZE", "1")) > 1 and world != 1):
             import datetime
             import torch.distributed as dist
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
             self.dist = dist
             self.world = dist.get_world_size()
             self.rank = dist.get_rank()

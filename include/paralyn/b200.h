@@ -88,6 +88,16 @@ pr_status pr_b200_buffer_read_async(pr_queue queue, pr_buffer buffer, uint64_t o
 pr_status pr_b200_host_register(void *pointer, uint64_t bytes);
 pr_status pr_b200_host_unregister(void *pointer);
 
+/* C = activation(op(A) op(B) + bias[column]) as one command (no counterpart in the
+ * reference, which takes two: pr_matmul_f32 then pr_bias_activation_f32). The
+ * record, validation order and statuses are pr_matmul_f32's; `bias` (may be NULL) is
+ * a contiguous [n] tensor not aliasing C; activation is a pr_activation value. The
+ * bias add and activation run in the GEMM epilogue, so C is written once, and the
+ * result equals the two-command sequence bit for bit in every matmul mode. */
+pr_status pr_b200_matmul_bias_activation_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
+                                             const pr_tensor_desc_v1 *bias, uint32_t activation,
+                                             pr_event *event);
+
 /* Failure-path probe (no counterpart in the reference). Enqueues a one-thread
  * kernel that waits on a shared-memory barrier nothing completes and gives up after
  * `cycles` SM clock cycles (1 .. 4e9), exactly as the library's TMA and tensor-core

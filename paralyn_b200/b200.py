@@ -33,6 +33,7 @@ def _b200(lib):
             "pr_b200_host_unregister": (_c.c_int, [_c.c_void_p]),
             "pr_b200_marker": (_c.c_int, [h, ptr(h)]),
             "pr_b200_selftest_bounded_wait": (_c.c_int, [h, u64, ptr(h)]),
+            "pr_b200_matmul_bias_activation_f32": (_c.c_int, [h, h, _c.c_void_p, _c.c_void_p, u32, ptr(h)]),
             "pr_b200_event_elapsed": (_c.c_int, [h, h, ptr(_c.c_double)]),
             "pr_b200_fill_synthetic_f32": (_c.c_int, [h, ptr(TensorDescRecord), u64, u64, u32,
                                                       _c.c_float, _c.c_float, ptr(h)]),
@@ -170,6 +171,23 @@ def host_unregister(host, library_path=None):
     lib = _b200(library(library_path))
     address, _ = _host_range(host, 0 if isinstance(host, int) else None)
     lib.check(lib.api.pr_b200_host_unregister(address))
+
+
+def matmul_bias_activation_into(queue, operators, a, b, c, bias, *, m, n, k, transpose_a=False, transpose_b=False,
+                                activation=0):
+    """C = activation(op(A) op(B) + bias[column]) as one command (bias may be None);
+    equal to matmul_into followed by bias_activation_into, bit for bit."""
+    from .tensor import MatmulRecord, TENSOR_VERSION_1, Activation
+    lib = _b200(queue._lib)
+    descs = [x._native() for x in (a, b, c)]
+    record = MatmulRecord(_c.sizeof(MatmulRecord), TENSOR_VERSION_1, m, n, k, int(bool(transpose_a)),
+                          int(bool(transpose_b)), *(_c.pointer(d) for d in descs))
+    bias_native = bias._native() if bias is not None else None
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_matmul_bias_activation_f32(
+        queue.handle, operators.handle, _c.byref(record),
+        _c.byref(bias_native) if bias_native is not None else None, int(Activation(activation)), _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
 
 
 def selftest_bounded_wait(queue, cycles):

@@ -12,6 +12,7 @@
 // grid is a multiple of the SM count, each thread keeps four independent 128-bit
 // loads per operand in flight.
 #include "../runtime/builtin.hpp"
+#include "activation.cuh"
 #include <algorithm>
 
 namespace pb {
@@ -150,20 +151,7 @@ template <int OP> void ir_elementwise(Launch &L, uint64_t count) {
               static_cast<float *>(v[2].ptr), count, OP == op_affine ? v[4].f32() : 0.f, 0.f);
 }
 
-// ---- bias + activation (reference runtime/tensor.cpp:79-115) ----
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float cube = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fadd_rn(x, __fmul_rn(0.044715f, cube));
-  const float t = tanhf(__fmul_rn(0.7978845608028654f, inner));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
-}
-__device__ __forceinline__ float activate(float v, uint32_t activation) {
-  if (activation == 1u && v < 0.0f)
-    return 0.0f;
-  if (activation == 2u)
-    return gelu_tanh(v);
-  return v;
-}
+// ---- bias + activation (reference runtime/tensor.cpp:79-115; activation.cuh) ----
 __global__ void __launch_bounds__(256) bias_activation(const float *x, const float *bias, float *out,
                                                        uint64_t count, uint32_t columns,
                                                        uint32_t activation) {

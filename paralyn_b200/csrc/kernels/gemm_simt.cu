@@ -13,6 +13,7 @@
 // Blocks walk the output in groups of 8 tile-rows so consecutive blocks share B
 // in L2.
 #include "../runtime/builtin.hpp"
+#include "activation.cuh"
 #include <algorithm>
 
 namespace pb {
@@ -29,6 +30,9 @@ struct GemmArgs {
   // Batched launches (grid.z = batch): matrix z starts sa / sb / sc elements after
   // matrix z-1; C's column stride may differ from 1.
   int64_t sa = 0, sb = 0, sc = 0, c_col = 1;
+  // Fused epilogue: C = activate(fl(acc + bias[column])) (activation.cuh).
+  const float *bias = nullptr;
+  uint32_t activation = 0;
 };
 
 template <int MODE> __device__ __forceinline__ float mac(float acc, float a, float b) {
@@ -197,7 +201,13 @@ __global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs batch) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int64_t n = n0 + h * 64 + tx * 4;
-      const float *v = &acc[i][4 * h];
+      float v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
+      if (g.bias || g.activation) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < g.n)
+            v[j] = bias_activate(v[j], g.bias, n + j, g.activation);
+      }
       if (g.c_col != 1) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -260,18 +270,22 @@ bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
 } // namespace
 
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n,
-                        int64_t k, int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb);
+                        int64_t k, int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb,
+                        const float *bias = nullptr, uint32_t activation = 0);
 bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
                            int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
                            int64_t ldc, int64_t sc);
 
-// (a, b, c, m, n, k, transpose_a, transpose_b) with a 16x16 block per 16x16 output
-// tile: the grid bounds the computed region to min(m, 16*grid.y) x min(n, 16*grid.x).
-void launch_provider_matmul(Launch &L) {
+namespace {
+// C = op(A) op(B) over the grid-bounded region, optionally with the bias/activation
+// epilogue fused (bias: view of n values or absent; activation 0..2).
+void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
   const uint32_t m = L.args[3].u32(), n = L.args[4].u32(), k = L.args[5].u32();
   const uint32_t ta = L.args[6].u32(), tb = L.args[7].u32();
   if (ta > 1 || tb > 1)
     throw Failure(PR_INVALID_ARGUMENT, "Transpose flags must be 0 or 1");
+  if (activation > 2)
+    throw Failure(PR_INVALID_ARGUMENT, "Unknown activation");
   const int64_t me = std::min<int64_t>(m, int64_t(L.grid.y) * 16);
   const int64_t ne = std::min<int64_t>(n, int64_t(L.grid.x) * 16);
   if (!me || !ne) {
@@ -286,9 +300,13 @@ void launch_provider_matmul(Launch &L) {
     need_elements(L.args[1], b_need, "b");
   }
   need_elements(L.args[2], uint64_t(me - 1) * n + ne, "c");
+  if (bias_view)
+    need_elements(*bias_view, ne, "bias");
   if (L.dry_run)
     return;
   GemmArgs g;
+  g.bias = bias_view ? static_cast<const float *>(bias_view->ptr) : nullptr;
+  g.activation = activation;
   g.a = static_cast<const float *>(L.args[0].ptr);
   g.b = static_cast<const float *>(L.args[1].ptr);
   g.c = static_cast<float *>(L.args[2].ptr);
@@ -303,7 +321,7 @@ void launch_provider_matmul(Launch &L) {
   g.vec_c = aligned16(g.c) && g.ldc % 4 == 0;
   uint32_t mode = L.matmul_mode;
   if (mode == matmul_auto || mode == matmul_tf32x3) {
-    if (launch_tf32x3_gemm(L, g.a, g.b, g.c, me, ne, k, g.lda, g.ldb, g.ldc, ta, tb))
+    if (launch_tf32x3_gemm(L, g.a, g.b, g.c, me, ne, k, g.lda, g.ldb, g.ldc, ta, tb, g.bias, g.activation))
       return;
     mode = matmul_ffma;
   }
@@ -315,6 +333,19 @@ void launch_provider_matmul(Launch &L) {
     L.variant = "simt_ffma";
   }
   L.kernels = 1;
+}
+} // namespace
+
+// (a, b, c, m, n, k, transpose_a, transpose_b) with a 16x16 block per 16x16 output
+// tile: the grid bounds the computed region to min(m, 16*grid.y) x min(n, 16*grid.x).
+void launch_provider_matmul(Launch &L) { run_matmul(L, nullptr, 0); }
+
+// pr_b200_matmul_bias_activation_f32: (a, b, c, m, n, k, transpose_a, transpose_b,
+// bias or an empty view, activation, has_bias) -- the matmul launch with the
+// bias/activation epilogue fused. k == 0 runs the SIMT kernel (act(bias) everywhere).
+void launch_matmul_bias_activation(Launch &L) {
+  const bool has_bias = L.args[10].u32() != 0;
+  run_matmul(L, has_bias ? &L.args[8] : nullptr, L.args[9].u32());
 }
 
 namespace {

@@ -27,6 +27,7 @@
 //  records a status code in host-mapped memory, stops issuing, frees its TMEM and
 //  returns, and the engine reports PR_EXECUTION_FAILED.
 #include "../runtime/builtin.hpp"
+#include "activation.cuh"
 #include <cuda.h>
 #include <algorithm>
 
@@ -186,6 +187,9 @@ struct TileArgs {
   // `partials` (one 128x256 tile each) and are added by split_fixup.
   int units_total = 0, full_units = 0, split = 1;
   float *partials = nullptr;
+  // Fused epilogue: C = activate(fl(acc + bias[column])) (activation.cuh).
+  const float *bias = nullptr;
+  uint32_t activation = 0;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -541,6 +545,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int64_t first = col0 + col;
         if (first >= n_lim)
           break; // the remaining columns of the tile are past n
+        if (whole && (args.bias || args.activation)) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q)
+            if (first + q < n_lim)
+              v[q] = bias_activate(v[q], args.bias, first + q, args.activation);
+        }
 #pragma unroll
         for (int q = 0; q < 32; q += 4)
           *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH + q]) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
@@ -604,7 +614,7 @@ __global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
   float sum = p[0];
   for (int q = 1; q < args.split; ++q)
     sum = __fadd_rn(sum, p[int64_t(q) * (TM * TN)]);
-  args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = sum;
+  args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = bias_activate(sum, args.bias, col, args.activation);
 }
 
 // ---- host side ----
@@ -703,7 +713,8 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
 // Plans and enqueues the 3xTF32 GEMM; returns false (nothing enqueued) when the
 // shape is outside what this kernel covers or scratch is unavailable.
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
-                        int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb) {
+                        int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb, const float *bias,
+                        uint32_t activation) {
   if (k < 16 || m < 1 || n < 1)
     return false;
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n < 128 * 256))
@@ -736,6 +747,8 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi,
                                                                                     blo, k_pad, 0, n_pad);
   TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
+  t.bias = bias;
+  t.activation = activation;
   L.kernels = 3;
   launch_persistent(L, maps, t, tiles_m * tiles_n, plan, partials);
   L.variant = "tcgen05_tf32x3";

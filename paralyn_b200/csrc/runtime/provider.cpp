@@ -725,10 +725,11 @@ PB_EXPORT pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module oper
       const QueueAccess q = queue_access(queue);
       std::vector<BoundArg> args;
       std::vector<std::shared_ptr<Allocation>> retained;
-      auto view = [&](const pr_tensor_desc_v1 *d, const Layout &l) {
+      auto view = [&](const pr_tensor_desc_v1 *d, const Layout &l, bool writes = true) {
         auto allocation = buffer_allocation(d->buffer, q.context);
         BoundArg a;
         a.buffer = true;
+        a.writes = writes;
         a.ptr = static_cast<char *>(allocation->ptr) + d->byte_offset;
         a.bytes = l.bytes;
         args.push_back(a);
@@ -739,9 +740,9 @@ PB_EXPORT pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module oper
         a.bits = bits;
         args.push_back(a);
       };
-      view(op->x, x);
-      view(op->gamma, g);
-      view(op->beta, b);
+      view(op->x, x, false);
+      view(op->gamma, g, false);
+      view(op->beta, b, false);
       view(op->out, o);
       uint32_t eps_bits;
       std::memcpy(&eps_bits, &op->epsilon, 4);
@@ -755,6 +756,94 @@ PB_EXPORT pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module oper
         view(gathered[i], layouts[i]);
       *out = submit_command(queue, "b200_layer_norm_gather_f32", launch_layer_norm_gather,
                             Dim3{uint32_t(rows), 1, 1}, Dim3{256, 1, 1}, std::move(args), std::move(retained));
+    }));
+  });
+}
+
+namespace pb {
+void launch_matmul_bias_activation(Launch &);
+}
+
+// C = activation(op(A) op(B) + bias[column]) in one command: the matmul record and its
+// validation as pr_matmul_f32 (same order and statuses), plus an optional bias [n] and
+// the activation of pr_bias_activation_f32. Results equal pr_matmul_f32 followed by
+// pr_bias_activation_f32 bit for bit; C is written once.
+PB_EXPORT pr_status pr_b200_matmul_bias_activation_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
+                                                       const pr_tensor_desc_v1 *bias, uint32_t activation,
+                                                       pr_event *out) {
+  return boundary("matmul_bias_activation_f32", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    require(op, PR_INVALID_ARGUMENT, "Missing matmul record");
+    require(op->version == PR_TENSOR_VERSION_1, PR_UNSUPPORTED, "Unsupported matmul record version");
+    require(op->struct_size == sizeof(pr_matmul_v1), PR_INVALID_ARGUMENT, "Matmul record size mismatch");
+    require(op->transpose_a <= 1 && op->transpose_b <= 1, PR_INVALID_ARGUMENT,
+            "Transpose flags must be 0 or 1");
+    require(activation == PR_ACTIVATION_NONE || activation == PR_ACTIVATION_RELU ||
+                activation == PR_ACTIVATION_GELU_TANH,
+            PR_INVALID_ARGUMENT, "Unknown activation");
+    require(op->a && op->b && op->c, PR_INVALID_ARGUMENT, "Missing matmul tensor");
+    const Layout a = operand(op->a, "A", 2), b = operand(op->b, "B", 2), c = operand(op->c, "C", 2);
+    const uint64_t m = op->m, n = op->n, k = op->k;
+    require(m <= max_elements && n <= max_elements && k <= max_elements, PR_UNSUPPORTED,
+            "Matmul dimensions must not exceed INT32_MAX");
+    if (op->transpose_a)
+      expect_dims(op->a, "A (transposed storage [k,m])", {k, m});
+    else
+      expect_dims(op->a, "A [m,k]", {m, k});
+    if (op->transpose_b)
+      expect_dims(op->b, "B (transposed storage [n,k])", {n, k});
+    else
+      expect_dims(op->b, "B [k,n]", {k, n});
+    expect_dims(op->c, "C [m,n]", {m, n});
+    Layout bl;
+    if (bias) {
+      bl = operand(bias, "bias", 1);
+      expect_dims(bias, "bias", {n});
+    }
+    no_alias(op->c, c, op->a, a, "A");
+    no_alias(op->c, c, op->b, b, "B");
+    no_alias(op->c, c, bias, bl, "bias");
+    same_context(queue, operators, {{op->a, "A"}, {op->b, "B"}, {op->c, "C"}, {bias, "bias"}});
+    Owned fn;
+    kernel(operators, "paralyn_matmul_f32", fn);
+    if (!m || !n)
+      return; // no output elements: nothing is submitted and no event is invented
+    call(api("matmul_bias_activation_f32", [&] {
+      const QueueAccess q = queue_access(queue);
+      std::vector<BoundArg> args;
+      std::vector<std::shared_ptr<Allocation>> retained;
+      auto view = [&](const pr_tensor_desc_v1 *d, const Layout &l, bool writes) {
+        BoundArg arg;
+        arg.buffer = true;
+        arg.writes = writes;
+        if (d && l.bytes) {
+          auto allocation = buffer_allocation(d->buffer, q.context);
+          arg.ptr = static_cast<char *>(allocation->ptr) + d->byte_offset;
+          arg.bytes = l.bytes;
+          retained.push_back(std::move(allocation));
+        }
+        args.push_back(arg);
+      };
+      auto scalar = [&](uint64_t bits) {
+        BoundArg arg;
+        arg.bits = uint32_t(bits);
+        args.push_back(arg);
+      };
+      view(op->a, a, false);
+      view(op->b, b, false);
+      view(op->c, c, true);
+      scalar(m);
+      scalar(n);
+      scalar(k);
+      scalar(op->transpose_a);
+      scalar(op->transpose_b);
+      view(bias, bl, false);
+      scalar(activation);
+      scalar(bias ? 1 : 0);
+      *out = submit_command(queue, "b200_matmul_bias_activation_f32", launch_matmul_bias_activation,
+                            Dim3{uint32_t((n + tile - 1) / tile), uint32_t((m + tile - 1) / tile), 1},
+                            Dim3{tile, tile, 1}, std::move(args), std::move(retained));
     }));
   });
 }

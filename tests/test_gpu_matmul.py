@@ -149,3 +149,72 @@ def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
         assert np.all(np.abs(c[rows].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
     finally:
         p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+@pytest.mark.parametrize("mode", (p.MatmulMode.REFERENCE, p.MatmulMode.FFMA, p.MatmulMode.TF32X3, p.MatmulMode.AUTO))
+@pytest.mark.parametrize("m,n,k,ta,tb", [(129, 65, 257, False, False), (300, 260, 96, True, False),
+                                         (2432, 2048, 256, False, True), (64, 40, 0, False, False)])
+def test_fused_bias_activation_equals_two_commands(context, mode, m, n, k, ta, tb):
+    # One command (GEMM epilogue adds the bias and applies the activation) against
+    # pr_matmul_f32 followed by pr_bias_activation_f32: identical bits, every mode,
+    # including the split tail tiles (2432 x 2048) and k = 0.
+    p.set_matmul_mode(context, mode)
+    res = T.operators_of(context)
+    D = T.TensorDescriptor
+    try:
+        a = synthetic.uniform(900 + m, 0, m * k, 2.0)
+        b = synthetic.uniform(901 + n, 0, k * n, 2.0)
+        bias = synthetic.uniform(902, 0, n, 1.0)
+        bufs = [context.buffer(max(16, a.nbytes)), context.buffer(max(16, b.nbytes)), context.buffer(bias.nbytes),
+                context.buffer(4 * m * n), context.buffer(4 * m * n), context.buffer(4 * m * n)]
+        for buf, host in zip(bufs, (a, b, bias)):
+            if host.size:
+                buf.write(host)
+        da = D(bufs[0], (k, m) if ta else (m, k))
+        db = D(bufs[1], (n, k) if tb else (k, n))
+        dbias = D(bufs[2], (n,))
+        for activation in (p.Activation.NONE, p.Activation.RELU, p.Activation.GELU_TANH):
+            for with_bias in (True, False):
+                e1 = T.matmul_into(res.queue, res.module, da, db, D(bufs[3], (m, n)), m=m, n=n, k=k,
+                                   transpose_a=ta, transpose_b=tb)
+                e2 = T.bias_activation_into(res.queue, res.module, D(bufs[3], (m, n)), dbias if with_bias else None,
+                                            D(bufs[4], (m, n)), activation=activation)
+                e3 = p.b200.matmul_bias_activation_into(res.queue, res.module, da, db, D(bufs[5], (m, n)),
+                                                        dbias if with_bias else None, m=m, n=n, k=k, transpose_a=ta,
+                                                        transpose_b=tb, activation=activation)
+                e3.wait()
+                for e in (e1, e2, e3):
+                    e.close()
+                two = np.frombuffer(bufs[4].read(), np.float32)
+                one = np.frombuffer(bufs[5].read(), np.float32)
+                assert one.tobytes() == two.tobytes(), (mode, activation, with_bias)
+        for buf in bufs:
+            buf.close()
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+def test_fused_mlp_reproduces_the_golden_hash(context):
+    # The reference's MLP (docs/tensors-matmul.md:79) with both layers' bias (+ ReLU)
+    # fused into the GEMM: the published output SHA-256 in REFERENCE mode.
+    p.set_matmul_mode(context, p.MatmulMode.REFERENCE)
+    res = T.operators_of(context)
+    try:
+        x, w1, b1, w2, b2 = mlp_inputs()
+        with p.tensor(x, shape=(64, 257), context=context) as tx, p.tensor(w1, shape=(257, 130), context=context) as tw1, \
+                p.tensor(b1, shape=(130,), context=context) as tb1, p.tensor(w2, shape=(130, 11), context=context) as tw2, \
+                p.tensor(b2, shape=(11,), context=context) as tb2:
+            h, y = context.buffer(4 * 64 * 130), context.buffer(4 * 64 * 11)
+            D = T.TensorDescriptor
+            e1 = p.b200.matmul_bias_activation_into(res.queue, res.module, tx.descriptor(), tw1.descriptor(),
+                                                    D(h, (64, 130)), tb1.descriptor(), m=64, n=130, k=257,
+                                                    activation=p.Activation.RELU)
+            e2 = p.b200.matmul_bias_activation_into(res.queue, res.module, D(h, (64, 130)), tw2.descriptor(),
+                                                    D(y, (64, 11)), tb2.descriptor(), m=64, n=11, k=130)
+            e2.wait()
+            out = np.frombuffer(y.read(), np.float32)
+            for obj in (e1, e2, h, y):
+                obj.close()
+        assert hashlib.sha256(out.astype("<f4").tobytes()).hexdigest() == MLP_OUTPUT_SHA256
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)

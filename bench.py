@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--matmul-mode", default="auto", choices=("auto", "reference", "ffma", "tf32x3"),
+                    help="summation mode of the GEMM workloads (default auto: the 3xTF32 tensor-core kernel)")
     ap.add_argument("--gather", action="store_true",
                     help="chain: also gather Y on every GPU (LayerNorm writes its rows to all ranks over NVLink)")
     return ap.parse_args()
@@ -457,7 +459,11 @@ def run_ours(args, group):
     from paralyn_b200 import b200
     world = group.world
     ctx = p.Context(f"cuda:{group.local_rank}")
+    p.set_matmul_mode(ctx, {"auto": p.MatmulMode.AUTO, "reference": p.MatmulMode.REFERENCE,
+                            "ffma": p.MatmulMode.FFMA, "tf32x3": p.MatmulMode.TF32X3}[args.matmul_mode])
     w = Workload(args.workload, ctx, group, gather=args.gather)
+    if args.matmul_mode != "auto":
+        w.config["matmul_mode"] = args.matmul_mode
     # Sharded workloads shrink per GPU as N grows; keep the timed region near a second.
     steps = args.steps or DEFAULT_STEPS[args.workload] * (world if w.scaling == "strong" else 1)
     warm = []
@@ -502,6 +508,9 @@ def run_ours(args, group):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded SplitMix64 stream generated on device)",
             "config": w.config, "e2e": e2e, "gpu_launches": int(group.max(kernels)), "roofline": roofline,
             "clocks": clocks.summary(), "dominant_kernel_variant": variant, "headline_metric": METRIC}
+    mhz = line["clocks"].get("sm_mhz")
+    if roofline.get("bound") == "fp32_ffma" and mhz:  # the FFMA peak scales with the clock actually run
+        roofline["frac_at_median_sm_clock"] = round(roofline["achieved"] / (148 * 128 * 2 * mhz * 1e6 / 1e12), 4)
     if group.rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload)
     ctx.close()

@@ -128,7 +128,7 @@ template <bool TB> __device__ __forceinline__ void store_b(float (*sb)[BN], cons
 }
 
 template <int MODE, bool TA, bool TB>
-__global__ void __launch_bounds__(THREADS) gemm_simt(const GemmArgs batch) {
+__global__ void __launch_bounds__(THREADS, 2) gemm_simt(const GemmArgs batch) {
   GemmArgs g = batch;
   g.a += int64_t(blockIdx.z) * batch.sa;
   g.b += int64_t(blockIdx.z) * batch.sb;

@@ -64,12 +64,12 @@ __global__ void __launch_bounds__(256) elementwise_vec(const float *a, const flo
     float4 va[4], vb[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      va[u] = reads_a(OP) ? a4[i + u * stride] : zero;
-      vb[u] = reads_b(OP) ? b4[i + u * stride] : zero;
+      va[u] = reads_a(OP) ? __ldcs(a4 + i + u * stride) : zero; // streamed: read once
+      vb[u] = reads_b(OP) ? __ldcs(b4 + i + u * stride) : zero;
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      o4[i + u * stride] = apply4<OP>(va[u], vb[u], scale, c);
+      __stcs(o4 + i + u * stride, apply4<OP>(va[u], vb[u], scale, c));
   }
   for (; i < n4; i += stride)
     o4[i] = apply4<OP>(reads_a(OP) ? a4[i] : zero, reads_b(OP) ? b4[i] : zero, scale, c);

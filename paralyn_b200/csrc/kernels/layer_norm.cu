@@ -44,7 +44,7 @@ struct Gather {
 template <bool GATHER>
 __device__ __forceinline__ void store4(float *yr, const Gather &g, uint64_t row, uint32_t columns, uint32_t col,
                                        const float4 &y) {
-  *reinterpret_cast<float4 *>(yr + col) = y;
+  __stcs(reinterpret_cast<float4 *>(yr + col), y); // streamed: written once
   if constexpr (GATHER)
     for (uint32_t d = 0; d < g.count; ++d)
       *reinterpret_cast<float4 *>(g.dest[d] + (g.row_offset + row) * columns + col) = y;

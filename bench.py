@@ -16,6 +16,9 @@ benchmark configurations; one "step" is one pass of the path over one batch):
   reduce     row sums of x [65536 x 1024] ~ U[-4,4), seed 6 (replica per rank)
   attention  batched Q K^T: Q, K [32 heads, 2048, 128] ~ U[-1,1), seed 7, K^T as a strided view
              (replica per rank)
+  block      the reference example's pre-LN encoder block at T = 2048 tokens, d = 1024, 16 heads,
+             d_ff = 4096, causal, in 11 launches (bias and GELU fused into the GEMMs); value =
+             the block's GEMM flops per second (replica per rank)
 `value` is device time (CUDA events on the library's context stream between two
 queue markers, max over ranks); `e2e` times the same steps through the public API
 with pinned host inputs copied in and results copied out every step. Under
@@ -46,7 +49,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="chain",
-                    choices=("chain", "gemm", "layernorm", "affine", "add", "softmax", "reduce", "attention"))
+                    choices=("chain", "gemm", "layernorm", "affine", "add", "softmax", "reduce", "attention", "block"))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -60,7 +63,7 @@ def parse():
 # Sized so the timed region lasts about a second (the clock sampler needs several
 # 200 ms samples inside it).
 DEFAULT_STEPS = {"chain": 100, "gemm": 1500, "layernorm": 8000, "affine": 8000, "add": 20000, "softmax": 20000,
-                 "reduce": 20000, "attention": 5000}
+                 "reduce": 20000, "attention": 5000, "block": 1500}
 METRICS = {"chain": "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)",
            "gemm": "FP32 GEMM TFLOP/s (4096^3, rows sharded)",
            "layernorm": "FP32 row LayerNorm HBM GB/s (16384x4096, rows sharded)",
@@ -68,7 +71,8 @@ METRICS = {"chain": "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)",
            "add": "FP32 vector add HBM GB/s (n = 2^20)",
            "softmax": "FP32 causal row softmax HBM GB/s ([32, 1024, 1024])",
            "reduce": "FP32 row sum HBM GB/s (65536 x 1024)",
-           "attention": "FP32 batched matmul TFLOP/s (32 x 2048x2048x128, Q K^T)"}
+           "attention": "FP32 batched matmul TFLOP/s (32 x 2048x2048x128, Q K^T)",
+           "block": "FP32 encoder block GEMM TFLOP/s (T=2048, d=1024, 16 heads, d_ff=4096, causal)"}
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -313,6 +317,20 @@ class Workload:
             self.units_total = self.units_local * world
             self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
             self.metric = METRICS[name]
+        elif name == "block":
+            from paralyn_b200.block import EncoderBlock
+            self.block = EncoderBlock(ctx, 2048, 1024, 16, 4096, causal=True, seed=2026)
+            self.units_local = self.block.flops()
+            self.units_total = self.units_local * world
+            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "weak"
+            self.metric = METRICS[name]
+            self.config = {"workload": "block: pre-LN encoder block (reference examples/native/transformer_block), "
+                                       "T=2048, d=1024, 16 heads of 64, d_ff=4096, causal, seeded weights; 11 launches "
+                                       "per block (bias/GELU fused into the GEMM epilogues)",
+                           "tokens": 2048, "d_model": 1024, "heads": 16, "d_ff": 4096,
+                           "gemm_flops_per_block": self.units_local, "parallelism": f"replica{world}",
+                           "l2": "scores and probabilities 256 MiB each exceed L2"}
+            self.h2d = self.d2h = 4 * 2048 * 1024
         elif name == "attention":
             D = self.T.TensorDescriptor
             self.heads, self.seq, self.dh = 32, 2048, 128
@@ -363,6 +381,9 @@ class Workload:
                 e = self.T.reduce_rows_into(self.queue, self.res.module, D(self.x, self.shape),
                                             D(self.y, (self.shape[0],)))
             return [e], e
+        if self.name == "block":
+            events = self.block.run(fused=True)
+            return events, events[8]  # the MLP up-projection (+ bias + GELU), the largest GEMM
         if self.name == "attention":
             D = self.T.TensorDescriptor
             H, S, K = self.heads, self.seq, self.dh
@@ -409,7 +430,7 @@ class Workload:
                                                          D(self.y, (n_rows, self.cols), oo), epsilon=1e-5))
                 events.append(b200.read_async(self.queue, dst, host_out + oo, offset=oo, nbytes=4 * n_rows * width_out))
             return events
-        if self.name in ("softmax", "reduce", "attention"):  # one slice: upload, step, download
+        if self.name in ("softmax", "reduce", "attention", "block"):  # one slice: upload, step, download
             ins, (out, out_bytes) = self.io_buffers()
             for (buf, nbytes), host in zip(ins, host_in):
                 events.append(b200.write_async(self.queue, buf, host, nbytes=nbytes))
@@ -449,6 +470,8 @@ class Workload:
             return [(self.x, self.h2d)], (self.y, self.d2h)
         if self.name == "attention":
             return [(self.q, self.h2d // 2), (self.kmat, self.h2d // 2)], (self.c, self.d2h)
+        if self.name == "block":
+            return [(self.block.buf["x"], self.h2d)], (self.block.buf["out"], self.d2h)
         a, b, c = self.bufs[0][:3]
         return [(a, 4 * self.count), (b, 4 * self.count)], (c, self.d2h)
 
@@ -520,7 +543,7 @@ def run_ours(args, group):
 DOMINANT_ENTRY = {"chain": "paralyn_matmul_f32", "gemm": "paralyn_matmul_f32",
                   "layernorm": "paralyn_layer_norm_f32", "affine": "array_affine_scalar", "add": "array_add",
                   "softmax": "paralyn_softmax_rows_f32", "reduce": "paralyn_reduce_rows_f32",
-                  "attention": "paralyn_batched_matmul_f32"}
+                  "attention": "paralyn_batched_matmul_f32", "block": "b200_matmul_bias_activation_f32"}
 
 
 def last_variant(ctx, workload):
@@ -636,8 +659,12 @@ def roofline_for(w, seconds, variant, region_seconds):
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                 "peak_basis": f"{basis} STREAM-style copy"}
-    flops = w.units_local if w.name == "attention" else 2 * (
-        w.chain.local_rows if w.name == "chain" else w.m_local) * w.n * w.k
+    if w.name == "block":
+        flops = 2 * w.block.T * w.block.D * w.block.F  # the up-projection launch
+    elif w.name == "attention":
+        flops = w.units_local
+    else:
+        flops = 2 * (w.chain.local_rows if w.name == "chain" else w.m_local) * w.n * w.k
     achieved = flops / seconds / 1e12
     if variant and "tf32x3" in variant:
         sustained = region_seconds >= 0.5 and "bf16_tflops_sustained" in peaks
@@ -715,6 +742,20 @@ def cpu_sample(workload, budget_seconds):
         t = time.perf_counter() - t0
         per = 8 * x.size if workload == "softmax" else 4 * x.size + 4 * shape[0]
         return reps * per / t * 1e-9, "GB/s", f"{reps} passes over x {list(shape)}"
+    if workload == "block":  # the up-projection GEMM [T, 1024] x [1024, 4096] on a row sample
+        k, n = 1024, 4096
+        b = synthetic.uniform(7, 0, k * n, 0.125)
+        rows = max(8, oracle.threads())
+        while True:
+            a = synthetic.uniform(7, 1 << 30, rows * k)
+            t0 = time.perf_counter()
+            oracle.matmul(a, b, rows, n, k, threaded=True)
+            t = time.perf_counter() - t0
+            if t >= budget_seconds / 4 or rows >= 2048:
+                break
+            rows = min(2048, rows * 2)
+        return 2 * rows * n * k / t * 1e-12, "TFLOP/s", (f"{rows} rows of the MLP up-projection "
+                                                          "[T,1024]x[1024,4096] (sequential reference order)")
     if workload == "attention":
         S, K = 2048, 128
         q, kk = synthetic.uniform(7, 0, S * K), synthetic.uniform(7, 1, S * K)

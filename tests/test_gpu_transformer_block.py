@@ -218,3 +218,40 @@ def test_encoder_block_stage_local(context, tmp_path, causal):
 def _evidence(context, directory):
     context.write_evidence(str(directory))
     return (directory / "execution.json").read_text()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_library_block_fused_equals_fifteen_launches(context, causal):
+    # paralyn_b200.block.EncoderBlock: the 11-launch form (bias and GELU in the GEMM
+    # epilogues) writes exactly the bits of the reference's 15-launch sequence, at a
+    # size where the GEMMs run on the tensor-core kernel (AUTO mode).
+    from paralyn_b200.block import EncoderBlock
+    block = EncoderBlock(context, 384, 256, 4, 1024, causal=causal, seed=77)
+    try:
+        events = block.run()
+        assert len(events) == 15
+        events[-1].wait()
+        for e in events:
+            e.close()
+        names = ("qkv_b", "probs", "attn", "proj_b", "h1", "ff1_g", "ff2_b", "out")
+        want = {name: block.read(name) for name in names}
+        for name in names:
+            block.buf[name].write(np.full(int(np.prod(block.shapes[name])), np.nan, np.float32))
+        events = block.run(fused=True)
+        assert len(events) == 11
+        events[-1].wait()
+        for e in events:
+            e.close()
+        for name in names:
+            assert block.read(name).tobytes() == want[name].tobytes(), name
+        # stage-local check of the fused MLP up-projection against the oracle
+        ln2, w1, b1 = block.read("ln2"), block.read("w_1"), block.read("b_1")
+        value, _, magnitude = oracle.batched_dot_bound(ln2.ravel(), (0, (0, 256, 1)), w1.ravel(), (0, (0, 1024, 1)),
+                                                       1, 384, 1024, 256, magnitude=True)
+        ff1 = block.read("ff1_g")
+        pre = value.reshape(384, 1024) + b1[None, :]
+        assert np.all(np.isfinite(ff1))
+        assert np.all(np.abs(ff1 - 0.5 * pre * (1 + np.tanh(0.7978845608028654 * (pre + 0.044715 * pre ** 3))))
+                      <= 1e-4 * (1 + np.abs(pre)))
+    finally:
+        block.close()

@@ -42,6 +42,7 @@ class EncoderBlock:
             "attn": (T, D), "proj": (T, D), "proj_b": (T, D), "h1": (T, D), "ln2": (T, D), "ff1": (T, F),
             "ff1_g": (T, F), "ff2": (T, D), "ff2_b": (T, D), "out": (T, D)}
         self.buf = {name: context.buffer(4 * int(np.prod(shape))) for name, shape in self.shapes.items()}
+        self._descriptors = {}
         fills = {"x": (1.0, 0.0), "w_qkv": (0.125, 0.0), "w_o": (0.125, 0.0), "w_1": (0.125, 0.0),
                  "w_2": (0.0625, 0.0), "b_qkv": (0.25, 0.0), "b_o": (0.25, 0.0), "b_1": (0.25, 0.0),
                  "b_2": (0.25, 0.0), "beta1": (0.25, 0.0), "beta2": (0.25, 0.0)}
@@ -57,7 +58,12 @@ class EncoderBlock:
             self.buf[name].write(g.astype(np.float32))
 
     def d(self, name, shape=None, offset=0, strides=None):
-        return TensorDescriptor(self.buf[name], shape or self.shapes[name], offset, strides)
+        key = (name, shape, offset, strides)
+        desc = self._descriptors.get(key)
+        if desc is None:  # built once: repeated blocks reuse the descriptors and their records
+            desc = self._descriptors[key] = TensorDescriptor(self.buf[name], shape or self.shapes[name], offset,
+                                                             strides)
+        return desc
 
     def flops(self):
         """GEMM flops of one block (projections, scores, P V, MLP)."""

@@ -330,12 +330,12 @@ pr_event submit_locked(const std::shared_ptr<QueueObj> &queue, const std::string
 
 } // namespace
 
-pr_status api(const char *operation, const std::function<void()> &fn) noexcept {
+std::mutex &api_lock() noexcept { return api_mutex; }
+
+// Called from api()'s catch block: classifies the exception in flight.
+pr_status api_failure(const char *operation) noexcept {
   try {
-    std::lock_guard<std::mutex> lock(api_mutex);
-    fn();
-    last_error = {};
-    return PR_SUCCESS;
+    throw;
   } catch (const Failure &e) {
     last_error.code = e.status;
     text(last_error.message, e.what());

@@ -6,17 +6,33 @@
 #include "module.hpp"
 #include <functional>
 #include <memory>
+#include <mutex>
 
 namespace pb {
 
 enum class HandleKind { context, buffer, view, module, kernel, queue, event, collective };
 
+std::mutex &api_lock() noexcept;
+void clear_error() noexcept;
+// Records the exception being handled as (status, operation, message) in
+// pr_last_error; only valid inside a catch block.
+pr_status api_failure(const char *operation) noexcept;
+
 // Runs `fn` under the global API lock with the reference's error boundary:
 // success clears pr_last_error, a failure records (status, operation, message).
-pr_status api(const char *operation, const std::function<void()> &fn) noexcept;
+// A template, so the call costs no std::function allocation.
+template <class F> pr_status api(const char *operation, F &&fn) noexcept {
+  try {
+    std::lock_guard<std::mutex> lock(api_lock());
+    fn();
+    clear_error();
+    return PR_SUCCESS;
+  } catch (...) {
+    return api_failure(operation);
+  }
+}
 // Records a failure for `operation` without running anything (returns `code`).
 pr_status report_error(pr_status code, const char *operation, const std::string &message) noexcept;
-void clear_error() noexcept;
 // Records a failure from fixed strings without allocating (for entry points that
 // must not allocate); does not take the API lock or write the event log.
 pr_status set_error_fixed(pr_status code, const char *operation, const char *message) noexcept;

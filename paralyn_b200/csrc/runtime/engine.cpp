@@ -183,6 +183,15 @@ const Probe &probe() {
   return value;
 }
 
+// Makes room for `extra` more elements so that later push_backs cannot throw. The
+// capacity at least doubles: a plain reserve(size + 1) reallocates on every call,
+// which made each submission cost time in proportion to every launch recorded so far.
+template <class V> void reserve_more(V &v, size_t extra) {
+  const size_t need = v.size() + extra;
+  if (need > v.capacity())
+    v.reserve(std::max(need, 2 * v.capacity()));
+}
+
 uint64_t next_trace_id() {
   static std::atomic<uint64_t> next{1};
   return (uint64_t(2) << 32) | next.fetch_add(1);
@@ -669,8 +678,8 @@ std::shared_ptr<Work> Engine::submit(const std::string &name, Launcher launcher,
   launch.dry_run = true;
   launcher(launch); // validation: throws before anything is enqueued
   launch.dry_run = false;
-  pending_.reserve(pending_.size() + 1);
-  executions_.reserve(executions_.size() + pending_.size() + 1);
+  reserve_more(pending_, 1);
+  reserve_more(executions_, pending_.size() + 1);
   work->start = take_event();
   work->end = take_event();
   runtime_event("submission", "prepared", name, trace_id_, work->operation_id);
@@ -807,7 +816,7 @@ std::shared_ptr<Work> Engine::transfer(bool to_device, const std::shared_ptr<All
   access[0].writes = to_device;
   access[0].ptr = static_cast<char *>(allocation->ptr) + offset;
   access[0].bytes = bytes;
-  pending_.reserve(pending_.size() + 1);
+  reserve_more(pending_, 1);
   work->start = take_event();
   work->end = take_event();
   order_after(lane, access, false);

@@ -133,6 +133,16 @@ class TensorDescriptor:
     strides: object = None
 
     def _native(self):
+        # The record is built once per descriptor (descriptors are immutable) and
+        # rebuilt only to report a closed buffer the same way as the first time.
+        cached = self.__dict__.get("_record")
+        if cached is not None and not self.buffer.closed:
+            return cached
+        record = self._build_native()
+        object.__setattr__(self, "_record", record)
+        return record
+
+    def _build_native(self):
         lib = _api(self.buffer._lib)
         shape = tuple(self.shape)
         if len(shape) > MAX_RANK:

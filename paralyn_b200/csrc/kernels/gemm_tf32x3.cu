@@ -14,7 +14,9 @@
 //     [N_pad][K_pad] in the context workspace, K contiguous, zero padded (one read,
 //     two writes of each operand; a 32x32 shared-memory transpose for the
 //     transposed layouts).
-//  2. GEMM kernel, one 128x256 output tile per CTA, 6 warps:
+//  2. GEMM kernel (the one-tile form below serves the allocation-free entry point;
+//     the persistent form further down serves the tensor provider), one 128x256
+//     output tile per CTA, 6 warps:
 //     warp 0 lane 0: TMA producer. Each 16-deep k-slice is four 2-D boxes
 //       (A_hi, A_lo 128x16; B_hi, B_lo 256x16; 64-byte rows, SWIZZLE_64B) into a
 //       4-stage ring of 48 KB stages, signalled by mbarrier transaction counts.
@@ -361,25 +363,71 @@ __global__ void __launch_bounds__(THREADS, 1)
 // bank-conflict-free for 128-bit accesses by each quarter warp) and writes it
 // back with 128-bit stores, eight threads per 128-byte row segment, four rows per
 // instruction.
+// ---- persistent kernel ----
+// One CTA per SM walks work units (whole tiles, then k-ranges of the tiles of a
+// short last round). The N tile width BN is 64, 128 or 256 (the narrow tiles keep
+// the tensor cores off padding when n is small); every form uses a 192 KB ring of
+// 16-deep k-slices. With RAW_A the producer loads raw FP32 boxes of A and four
+// converter warps split them into the hi/lo pair in shared memory with the same
+// conversion as split_tf32 (so the operands, and the result, are bit-identical),
+// which saves the split pass over A when few column tiles re-read it.
 constexpr int EPI_PITCH = 36;
 constexpr int EPI_TILE_FLOATS = 32 * EPI_PITCH;
-constexpr int SMEM_BYTES_PERSISTENT = SMEM_BYTES + 4 * EPI_TILE_FLOATS * 4;
-__global__ void __launch_bounds__(THREADS, 1)
+constexpr int RING_BYTES = 192 * 1024, BARRIER_BYTES = 512;
+constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + 4 * EPI_TILE_FLOATS * 4;
+constexpr int STATUS_TIMEOUT_CONVERT = 0x7f3204;
+
+template <int BN> struct Tile {
+  static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
+  static constexpr int B_BYTES = BN * TK * 4;
+  static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES = RING_BYTES / STAGE; // 4, 6 or 8
+  static constexpr uint32_t COLUMNS = BN;            // TMEM columns of one accumulator
+  // D f32, A and B tf32, both K-major, N = BN, M = 128.
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(TM >> 4) << 24);
+};
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int BN>
+__device__ __forceinline__ void mma_tf32_n(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(Tile<BN>::IDESC), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ float4 tf32_hi(float4 v) {
+  return make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+}
+
+template <int BN, bool RAW_A>
+__global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
     gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                            const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                            const TileArgs args) {
+  using C = Tile<BN>;
+  constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-  uint64_t *empty = full + STAGES;
-  uint64_t *tmem_full = empty + STAGES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + RING_BYTES);
+  uint64_t *empty = full + S;
+  uint64_t *converted = empty + S; // RAW_A: the stage's A pair is in shared memory
+  uint64_t *tmem_full = converted + S;
   uint64_t *tmem_empty = tmem_full + 2;
   uint64_t *drained = tmem_empty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile int *issued = abort_flag + 1;   // k-slices the producer has requested
   volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received
-  float *epi_tiles = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + 256);
+  float *epi_tiles = reinterpret_cast<float *>(smem + RING_BYTES + BARRIER_BYTES);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
@@ -389,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int first_m = (id / per_group) * group;
     const int rows_in_group = min(group, args.tiles_m - first_m);
     m0 = (first_m + (id % per_group) % rows_in_group) * TM;
-    n0 = ((id % per_group) / rows_in_group) * TN;
+    n0 = ((id % per_group) / rows_in_group) * BN;
     a_y = z * args.a_rows + m0;
     b_y = z * args.b_rows + n0;
   };
@@ -408,9 +456,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&converted[s], 4);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
@@ -425,7 +474,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * TMEM_COLUMNS)
+                 "r"(2 * C::COLUMNS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -442,26 +491,32 @@ __global__ void __launch_bounds__(THREADS, 1)
         unit(u, tile, kb0, kb1);
         locate(tile, a_y, b_y, m0, n0, z);
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int s = g % STAGES;
-          const uint32_t round = g / STAGES;
-          if (g >= STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
+          const int s = g % S;
+          const uint32_t round = g / S;
+          if (g >= S && !mbar_wait(&empty[s], (round - 1) & 1)) {
             atomicExch(args.status, STATUS_TIMEOUT_PRODUCER);
             *abort_flag = 1;
           }
           if (*abort_flag)
             break;
-          uint8_t *stage = smem + s * STAGE_BYTES;
-          mbar_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_2d(stage, &a_hi, &full[s], kb * TK, a_y);
-          tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, a_y);
+          uint8_t *stage = smem + s * C::STAGE;
+          if (RAW_A) {
+            mbar_expect_tx(&full[s], A_BYTES + 2 * C::B_BYTES);
+            tma_load_3d(stage, &a_hi, &full[s], kb * TK, m0, z);
+          } else {
+            mbar_expect_tx(&full[s], C::STAGE);
+            tma_load_2d(stage, &a_hi, &full[s], kb * TK, a_y);
+            tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, a_y);
+          }
           tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, b_y);
-          tma_load_2d(stage + 2 * A_BYTES + B_BYTES, &b_lo, &full[s], kb * TK, b_y);
+          tma_load_2d(stage + 2 * A_BYTES + C::B_BYTES, &b_lo, &full[s], kb * TK, b_y);
           *issued = g + 1;
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) { // MMA issuer
+      uint64_t *ready = RAW_A ? converted : full;
       int g = 0, j = 0;
       for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x, ++j) {
         int tile, kb0, kb1;
@@ -473,10 +528,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS;
+        const uint32_t acc = tmem + uint32_t(b) * C::COLUMNS;
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int s = g % STAGES;
-          if (!mbar_wait(&full[s], (g / STAGES) & 1)) {
+          const int s = g % S;
+          if (!mbar_wait(&ready[s], (g / S) & 1)) {
             atomicExch(args.status, STATUS_TIMEOUT_MMA);
             *abort_flag = 1;
             break;
@@ -485,16 +540,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (*abort_flag)
             break;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t stage = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t stage = smem_u32(smem + s * C::STAGE);
 #pragma unroll
           for (int kk = 0; kk < TK / 8; ++kk) {
             const uint32_t step = kk * 32;
             const uint64_t ah = desc_k_sw64(stage + step), al = desc_k_sw64(stage + A_BYTES + step);
             const uint64_t bh = desc_k_sw64(stage + 2 * A_BYTES + step);
-            const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + B_BYTES + step);
-            mma_tf32(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
-            mma_tf32(acc, ah, bl, 1u);
-            mma_tf32(acc, al, bh, 1u);
+            const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + C::B_BYTES + step);
+            mma_tf32_n<BN>(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
+            mma_tf32_n<BN>(acc, ah, bl, 1u);
+            mma_tf32_n<BN>(acc, al, bh, 1u);
           }
           mma_commit(&empty[s]);
         }
@@ -504,6 +559,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // Fires once every MMA issued above has finished (TMEM quiet before it is freed).
       mma_commit(drained);
+    }
+  } else if (warp >= 6) { // RAW_A converter warps 6..9: raw A box -> hi in place, lo beside it
+    const int t = threadIdx.x - 192;
+    int g = 0;
+    for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x) {
+      int tile, kb0, kb1;
+      unit(u, tile, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb, ++g) {
+        const int s = g % S;
+        if (!mbar_wait(&full[s], (g / S) & 1)) {
+          atomicExch(args.status, STATUS_TIMEOUT_CONVERT);
+          *abort_flag = 1;
+        }
+        if (*abort_flag)
+          break;
+        float4 *hi = reinterpret_cast<float4 *>(smem + s * C::STAGE);
+        float4 *lo = reinterpret_cast<float4 *>(smem + s * C::STAGE + A_BYTES);
+        // The swizzle is the same for both boxes, so the pair is formed position by position.
+#pragma unroll
+        for (int i = 0; i < A_BYTES / 16 / 128; ++i) {
+          const float4 v = hi[t + 128 * i];
+          const float4 h = tf32_hi(v);
+          lo[t + 128 * i] = tf32_hi(make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
+          hi[t + 128 * i] = h;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // visible to the tensor cores
+        __syncwarp();
+        if (lane == 0)
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&converted[s])) : "memory");
+      }
     }
   } else { // epilogue warps 2..5: TMEM lanes 32*(warp % 4) ..
     const int sub = warp % 4;
@@ -526,20 +611,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       int a_y, b_y, m0, n0, z;
       locate(tile, a_y, b_y, m0, n0, z);
       // Whole tiles go to C; the k-range parts of split tiles go to their own
-      // 128x256 partial tile (row stride 256), all of it written.
+      // 128 x BN partial tile (row stride BN), all of it written.
       const bool whole = u < args.full_units;
       float *const c_base = whole ? args.c + int64_t(z) * args.c_batch
-                                  : args.partials + int64_t(u - args.full_units) * (TM * TN);
-      const int64_t ldc = whole ? args.ldc : TN, m_lim = whole ? args.m : TM, n_lim = whole ? args.n : TN;
+                                  : args.partials + int64_t(u - args.full_units) * (TM * BN);
+      const int64_t ldc = whole ? args.ldc : BN, m_lim = whole ? args.m : TM, n_lim = whole ? args.n : BN;
       const int64_t row0 = (whole ? int64_t(m0) : 0) + 32 * sub; // this warp's 32 rows
       const int64_t col0 = whole ? int64_t(n0) : 0;
       const int64_t left = m_lim - row0;
       const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
       float *tile_s = epi_tiles + sub * EPI_TILE_FLOATS;
-      const uint32_t acc = tmem + uint32_t(b) * TMEM_COLUMNS + (uint32_t(32 * sub) << 16);
+      const uint32_t acc = tmem + uint32_t(b) * C::COLUMNS + (uint32_t(32 * sub) << 16);
       const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
-      for (int col = 0; col < TN; col += 32) {
+      for (int col = 0; col < BN; col += 32) {
         float v[32];
         tmem_load_32(acc + uint32_t(col), v); // thread = row 32*sub + lane, 32 columns
         const int64_t first = col0 + col;
@@ -586,20 +671,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     if (*abort_flag) // copies requested but never consumed must land before shared memory is released
       for (int g = *consumed; g < *issued; ++g)
-        (void)mbar_wait(&full[g % STAGES], (g / STAGES) & 1);
+        (void)mbar_wait(&full[g % S], (g / S) & 1);
     (void)mbar_wait(drained, 0); // bounded: every MMA has finished writing TMEM
   }
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TMEM_COLUMNS)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * C::COLUMNS)
                  : "memory");
   }
 }
 
 // C of every split tile = its partial tiles added in k order (one thread per
-// element, 256 columns per block, one block per tile row).
-__global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
+// element, BN columns per block, one block per tile row).
+template <int BN> __global__ void __launch_bounds__(BN) split_fixup(const TileArgs args) {
   const int t = blockIdx.y, i = blockIdx.x, j = threadIdx.x; // remaining tile, row, column in tile
   const int tile = args.full_units + t;
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
@@ -607,13 +692,13 @@ __global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
   const int first_m = (id / per_group) * group;
   const int rows_in_group = min(group, args.tiles_m - first_m);
   const int64_t row = int64_t(first_m + (id % per_group) % rows_in_group) * TM + i;
-  const int64_t col = int64_t((id % per_group) / rows_in_group) * TN + j;
+  const int64_t col = int64_t((id % per_group) / rows_in_group) * BN + j;
   if (row >= args.m || col >= args.n)
     return;
-  const float *p = args.partials + int64_t(t) * args.split * (TM * TN) + i * TN + j;
+  const float *p = args.partials + int64_t(t) * args.split * (TM * BN) + i * BN + j;
   float sum = p[0];
   for (int q = 1; q < args.split; ++q)
-    sum = __fadd_rn(sum, p[int64_t(q) * (TM * TN)]);
+    sum = __fadd_rn(sum, p[int64_t(q) * (TM * BN)]);
   args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = bias_activate(sum, args.bias, col, args.activation);
 }
 
@@ -650,18 +735,33 @@ bool make_map(CUtensorMap *map, float *base, int64_t rows_pad, int64_t k_pad, ui
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Raw A as a [batch][m][k] box source (k contiguous, row stride lda, matrix stride
+// sa, all in elements): boxes of 128 rows x 16 k, zero outside the matrix, so the
+// k tail and the rows past m read as the zero padding of the split path.
+bool make_raw_map(CUtensorMap *map, const float *a, int64_t batch, int64_t m, int64_t k, int64_t lda, int64_t sa) {
+  const EncodeTiled encode = encoder();
+  if (!encode)
+    return false;
+  const cuuint64_t dims[3] = {cuuint64_t(k), cuuint64_t(m), cuuint64_t(batch)};
+  const cuuint64_t strides[2] = {cuuint64_t(lda) * 4, cuuint64_t(sa) * 4};
+  const cuuint32_t box[3] = {TK, TM, 1};
+  const cuuint32_t element[3] = {1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(a), dims, strides, box, element,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int64_t round_up(int64_t v, int64_t to) { return (v + to - 1) / to * to; }
 
-// Shared-memory limit of the persistent kernel, set once per device (the
+// Shared-memory limit of one persistent-kernel form, set once per device (the
 // attribute belongs to the device's context).
-bool configure_persistent(int device) {
+template <int BN, bool RAW_A> bool configure_persistent(int device) {
   static bool configured[64] = {};
   if (device < 0 || device >= 64)
     return false;
   if (!configured[device]) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES_PERSISTENT) !=
-        cudaSuccess) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_persistent<BN, RAW_A>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES_PERSISTENT) != cudaSuccess) {
       cudaGetLastError();
       return false;
     }
@@ -670,29 +770,31 @@ bool configure_persistent(int device) {
   return true;
 }
 
-// Work units of the persistent kernel. With G CTAs, tiles = R*G + r: when the last
-// round would keep fewer than half of the SMs busy, its r tiles are cut into
-// s = min(G / r, 4) k-ranges so that round ends about s times sooner.
+// Work units of the persistent kernel. With G = SM count, tiles = R*G + r: when the
+// last (or only) round would keep at most half of the SMs busy, its r tiles are cut
+// into s = min(G / r, 4) k-ranges so that round ends about s times sooner.
 struct UnitPlan {
   int ctas, full_units, split, units, remaining;
   size_t partial_bytes;
 };
-UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks) {
+UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks, int bn) {
   UnitPlan p{};
-  p.ctas = int(std::min<int64_t>(tiles, std::max(1, sm_count)));
-  const int64_t r = tiles % p.ctas;
+  const int64_t g = std::max(1, sm_count);
+  const int64_t r = tiles % g;
   p.split = 1;
-  if (r > 0 && 2 * r <= p.ctas)
-    p.split = int(std::min<int64_t>({p.ctas / r, 4, k_blocks / 2}));
+  if (r > 0 && 2 * r <= g)
+    p.split = int(std::min<int64_t>({g / r, 4, k_blocks / 2}));
   if (p.split < 2)
     p.split = 1;
   p.remaining = p.split > 1 ? int(r) : 0;
   p.full_units = int(tiles - p.remaining);
   p.units = p.full_units + p.remaining * p.split;
-  p.partial_bytes = size_t(p.remaining) * p.split * TM * TN * sizeof(float);
+  p.ctas = int(std::min<int64_t>(p.units, g));
+  p.partial_bytes = size_t(p.remaining) * p.split * TM * bn * sizeof(float);
   return p;
 }
 
+template <int BN, bool RAW_A>
 void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
                        float *partials) {
   t.tiles_total = int(tiles);
@@ -700,12 +802,111 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
   t.full_units = plan.full_units;
   t.split = plan.split;
   t.partials = partials;
-  gemm_tf32x3_persistent<<<uint32_t(plan.ctas), THREADS, SMEM_BYTES_PERSISTENT, L.stream>>>(maps[0], maps[1],
-                                                                                            maps[2], maps[3], t);
+  gemm_tf32x3_persistent<BN, RAW_A><<<uint32_t(plan.ctas), RAW_A ? 320 : 192, SMEM_BYTES_PERSISTENT, L.stream>>>(
+      maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
-    split_fixup<<<dim3(TM, uint32_t(plan.remaining)), TN, 0, L.stream>>>(t);
+    split_fixup<BN><<<dim3(TM, uint32_t(plan.remaining)), BN, 0, L.stream>>>(t);
     ++L.kernels;
   }
+}
+
+// The six kernel forms: N tile width x (A split in shared memory or by the split pass).
+bool configure_form(int bn, bool raw_a, int device) {
+  switch (bn * 2 + (raw_a ? 1 : 0)) {
+  case 128: return configure_persistent<64, false>(device);
+  case 129: return configure_persistent<64, true>(device);
+  case 256: return configure_persistent<128, false>(device);
+  case 257: return configure_persistent<128, true>(device);
+  case 512: return configure_persistent<256, false>(device);
+  case 513: return configure_persistent<256, true>(device);
+  }
+  return false;
+}
+void launch_form(int bn, bool raw_a, Launch &L, const CUtensorMap (&maps)[4], const TileArgs &t, int64_t tiles,
+                 const UnitPlan &plan, float *partials) {
+  switch (bn * 2 + (raw_a ? 1 : 0)) {
+  case 128: return launch_persistent<64, false>(L, maps, t, tiles, plan, partials);
+  case 129: return launch_persistent<64, true>(L, maps, t, tiles, plan, partials);
+  case 256: return launch_persistent<128, false>(L, maps, t, tiles, plan, partials);
+  case 257: return launch_persistent<128, true>(L, maps, t, tiles, plan, partials);
+  case 512: return launch_persistent<256, false>(L, maps, t, tiles, plan, partials);
+  default: return launch_persistent<256, true>(L, maps, t, tiles, plan, partials);
+  }
+}
+
+// N tile width for n columns: the narrowest of 64 / 128 / 256 that holds them, else 256.
+int tile_width(int64_t n) { return n <= 64 ? 64 : (n <= 128 ? 128 : 256); }
+
+// Raw A boxes need A stored [m][k] (k contiguous) with 16-byte aligned rows and
+// matrices; they pay off when few column tiles re-read A (each re-read converts
+// again, while the split pass converts once).
+// (sa is the matrix stride; matrices must not overlap.)
+bool raw_a_fits(const float *a, bool ta, int64_t m, int64_t lda, int64_t batch, int64_t sa, int64_t tiles_n) {
+  return !ta && tiles_n <= 2 && (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && lda % 4 == 0 && sa % 4 == 0 &&
+         sa >= m * lda && lda <= (int64_t(1) << 36) && sa <= (int64_t(1) << 36) && batch >= 1;
+}
+
+// Plans and enqueues C[z] = op(A[z]) op(B[z]) for z < batch (see the launchers below).
+bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m, int64_t n,
+                   int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb, int64_t ldc,
+                   int64_t sc, const float *bias, uint32_t activation) {
+  if (!encoder() || !L.workspace)
+    return false;
+  const int bn = tile_width(n);
+  const int64_t k_pad = round_up(k, 32), m_pad = round_up(m, TM), n_pad = round_up(n, bn);
+  const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / bn, batch_b = sb ? batch : 1;
+  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 ||
+      n_pad / 32 > 65535 || batch * m_pad > INT32_MAX || batch_b * n_pad > INT32_MAX)
+    return false; // grid limits and 32-bit TMA row coordinates
+  if (batch == 1)
+    sa = m * lda;
+  const bool raw_a = raw_a_fits(a, ta, m, lda, batch, sa, tiles_n);
+  const UnitPlan plan = plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn);
+  const int64_t a_split_rows = raw_a ? 0 : batch * m_pad;
+  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_split_rows + batch_b * n_pad);
+  const size_t bytes = split_bytes + plan.partial_bytes;
+  if (L.dry_run)
+    return true;
+  auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
+  if (!scratch)
+    return false;
+  float *partials = scratch + split_bytes / sizeof(float);
+  float *ahi = scratch, *alo = ahi + a_split_rows * k_pad, *bhi = alo + a_split_rows * k_pad,
+        *blo = bhi + batch_b * n_pad * k_pad;
+  CUtensorMap maps[4];
+  if (raw_a) {
+    if (!make_raw_map(&maps[0], a, batch, m, k, lda, sa))
+      return false;
+    maps[1] = maps[0]; // unused
+  } else if (!make_map(&maps[0], ahi, batch * m_pad, k_pad, TM) || !make_map(&maps[1], alo, batch * m_pad, k_pad, TM)) {
+    return false;
+  }
+  if (!make_map(&maps[2], bhi, batch_b * n_pad, k_pad, uint32_t(bn)) ||
+      !make_map(&maps[3], blo, batch_b * n_pad, k_pad, uint32_t(bn)))
+    return false;
+  if (!configure_form(bn, raw_a, L.device))
+    return false;
+  // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
+  if (!raw_a) {
+    split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
+        a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, m_pad);
+    ++L.kernels;
+  }
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
+      b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, n_pad);
+  ++L.kernels;
+  TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
+  if (batch > 1) {
+    t.tiles_per_batch = int(tiles_m * tiles_n);
+    t.a_rows = int(m_pad);
+    t.b_rows = sb ? int(n_pad) : 0;
+    t.c_batch = sc;
+  }
+  t.bias = bias;
+  t.activation = activation;
+  ++L.kernels;
+  launch_form(bn, raw_a, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
+  return true;
 }
 
 } // namespace
@@ -719,38 +920,9 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
     return false;
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n < 128 * 256))
     return false;
-  if (!encoder() || !L.workspace)
+  L.kernels = 0;
+  if (!launch_tf32x3(L, a, b, c, 1, m, n, k, lda, ta, 0, ldb, tb, 0, ldc, 0, bias, activation))
     return false;
-  const int64_t k_pad = round_up(k, 32), m_pad = round_up(m, TM), n_pad = round_up(n, TN);
-  const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / TN;
-  if (tiles_m * tiles_n > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 || n_pad / 32 > 65535)
-    return false; // split-kernel grid.y limit
-  const UnitPlan plan = plan_units(tiles_m * tiles_n, L.sm_count, int(k_pad / TK));
-  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(m_pad + n_pad);
-  const size_t bytes = split_bytes + plan.partial_bytes;
-  if (L.dry_run)
-    return true;
-  auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
-  if (!scratch)
-    return false;
-  float *ahi = scratch, *alo = ahi + m_pad * k_pad, *bhi = alo + m_pad * k_pad, *blo = bhi + n_pad * k_pad;
-  float *partials = scratch + split_bytes / sizeof(float);
-  CUtensorMap maps[4];
-  if (!make_map(&maps[0], ahi, m_pad, k_pad, TM) || !make_map(&maps[1], alo, m_pad, k_pad, TM) ||
-      !make_map(&maps[2], bhi, n_pad, k_pad, TN) || !make_map(&maps[3], blo, n_pad, k_pad, TN))
-    return false;
-  if (!configure_persistent(L.device))
-    return false;
-  // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
-  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi,
-                                                                                    alo, k_pad, 0, m_pad);
-  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi,
-                                                                                    blo, k_pad, 0, n_pad);
-  TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
-  t.bias = bias;
-  t.activation = activation;
-  L.kernels = 3;
-  launch_persistent(L, maps, t, tiles_m * tiles_n, plan, partials);
   L.variant = "tcgen05_tf32x3";
   return true;
 }
@@ -758,7 +930,7 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
 // Batched form: C[z] = op(A[z]) op(B[z]) for z < batch, matrix z of A at a + z*sa,
 // of B at b + z*sb (sb = 0: one B shared by all), of C at c + z*sc (row stride
 // ldc, column stride 1). Same split and GEMM kernels with a batch grid dimension
-// (split) and batch-major CTA numbering (GEMM); the split operands of all
+// (split) and batch-major tile numbering (GEMM); the split operands of all
 // matrices are stacked row-wise, so no tile crosses a matrix boundary.
 bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
                            int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
@@ -767,41 +939,9 @@ bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, 
     return false;
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n * batch < 128 * 256 * 4))
     return false;
-  if (!encoder() || !L.workspace)
+  L.kernels = 0;
+  if (!launch_tf32x3(L, a, b, c, batch, m, n, k, lda, ta, sa, ldb, tb, sb, ldc, sc, nullptr, 0))
     return false;
-  const int64_t k_pad = round_up(k, 32), m_pad = round_up(m, TM), n_pad = round_up(n, TN);
-  const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / TN, batch_b = sb ? batch : 1;
-  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 ||
-      n_pad / 32 > 65535 || batch * m_pad > INT32_MAX || batch_b * n_pad > INT32_MAX)
-    return false; // grid limits and 32-bit TMA row coordinates
-  const UnitPlan plan = plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK));
-  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(batch * m_pad + batch_b * n_pad);
-  const size_t bytes = split_bytes + plan.partial_bytes;
-  if (L.dry_run)
-    return true;
-  auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
-  if (!scratch)
-    return false;
-  float *partials = scratch + split_bytes / sizeof(float);
-  float *ahi = scratch, *alo = ahi + batch * m_pad * k_pad, *bhi = alo + batch * m_pad * k_pad,
-        *blo = bhi + batch_b * n_pad * k_pad;
-  CUtensorMap maps[4];
-  if (!make_map(&maps[0], ahi, batch * m_pad, k_pad, TM) || !make_map(&maps[1], alo, batch * m_pad, k_pad, TM) ||
-      !make_map(&maps[2], bhi, batch_b * n_pad, k_pad, TN) || !make_map(&maps[3], blo, batch_b * n_pad, k_pad, TN))
-    return false;
-  if (!configure_persistent(L.device))
-    return false;
-  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
-      a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, m_pad);
-  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
-      b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, n_pad);
-  TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
-  t.tiles_per_batch = int(tiles_m * tiles_n);
-  t.a_rows = int(m_pad);
-  t.b_rows = sb ? int(n_pad) : 0;
-  t.c_batch = sc;
-  L.kernels = 3;
-  launch_persistent(L, maps, t, tiles_m * tiles_n * batch, plan, partials);
   L.variant = "batched_tcgen05_tf32x3";
   return true;
 }

@@ -132,11 +132,13 @@ def test_matmul_validation(context):
     buf.close()
 
 
-@pytest.mark.parametrize("m,n,k", [(2432, 2048, 1024), (4096, 4096, 256), (4096, 4096, 40), (128 * 150, 256, 96)])
+@pytest.mark.parametrize("m,n,k", [(2432, 2048, 1024), (4096, 4096, 256), (4096, 4096, 40), (128 * 150, 256, 96),
+                                   (2048, 1024, 1024), (512, 512, 512), (1000, 60, 4000)])
 def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
-    # Tile counts just above a multiple of the 148 persistent CTAs: the tiles of the
-    # last, mostly idle round are cut into k-ranges whose partial sums are added by a
-    # second kernel. Rows sampled from every tile row, all columns checked.
+    # Tile counts just above a multiple of the 148 persistent CTAs, or below it: the
+    # tiles of the last (or only), mostly idle round are cut into k-ranges whose
+    # partial sums are added by a second kernel. Rows sampled from every tile row,
+    # all columns checked.
     p.set_matmul_mode(context, p.MatmulMode.TF32X3)
     try:
         a = synthetic.uniform(7000 + k, 0, m * k)
@@ -216,5 +218,43 @@ def test_fused_mlp_reproduces_the_golden_hash(context):
             for obj in (e1, e2, h, y):
                 obj.close()
         assert hashlib.sha256(out.astype("<f4").tobytes()).hexdigest() == MLP_OUTPUT_SHA256
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+def aligned_matmul(context, a, b, m, n, k, ta):
+    """C = op(A) B with every operand at byte offset 0 (16-byte aligned rows when k % 4 == 0)."""
+    res = T.operators_of(context)
+    bufs = [context.buffer(4 * x.size) for x in (a, b)] + [context.buffer(4 * m * n)]
+    try:
+        bufs[0].write(np.ascontiguousarray(a.T if ta else a).ravel())
+        bufs[1].write(b.ravel())
+        event = T.matmul_into(res.queue, res.module, T.TensorDescriptor(bufs[0], (k, m) if ta else (m, k)),
+                              T.TensorDescriptor(bufs[1], (k, n)), T.TensorDescriptor(bufs[2], (m, n)),
+                              m=m, n=n, k=k, transpose_a=ta)
+        event.wait()
+        event.close()
+        return np.frombuffer(bufs[2].read(), np.float32).reshape(m, n).copy()
+    finally:
+        for buf in bufs:
+            buf.close()
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 16), (16, 16, 16), (129, 65, 260), (257, 100, 96), (300, 129, 64),
+                                   (2048, 64, 2048), (1000, 512, 100), (4096, 200, 1024)])
+def test_a_split_in_shared_memory_equals_the_split_pass(context, m, n, k):
+    # A stored [m, k] with 16-byte aligned rows, re-read by at most two column tiles, is
+    # loaded raw and split into its TF32 pair inside the GEMM kernel; stored [k, m] it
+    # goes through the separate split pass. Same conversion, same order: equal bits.
+    p.set_matmul_mode(context, p.MatmulMode.TF32X3)
+    try:
+        a = synthetic.uniform(9100 + m, 0, m * k).reshape(m, k)
+        b = synthetic.uniform(9200 + n, 0, k * n).reshape(k, n)
+        raw = aligned_matmul(context, a, b, m, n, k, False)
+        split = aligned_matmul(context, a, b, m, n, k, True)
+        assert raw.tobytes() == split.tobytes()
+        rows = np.unique(np.concatenate([np.arange(0, m, 97), [m - 1]]))
+        exact, magnitude = oracle.matmul_exact(a[rows].ravel(), b.ravel(), len(rows), n, k)
+        assert np.all(np.abs(raw[rows].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
     finally:
         p.set_matmul_mode(context, p.MatmulMode.AUTO)

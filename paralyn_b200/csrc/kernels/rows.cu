@@ -22,9 +22,10 @@
 // 256i + 128 + 4L of chunk i. The tree then runs w = 128 inside the thread,
 // w = 64..4 as shuffles with thread L + 16..1 and w = 2, 1 inside the thread.
 //   reduce_warp_rows     streams chunks (any column count), 8 rows per block
-//   softmax_warp_rows<R> keeps the row in registers (columns <= 256 R, R <= 8),
+//   softmax_warp_rows<R> keeps the row in registers (columns <= 256 R, R <= 4),
 //                        skips masked columns and takes the row maximum with
 //                        max.NaN (same softmax values; see max_nan)
+//   softmax_stream_rows  longer rows: the same arithmetic over three passes
 // Other rows take one 256-thread block per row with thread t = lane t.
 #include "../runtime/builtin.hpp"
 #include <algorithm>
@@ -260,6 +261,105 @@ __global__ void __launch_bounds__(256, R <= 4 ? 3 : 1) softmax_warp_rows(const f
     }
 }
 
+// Long rows streamed three times (maximum, sum, output), 8 rows per block and two
+// chunks of loads in flight per pass: a few registers per thread keep 64 warps on
+// an SM, and the second and third reads of a row mostly hit L2. Same operations in
+// the same order as softmax_warp_rows, so the same bits.
+__device__ __forceinline__ float4 load_group(const float *p, bool last_use) {
+  const float4 *q = reinterpret_cast<const float4 *>(p);
+  return last_use ? __ldcs(q) : __ldcg(q);
+}
+
+__global__ void __launch_bounds__(256) softmax_stream_rows(const float *__restrict__ x, float *__restrict__ out,
+                                                           uint32_t all_rows, uint32_t rows, uint32_t columns,
+                                                           uint32_t causal, float scale) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t row = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= all_rows)
+    return;
+  const float *xr = x + row * columns;
+  float *yr = out + row * columns;
+  const uint32_t visible = visible_columns(row, rows, columns, causal != 0);
+  const uint32_t chunks = (visible + 255) / 256; // chunks holding a visible column
+  float s[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    s[c] = MaxValue::identity();
+  for (uint32_t i = 0; i < chunks; i += 2) {
+    float4 q[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t col = 256u * (i + u) + 128u * h + 4u * lane;
+        q[u][h] = col < visible ? load_group(xr + col, false) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t col = 256u * (i + u) + 128u * h + 4u * lane;
+        float v[4];
+        unpack(q[u][h], v);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (col + c < visible)
+            s[4 * h + c] = MaxValue::apply(s[4 * h + c], __fmul_rn(scale, v[c]));
+      }
+  }
+  const float m = warp_tree<MaxValue>(s);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    s[c] = 0.0f;
+  for (uint32_t i = 0; i < chunks; i += 2) {
+    float4 q[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t col = 256u * (i + u) + 128u * h + 4u * lane;
+        q[u][h] = col < visible ? load_group(xr + col, false) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t col = 256u * (i + u) + 128u * h + 4u * lane;
+        float v[4];
+        unpack(q[u][h], v);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (col + c < visible)
+            s[4 * h + c] = __fadd_rn(s[4 * h + c], expf(__fsub_rn(__fmul_rn(scale, v[c]), m)));
+      }
+  }
+  const float rinv = __frcp_rn(warp_tree<Sum>(s));
+  for (uint32_t i = 0; 256u * i < columns; i += 2) {
+    float4 q[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t col = 256u * (i + u) + 128u * h + 4u * lane;
+        q[u][h] = col < visible ? load_group(xr + col, true) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t col = 256u * (i + u) + 128u * h + 4u * lane;
+        if (col < columns) {
+          float v[4], y[4];
+          unpack(q[u][h], v);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            y[c] = col + c < visible ? __fmul_rn(expf(__fsub_rn(__fmul_rn(scale, v[c]), m)), rinv) : 0.0f;
+          __stcs(reinterpret_cast<float4 *>(yr + col), make_float4(y[0], y[1], y[2], y[3]));
+        }
+      }
+  }
+}
+
 __global__ void __launch_bounds__(256) softmax_block_rows(const float *x, float *out, uint32_t rows,
                                                           uint32_t columns, uint32_t causal, float scale) {
   __shared__ float scratch[256];
@@ -342,7 +442,7 @@ void launch_provider_softmax_rows(Launch &L) {
   const auto *x = static_cast<const float *>(L.args[0].ptr);
   auto *y = static_cast<float *>(L.args[1].ptr);
   L.kernels = 1;
-  if (aligned16(x) && aligned16(y) && columns % 4 == 0 && columns <= 2048) {
+  if (aligned16(x) && aligned16(y) && columns % 4 == 0) {
     const uint32_t chunks = (columns + 255) / 256;
     if (chunks <= 1)
       launch_softmax_warp<1>(L, x, y, all_rows, rows, columns, causal, scale);
@@ -350,8 +450,10 @@ void launch_provider_softmax_rows(Launch &L) {
       launch_softmax_warp<2>(L, x, y, all_rows, rows, columns, causal, scale);
     else if (chunks <= 4)
       launch_softmax_warp<4>(L, x, y, all_rows, rows, columns, causal, scale);
-    else
-      launch_softmax_warp<8>(L, x, y, all_rows, rows, columns, causal, scale);
+    else {
+      softmax_stream_rows<<<(all_rows + 7) / 8, 256, 0, L.stream>>>(x, y, all_rows, rows, columns, causal, scale);
+      L.variant = "softmax_stream_rows";
+    }
     return;
   }
   softmax_block_rows<<<all_rows, 256, 0, L.stream>>>(x, y, rows, columns, causal, scale);

@@ -220,7 +220,8 @@ SOFTMAX_CASES = [(1, 1, 1, 1.0, 4.0, False, False), (1, 3, 17, 1.0, 4.0, False, 
                  (2, 5, 12, 1.0, 8.0, True, True), (3, 7, 7, 3.0, 4.0, False, True), (1, 1, 300, 1.0, 100.0, True, False),
                  (1, 17, 17, 1.0, 60.0, True, False), (1, 0, 5, 1.0, 1.0, False, False), (1, 3, 0, 1.0, 1.0, False, False),
                  (0, 3, 3, 1.0, 1.0, True, True), (8, 128, 128, 0.125, 8.0, True, True), (2, 64, 2048, 1.0, 8.0, False, True),
-                 (1, 33, 4096, 1.0, 8.0, False, False)]
+                 (1, 33, 4096, 1.0, 8.0, False, False), (2, 40, 2048, 0.125, 8.0, True, True),
+                 (1, 1300, 1300, 1.0, 8.0, True, False), (1, 20, 3000, 1.0, 8.0, True, False)]
 
 
 def softmax_case(context, ops, x, batch, rows, cols, scale, causal, rank3, x_offset, out_offset):

@@ -192,6 +192,8 @@ struct TileArgs {
   // Fused epilogue: C = activate(fl(acc + bias[column])) (activation.cuh).
   const float *bias = nullptr;
   uint32_t activation = 0;
+  // The kernel computes D = C^T (m, n above are D's): D[i][j] is stored to C[j][i].
+  bool transposed = false;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -367,15 +369,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 // One CTA per SM walks work units (whole tiles, then k-ranges of the tiles of a
 // short last round). The N tile width BN is 64, 128 or 256 (the narrow tiles keep
 // the tensor cores off padding when n is small); every form uses a 192 KB ring of
-// 16-deep k-slices. With RAW_A the producer loads raw FP32 boxes of A and four
-// converter warps split them into the hi/lo pair in shared memory with the same
-// conversion as split_tf32 (so the operands, and the result, are bit-identical),
-// which saves the split pass over A when few column tiles re-read it.
+// 16-deep k-slices. With RAW = RAW_A (RAW_B) the producer loads raw FP32 boxes of
+// the A (B) operand and four converter warps split them into the hi/lo pair in
+// shared memory with the same conversion as split_tf32 (so the operands, and the
+// result, are bit-identical), which saves the split pass over that operand when
+// few tiles re-read it. TOUT computes C^T: the kernel's M side is C's columns and
+// its N side C's rows, and the epilogue stores D[i][j] to C[j][i] (a narrow C runs
+// this way, since a tcgen05 MMA of N = 64 costs about as much as one of N = 256).
 constexpr int EPI_PITCH = 36;
 constexpr int EPI_TILE_FLOATS = 32 * EPI_PITCH;
 constexpr int RING_BYTES = 192 * 1024, BARRIER_BYTES = 512;
 constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + 4 * EPI_TILE_FLOATS * 4;
 constexpr int STATUS_TIMEOUT_CONVERT = 0x7f3204;
+constexpr int RAW_NONE = 0, RAW_A = 1, RAW_B = 2;
 
 template <int BN> struct Tile {
   static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
@@ -408,8 +414,8 @@ __device__ __forceinline__ float4 tf32_hi(float4 v) {
   return make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
 }
 
-template <int BN, bool RAW_A>
-__global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
+template <int BN, int RAW, bool TOUT>
+__global__ void __launch_bounds__(RAW ? 320 : 192, 1)
     gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                            const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                            const TileArgs args) {
@@ -419,7 +425,7 @@ __global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + RING_BYTES);
   uint64_t *empty = full + S;
-  uint64_t *converted = empty + S; // RAW_A: the stage's A pair is in shared memory
+  uint64_t *converted = empty + S; // RAW: the stage's raw operand is split in shared memory
   uint64_t *tmem_full = converted + S;
   uint64_t *tmem_empty = tmem_full + 2;
   uint64_t *drained = tmem_empty + 2;
@@ -500,23 +506,26 @@ __global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
           if (*abort_flag)
             break;
           uint8_t *stage = smem + s * C::STAGE;
-          if (RAW_A) {
-            mbar_expect_tx(&full[s], A_BYTES + 2 * C::B_BYTES);
+          mbar_expect_tx(&full[s], C::STAGE - (RAW == RAW_A ? A_BYTES : 0) - (RAW == RAW_B ? C::B_BYTES : 0));
+          if (RAW == RAW_A) {
             tma_load_3d(stage, &a_hi, &full[s], kb * TK, m0, z);
           } else {
-            mbar_expect_tx(&full[s], C::STAGE);
             tma_load_2d(stage, &a_hi, &full[s], kb * TK, a_y);
             tma_load_2d(stage + A_BYTES, &a_lo, &full[s], kb * TK, a_y);
           }
-          tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, b_y);
-          tma_load_2d(stage + 2 * A_BYTES + C::B_BYTES, &b_lo, &full[s], kb * TK, b_y);
+          if (RAW == RAW_B) {
+            tma_load_3d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, n0, z);
+          } else {
+            tma_load_2d(stage + 2 * A_BYTES, &b_hi, &full[s], kb * TK, b_y);
+            tma_load_2d(stage + 2 * A_BYTES + C::B_BYTES, &b_lo, &full[s], kb * TK, b_y);
+          }
           *issued = g + 1;
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) { // MMA issuer
-      uint64_t *ready = RAW_A ? converted : full;
+      uint64_t *ready = RAW ? converted : full;
       int g = 0, j = 0;
       for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x, ++j) {
         int tile, kb0, kb1;
@@ -547,9 +556,11 @@ __global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
             const uint64_t ah = desc_k_sw64(stage + step), al = desc_k_sw64(stage + A_BYTES + step);
             const uint64_t bh = desc_k_sw64(stage + 2 * A_BYTES + step);
             const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + C::B_BYTES + step);
+            // Products in the order a_hi b_hi, a_hi b_lo, a_lo b_hi of C's own operands
+            // (the transposed form's A is C's B), so both forms give the same bits.
             mma_tf32_n<BN>(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
-            mma_tf32_n<BN>(acc, ah, bl, 1u);
-            mma_tf32_n<BN>(acc, al, bh, 1u);
+            mma_tf32_n<BN>(acc, TOUT ? al : ah, TOUT ? bh : bl, 1u);
+            mma_tf32_n<BN>(acc, TOUT ? ah : al, TOUT ? bl : bh, 1u);
           }
           mma_commit(&empty[s]);
         }
@@ -560,8 +571,9 @@ __global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
       // Fires once every MMA issued above has finished (TMEM quiet before it is freed).
       mma_commit(drained);
     }
-  } else if (warp >= 6) { // RAW_A converter warps 6..9: raw A box -> hi in place, lo beside it
+  } else if (warp >= 6) { // RAW converter warps 6..9: raw box -> hi in place, lo beside it
     const int t = threadIdx.x - 192;
+    constexpr int RAW_OFFSET = RAW == RAW_B ? 2 * A_BYTES : 0, RAW_BYTES = RAW == RAW_B ? C::B_BYTES : A_BYTES;
     int g = 0;
     for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x) {
       int tile, kb0, kb1;
@@ -574,11 +586,11 @@ __global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
         }
         if (*abort_flag)
           break;
-        float4 *hi = reinterpret_cast<float4 *>(smem + s * C::STAGE);
-        float4 *lo = reinterpret_cast<float4 *>(smem + s * C::STAGE + A_BYTES);
+        float4 *hi = reinterpret_cast<float4 *>(smem + s * C::STAGE + RAW_OFFSET);
+        float4 *lo = reinterpret_cast<float4 *>(smem + s * C::STAGE + RAW_OFFSET + RAW_BYTES);
         // The swizzle is the same for both boxes, so the pair is formed position by position.
 #pragma unroll
-        for (int i = 0; i < A_BYTES / 16 / 128; ++i) {
+        for (int i = 0; i < RAW_BYTES / 16 / 128; ++i) {
           const float4 v = hi[t + 128 * i];
           const float4 h = tf32_hi(v);
           lo[t + 128 * i] = tf32_hi(make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
@@ -630,6 +642,19 @@ __global__ void __launch_bounds__(RAW_A ? 320 : 192, 1)
         const int64_t first = col0 + col;
         if (first >= n_lim)
           break; // the remaining columns of the tile are past n
+        if (TOUT && whole) { // D row = C column (the lanes store 32 consecutive C columns)
+          const int64_t c_col = row0 + lane;
+          if (c_col < m_lim) {
+            float *cptr = c_base + first * ldc + c_col;
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (first + q < n_lim)
+                cptr[q * ldc] = (args.bias || args.activation)
+                                    ? bias_activate(v[q], args.bias, c_col, args.activation)
+                                    : v[q];
+          }
+          continue;
+        }
         if (whole && (args.bias || args.activation)) {
 #pragma unroll
           for (int q = 0; q < 32; ++q)
@@ -699,7 +724,10 @@ template <int BN> __global__ void __launch_bounds__(BN) split_fixup(const TileAr
   float sum = p[0];
   for (int q = 1; q < args.split; ++q)
     sum = __fadd_rn(sum, p[int64_t(q) * (TM * BN)]);
-  args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = bias_activate(sum, args.bias, col, args.activation);
+  if (args.transposed) // D[row][col] is C[col][row]
+    args.c[int64_t(z) * args.c_batch + col * args.ldc + row] = bias_activate(sum, args.bias, row, args.activation);
+  else
+    args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = bias_activate(sum, args.bias, col, args.activation);
 }
 
 // ---- host side ----
@@ -736,15 +764,16 @@ bool make_map(CUtensorMap *map, float *base, int64_t rows_pad, int64_t k_pad, ui
 }
 
 // Raw A as a [batch][m][k] box source (k contiguous, row stride lda, matrix stride
-// sa, all in elements): boxes of 128 rows x 16 k, zero outside the matrix, so the
-// k tail and the rows past m read as the zero padding of the split path.
-bool make_raw_map(CUtensorMap *map, const float *a, int64_t batch, int64_t m, int64_t k, int64_t lda, int64_t sa) {
+// sa, all in elements): boxes of box_rows rows x 16 k, zero outside the matrix, so
+// the k tail and the rows past m read as the zero padding of the split path.
+bool make_raw_map(CUtensorMap *map, const float *a, int64_t batch, int64_t m, int64_t k, int64_t lda, int64_t sa,
+                  uint32_t box_rows) {
   const EncodeTiled encode = encoder();
   if (!encode)
     return false;
   const cuuint64_t dims[3] = {cuuint64_t(k), cuuint64_t(m), cuuint64_t(batch)};
   const cuuint64_t strides[2] = {cuuint64_t(lda) * 4, cuuint64_t(sa) * 4};
-  const cuuint32_t box[3] = {TK, TM, 1};
+  const cuuint32_t box[3] = {TK, box_rows, 1};
   const cuuint32_t element[3] = {1, 1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(a), dims, strides, box, element,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -755,12 +784,12 @@ int64_t round_up(int64_t v, int64_t to) { return (v + to - 1) / to * to; }
 
 // Shared-memory limit of one persistent-kernel form, set once per device (the
 // attribute belongs to the device's context).
-template <int BN, bool RAW_A> bool configure_persistent(int device) {
+template <int BN, int RAW, bool TOUT> bool configure_persistent(int device) {
   static bool configured[64] = {};
   if (device < 0 || device >= 64)
     return false;
   if (!configured[device]) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_persistent<BN, RAW_A>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_tf32x3_persistent<BN, RAW, TOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES_PERSISTENT) != cudaSuccess) {
       cudaGetLastError();
       return false;
@@ -794,7 +823,7 @@ UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks, int bn) {
   return p;
 }
 
-template <int BN, bool RAW_A>
+template <int BN, int RAW, bool TOUT>
 void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
                        float *partials) {
   t.tiles_total = int(tiles);
@@ -802,68 +831,91 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
   t.full_units = plan.full_units;
   t.split = plan.split;
   t.partials = partials;
-  gemm_tf32x3_persistent<BN, RAW_A><<<uint32_t(plan.ctas), RAW_A ? 320 : 192, SMEM_BYTES_PERSISTENT, L.stream>>>(
-      maps[0], maps[1], maps[2], maps[3], t);
+  gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? 320 : 192, SMEM_BYTES_PERSISTENT,
+                                          L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
     split_fixup<BN><<<dim3(TM, uint32_t(plan.remaining)), BN, 0, L.stream>>>(t);
     ++L.kernels;
   }
 }
 
-// The six kernel forms: N tile width x (A split in shared memory or by the split pass).
-bool configure_form(int bn, bool raw_a, int device) {
-  switch (bn * 2 + (raw_a ? 1 : 0)) {
-  case 128: return configure_persistent<64, false>(device);
-  case 129: return configure_persistent<64, true>(device);
-  case 256: return configure_persistent<128, false>(device);
-  case 257: return configure_persistent<128, true>(device);
-  case 512: return configure_persistent<256, false>(device);
-  case 513: return configure_persistent<256, true>(device);
+// The kernel forms: N tile width x (which operand, if any, is split in shared
+// memory), plus the transposed form for narrow C (256 columns, raw B, D = C^T).
+enum class Form { n64, n64_raw_a, n128, n128_raw_a, n256, n256_raw_a, transposed };
+Form form_of(int bn, bool raw_a) {
+  if (bn == 64)
+    return raw_a ? Form::n64_raw_a : Form::n64;
+  if (bn == 128)
+    return raw_a ? Form::n128_raw_a : Form::n128;
+  return raw_a ? Form::n256_raw_a : Form::n256;
+}
+bool configure_form(Form f, int device) {
+  switch (f) {
+  case Form::n64: return configure_persistent<64, RAW_NONE, false>(device);
+  case Form::n64_raw_a: return configure_persistent<64, RAW_A, false>(device);
+  case Form::n128: return configure_persistent<128, RAW_NONE, false>(device);
+  case Form::n128_raw_a: return configure_persistent<128, RAW_A, false>(device);
+  case Form::n256: return configure_persistent<256, RAW_NONE, false>(device);
+  case Form::n256_raw_a: return configure_persistent<256, RAW_A, false>(device);
+  case Form::transposed: return configure_persistent<256, RAW_B, true>(device);
   }
   return false;
 }
-void launch_form(int bn, bool raw_a, Launch &L, const CUtensorMap (&maps)[4], const TileArgs &t, int64_t tiles,
+void launch_form(Form f, Launch &L, const CUtensorMap (&maps)[4], const TileArgs &t, int64_t tiles,
                  const UnitPlan &plan, float *partials) {
-  switch (bn * 2 + (raw_a ? 1 : 0)) {
-  case 128: return launch_persistent<64, false>(L, maps, t, tiles, plan, partials);
-  case 129: return launch_persistent<64, true>(L, maps, t, tiles, plan, partials);
-  case 256: return launch_persistent<128, false>(L, maps, t, tiles, plan, partials);
-  case 257: return launch_persistent<128, true>(L, maps, t, tiles, plan, partials);
-  case 512: return launch_persistent<256, false>(L, maps, t, tiles, plan, partials);
-  default: return launch_persistent<256, true>(L, maps, t, tiles, plan, partials);
+  switch (f) {
+  case Form::n64: return launch_persistent<64, RAW_NONE, false>(L, maps, t, tiles, plan, partials);
+  case Form::n64_raw_a: return launch_persistent<64, RAW_A, false>(L, maps, t, tiles, plan, partials);
+  case Form::n128: return launch_persistent<128, RAW_NONE, false>(L, maps, t, tiles, plan, partials);
+  case Form::n128_raw_a: return launch_persistent<128, RAW_A, false>(L, maps, t, tiles, plan, partials);
+  case Form::n256: return launch_persistent<256, RAW_NONE, false>(L, maps, t, tiles, plan, partials);
+  case Form::n256_raw_a: return launch_persistent<256, RAW_A, false>(L, maps, t, tiles, plan, partials);
+  case Form::transposed: return launch_persistent<256, RAW_B, true>(L, maps, t, tiles, plan, partials);
   }
 }
 
 // N tile width for n columns: the narrowest of 64 / 128 / 256 that holds them, else 256.
 int tile_width(int64_t n) { return n <= 64 ? 64 : (n <= 128 ? 128 : 256); }
 
-// Raw A boxes need A stored [m][k] (k contiguous) with 16-byte aligned rows and
-// matrices; they pay off when few column tiles re-read A (each re-read converts
-// again, while the split pass converts once).
-// (sa is the matrix stride; matrices must not overlap.)
-bool raw_a_fits(const float *a, bool ta, int64_t m, int64_t lda, int64_t batch, int64_t sa, int64_t tiles_n) {
-  return !ta && tiles_n <= 2 && (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && lda % 4 == 0 && sa % 4 == 0 &&
-         sa >= m * lda && lda <= (int64_t(1) << 36) && sa <= (int64_t(1) << 36) && batch >= 1;
+// Raw boxes of A need A stored [m][k] (k contiguous) with 16-byte aligned rows and
+// non-overlapping matrices (sa = matrix stride).
+bool raw_a_layout(const float *a, bool ta, int64_t m, int64_t lda, int64_t sa) {
+  return !ta && (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && lda % 4 == 0 && sa % 4 == 0 && sa >= m * lda &&
+         lda <= (int64_t(1) << 36) && sa <= (int64_t(1) << 36);
 }
 
 // Plans and enqueues C[z] = op(A[z]) op(B[z]) for z < batch (see the launchers below).
+//  * n <= 128 and A laid out for raw boxes: the transposed form. D = C^T =
+//    op(B)^T op(A)^T with op(B)^T split into 128-row tiles (n rows, zero padded)
+//    and A's rows as the 256-wide side, converted in shared memory.
+//  * otherwise: 128 x BN tiles of C; A converted in shared memory when at most two
+//    column tiles re-read it, else split by the split pass.
 bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m, int64_t n,
                    int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb, int64_t ldc,
                    int64_t sc, const float *bias, uint32_t activation) {
   if (!encoder() || !L.workspace)
     return false;
-  const int bn = tile_width(n);
-  const int64_t k_pad = round_up(k, 32), m_pad = round_up(m, TM), n_pad = round_up(n, bn);
-  const int64_t tiles_m = m_pad / TM, tiles_n = n_pad / bn, batch_b = sb ? batch : 1;
-  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || m_pad / 32 > 65535 ||
-      n_pad / 32 > 65535 || batch * m_pad > INT32_MAX || batch_b * n_pad > INT32_MAX)
-    return false; // grid limits and 32-bit TMA row coordinates
   if (batch == 1)
     sa = m * lda;
-  const bool raw_a = raw_a_fits(a, ta, m, lda, batch, sa, tiles_n);
+  const bool raw_a = raw_a_layout(a, ta, m, lda, sa);
+  const bool transposed = raw_a && n <= 128;
+  // The kernel's D [dm, dn]: C itself, or C^T in the transposed form.
+  const int64_t dm = transposed ? n : m, dn = transposed ? m : n;
+  const int bn = transposed ? 256 : tile_width(n);
+  const int64_t k_pad = round_up(k, 32), dm_pad = round_up(dm, TM), dn_pad = round_up(dn, bn);
+  const int64_t tiles_m = dm_pad / TM, tiles_n = dn_pad / bn, batch_b = sb ? batch : 1;
+  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || dm_pad / 32 > 65535 ||
+      dn_pad / 32 > 65535 || batch * dm_pad > INT32_MAX || batch_b * dn_pad > INT32_MAX)
+    return false; // grid limits and 32-bit TMA row coordinates
+  const Form form = transposed ? Form::transposed : form_of(bn, raw_a && tiles_n <= 2);
+  const bool a_split = !transposed && (form == Form::n64 || form == Form::n128 || form == Form::n256);
   const UnitPlan plan = plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn);
-  const int64_t a_split_rows = raw_a ? 0 : batch * m_pad;
-  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_split_rows + batch_b * n_pad);
+  // Split operands in the workspace: A's pair [batch * m_pad][k_pad] unless A is
+  // converted in shared memory; B's pair [batch_b * rows][k_pad], rows = n_pad
+  // (or, transposed, n padded to 128: the kernel's M side).
+  const int64_t a_rows = a_split ? batch * dm_pad : 0;
+  const int64_t b_rows_each = transposed ? dm_pad : dn_pad;
+  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_rows + batch_b * b_rows_each);
   const size_t bytes = split_bytes + plan.partial_bytes;
   if (L.dry_run)
     return true;
@@ -871,41 +923,54 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   if (!scratch)
     return false;
   float *partials = scratch + split_bytes / sizeof(float);
-  float *ahi = scratch, *alo = ahi + a_split_rows * k_pad, *bhi = alo + a_split_rows * k_pad,
-        *blo = bhi + batch_b * n_pad * k_pad;
+  float *ahi = scratch, *alo = ahi + a_rows * k_pad, *bhi = alo + a_rows * k_pad,
+        *blo = bhi + batch_b * b_rows_each * k_pad;
   CUtensorMap maps[4];
-  if (raw_a) {
-    if (!make_raw_map(&maps[0], a, batch, m, k, lda, sa))
+  if (transposed) { // kernel A = op(B)^T pair, kernel B = raw rows of A
+    if (!make_map(&maps[0], bhi, batch_b * dm_pad, k_pad, TM) || !make_map(&maps[1], blo, batch_b * dm_pad, k_pad, TM) ||
+        !make_raw_map(&maps[2], a, batch, m, k, lda, sa, uint32_t(bn)))
       return false;
-    maps[1] = maps[0]; // unused
-  } else if (!make_map(&maps[0], ahi, batch * m_pad, k_pad, TM) || !make_map(&maps[1], alo, batch * m_pad, k_pad, TM)) {
-    return false;
+    maps[3] = maps[2]; // unused
+  } else {
+    if (a_split) {
+      if (!make_map(&maps[0], ahi, batch * dm_pad, k_pad, TM) || !make_map(&maps[1], alo, batch * dm_pad, k_pad, TM))
+        return false;
+    } else {
+      if (!make_raw_map(&maps[0], a, batch, m, k, lda, sa, TM))
+        return false;
+      maps[1] = maps[0]; // unused
+    }
+    if (!make_map(&maps[2], bhi, batch_b * dn_pad, k_pad, uint32_t(bn)) ||
+        !make_map(&maps[3], blo, batch_b * dn_pad, k_pad, uint32_t(bn)))
+      return false;
   }
-  if (!make_map(&maps[2], bhi, batch_b * n_pad, k_pad, uint32_t(bn)) ||
-      !make_map(&maps[3], blo, batch_b * n_pad, k_pad, uint32_t(bn)))
-    return false;
-  if (!configure_form(bn, raw_a, L.device))
+  if (!configure_form(form, L.device))
     return false;
   // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
-  if (!raw_a) {
-    split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
-        a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, m_pad);
+  if (a_split) {
+    split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(dm_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
+        a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad);
     ++L.kernels;
   }
-  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
-      b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, n_pad);
+  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(b_rows_each / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
+      b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each);
   ++L.kernels;
-  TileArgs t{c, m, n, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
+  TileArgs t{c, dm, dn, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
   if (batch > 1) {
     t.tiles_per_batch = int(tiles_m * tiles_n);
-    t.a_rows = int(m_pad);
-    t.b_rows = sb ? int(n_pad) : 0;
+    if (transposed) {
+      t.a_rows = sb ? int(dm_pad) : 0; // kernel A rows = op(B)^T of matrix z
+    } else {
+      t.a_rows = int(dm_pad);
+      t.b_rows = sb ? int(dn_pad) : 0;
+    }
     t.c_batch = sc;
   }
   t.bias = bias;
   t.activation = activation;
+  t.transposed = transposed;
   ++L.kernels;
-  launch_form(bn, raw_a, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
+  launch_form(form, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
   return true;
 }
 

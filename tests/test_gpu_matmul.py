@@ -133,7 +133,7 @@ def test_matmul_validation(context):
 
 
 @pytest.mark.parametrize("m,n,k", [(2432, 2048, 1024), (4096, 4096, 256), (4096, 4096, 40), (128 * 150, 256, 96),
-                                   (2048, 1024, 1024), (512, 512, 512), (1000, 60, 4000)])
+                                   (2048, 1024, 1024), (512, 512, 512), (1000, 60, 4000), (5000, 128, 512)])
 def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
     # Tile counts just above a multiple of the 148 persistent CTAs, or below it: the
     # tiles of the last (or only), mostly idle round are cut into k-ranges whose
@@ -155,11 +155,13 @@ def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
 
 @pytest.mark.parametrize("mode", (p.MatmulMode.REFERENCE, p.MatmulMode.FFMA, p.MatmulMode.TF32X3, p.MatmulMode.AUTO))
 @pytest.mark.parametrize("m,n,k,ta,tb", [(129, 65, 257, False, False), (300, 260, 96, True, False),
-                                         (2432, 2048, 256, False, True), (64, 40, 0, False, False)])
+                                         (2432, 2048, 256, False, True), (64, 40, 0, False, False),
+                                         (300, 64, 96, False, False), (1000, 100, 2048, False, True)])
 def test_fused_bias_activation_equals_two_commands(context, mode, m, n, k, ta, tb):
     # One command (GEMM epilogue adds the bias and applies the activation) against
     # pr_matmul_f32 followed by pr_bias_activation_f32: identical bits, every mode,
-    # including the split tail tiles (2432 x 2048) and k = 0.
+    # including the split tail tiles (2432 x 2048), k = 0 and narrow C computed
+    # transposed (n = 64 and n = 100, the latter with split k-ranges).
     p.set_matmul_mode(context, mode)
     res = T.operators_of(context)
     D = T.TensorDescriptor
@@ -243,9 +245,13 @@ def aligned_matmul(context, a, b, m, n, k, ta):
 @pytest.mark.parametrize("m,n,k", [(1, 1, 16), (16, 16, 16), (129, 65, 260), (257, 100, 96), (300, 129, 64),
                                    (2048, 64, 2048), (1000, 512, 100), (4096, 200, 1024)])
 def test_a_split_in_shared_memory_equals_the_split_pass(context, m, n, k):
-    # A stored [m, k] with 16-byte aligned rows, re-read by at most two column tiles, is
-    # loaded raw and split into its TF32 pair inside the GEMM kernel; stored [k, m] it
-    # goes through the separate split pass. Same conversion, same order: equal bits.
+    # A stored [m, k] with 16-byte aligned rows is loaded raw and split into its TF32
+    # pair inside the GEMM kernel: as the A operand when at most two column tiles
+    # re-read it, as the 256-wide B operand of C^T when n <= 128. Stored [k, m] it goes
+    # through the separate split pass into 128 x BN tiles of C. Same conversion, same
+    # products in the same order and, at these sizes, the same k-ranges for the
+    # split tail: equal bits. (Where the two tilings cut k differently the partial
+    # sums round differently; the split-tail test bounds those cases.)
     p.set_matmul_mode(context, p.MatmulMode.TF32X3)
     try:
         a = synthetic.uniform(9100 + m, 0, m * k).reshape(m, k)

@@ -707,10 +707,13 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
   }
 }
 
-// C of every split tile = its partial tiles added in k order (one thread per
-// element, BN columns per block, one block per tile row).
-template <int BN> __global__ void __launch_bounds__(BN) split_fixup(const TileArgs args) {
-  const int t = blockIdx.y, i = blockIdx.x, j = threadIdx.x; // remaining tile, row, column in tile
+// C of every split tile = its partial tiles added in k order: one thread per four
+// columns of a tile row (128-bit loads), 1024 / BN rows per 256-thread block.
+template <int BN> __global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
+  constexpr int PER_ROW = BN / 4, ROWS = 256 / PER_ROW;
+  const int t = blockIdx.y;                                     // remaining tile
+  const int i = blockIdx.x * ROWS + threadIdx.x / PER_ROW;      // row in the tile
+  const int j = 4 * (threadIdx.x % PER_ROW);                    // first of four columns
   const int tile = args.full_units + t;
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
   const int z = tile / per_batch, id = tile % per_batch, group = 8, per_group = group * args.tiles_n;
@@ -720,14 +723,30 @@ template <int BN> __global__ void __launch_bounds__(BN) split_fixup(const TileAr
   const int64_t col = int64_t((id % per_group) / rows_in_group) * BN + j;
   if (row >= args.m || col >= args.n)
     return;
-  const float *p = args.partials + int64_t(t) * args.split * (TM * BN) + i * BN + j;
-  float sum = p[0];
-  for (int q = 1; q < args.split; ++q)
-    sum = __fadd_rn(sum, p[int64_t(q) * (TM * BN)]);
-  if (args.transposed) // D[row][col] is C[col][row]
-    args.c[int64_t(z) * args.c_batch + col * args.ldc + row] = bias_activate(sum, args.bias, row, args.activation);
-  else
-    args.c[int64_t(z) * args.c_batch + row * args.ldc + col] = bias_activate(sum, args.bias, col, args.activation);
+  const float4 *p = reinterpret_cast<const float4 *>(args.partials + int64_t(t) * args.split * (TM * BN) + i * BN + j);
+  float4 s4 = p[0];
+  for (int q = 1; q < args.split; ++q) {
+    const float4 v = p[int64_t(q) * (TM * BN / 4)];
+    s4 = make_float4(__fadd_rn(s4.x, v.x), __fadd_rn(s4.y, v.y), __fadd_rn(s4.z, v.z), __fadd_rn(s4.w, v.w));
+  }
+  const float sum[4] = {s4.x, s4.y, s4.z, s4.w};
+  float *const c = args.c + int64_t(z) * args.c_batch;
+  if (args.transposed) { // D[row][col] is C[col][row]
+    for (int e = 0; e < 4 && col + e < args.n; ++e)
+      c[(col + e) * args.ldc + row] = bias_activate(sum[e], args.bias, row, args.activation);
+    return;
+  }
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    y[e] = bias_activate(sum[e], args.bias, col + e < args.n ? col + e : col, args.activation);
+  float *dst = c + row * args.ldc + col;
+  if (col + 3 < args.n && args.ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    *reinterpret_cast<float4 *>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+  } else {
+    for (int e = 0; e < 4 && col + e < args.n; ++e)
+      dst[e] = y[e];
+  }
 }
 
 // C = activate(C) in place over [m, n] with row stride ldc: the tanh GELU of a fused
@@ -859,7 +878,7 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
   gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? 320 : 192, SMEM_BYTES_PERSISTENT,
                                           L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
-    split_fixup<BN><<<dim3(TM, uint32_t(plan.remaining)), BN, 0, L.stream>>>(t);
+    split_fixup<BN><<<dim3(TM / (1024 / BN), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);
     ++L.kernels;
   }
 }

@@ -173,6 +173,67 @@ __global__ void __launch_bounds__(256) split_tf32(const float *__restrict__ x, i
   }
 }
 
+// The same split with 128-bit accesses, for 16-byte aligned operands whose leading
+// dimension is a multiple of 4 (both grids cover [rows_pad][k_pad] in 32x32 tiles,
+// z = matrix). Stored [rows][k]: each thread converts four consecutive k of a row,
+// no shared memory. Stored [k][rows] (transposed): a 32x32 tile is read as float4
+// along the rows, transposed in shared memory and written as float4 along k.
+__device__ __forceinline__ void split4(float4 v, float4 &h, float4 &l) {
+  h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+  l = make_float4(tf32_rna(v.x - h.x), tf32_rna(v.y - h.y), tf32_rna(v.z - h.z), tf32_rna(v.w - h.w));
+}
+__global__ void __launch_bounds__(256) split_tf32_vec(const float *__restrict__ x, int64_t ld, int transposed,
+                                                      int64_t rows, int64_t k, float *__restrict__ hi,
+                                                      float *__restrict__ lo, int64_t k_pad, int64_t x_batch,
+                                                      int64_t rows_pad) {
+  __shared__ float tile[32][33];
+  x += int64_t(blockIdx.z) * x_batch;
+  hi += int64_t(blockIdx.z) * rows_pad * k_pad;
+  lo += int64_t(blockIdx.z) * rows_pad * k_pad;
+  const int64_t r0 = int64_t(blockIdx.y) * 32, k0 = int64_t(blockIdx.x) * 32;
+  const int q = threadIdx.x % 8, a = threadIdx.x / 8; // 8 float4 x 32 lines
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (!transposed) { // line a = row r0 + a, k0 + 4q .. +3
+    const int64_t r = r0 + a, kk = k0 + 4 * q;
+    float4 v = zero;
+    if (r < rows && kk + 3 < k)
+      v = *reinterpret_cast<const float4 *>(x + r * ld + kk);
+    else if (r < rows)
+      for (int e = 0; e < 4; ++e)
+        if (kk + e < k)
+          (&v.x)[e] = x[r * ld + kk + e];
+    float4 h, l;
+    split4(v, h, l);
+    const int64_t offset = r * k_pad + kk;
+    *reinterpret_cast<float4 *>(hi + offset) = h;
+    *reinterpret_cast<float4 *>(lo + offset) = l;
+    return;
+  }
+  { // line a = k0 + a, rows r0 + 4q .. +3
+    const int64_t kk = k0 + a, r = r0 + 4 * q;
+    float4 v = zero;
+    if (kk < k && r + 3 < rows)
+      v = *reinterpret_cast<const float4 *>(x + kk * ld + r);
+    else if (kk < k)
+      for (int e = 0; e < 4; ++e)
+        if (r + e < rows)
+          (&v.x)[e] = x[kk * ld + r + e];
+    tile[4 * q + 0][a] = v.x;
+    tile[4 * q + 1][a] = v.y;
+    tile[4 * q + 2][a] = v.z;
+    tile[4 * q + 3][a] = v.w;
+  }
+  __syncthreads();
+  { // line a = row r0 + a, k0 + 4q .. +3
+    const float4 v = make_float4(tile[a][4 * q], tile[a][4 * q + 1], tile[a][4 * q + 2], tile[a][4 * q + 3]);
+    float4 h, l;
+    split4(v, h, l);
+    const int64_t offset = (r0 + a) * k_pad + k0 + 4 * q;
+    *reinterpret_cast<float4 *>(hi + offset) = h;
+    *reinterpret_cast<float4 *>(lo + offset) = l;
+  }
+}
+
 struct TileArgs {
   float *c;
   int64_t m, n, ldc;
@@ -991,14 +1052,26 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   if (!configure_form(form, L.device))
     return false;
   // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
+  // 128-bit split when the operand's rows (or columns) start on 16-byte boundaries.
+  auto vec_ok = [](const float *x, int64_t ld, int64_t stride) {
+    return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && ld % 4 == 0 && stride % 4 == 0;
+  };
   if (a_split) {
-    split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(dm_pad / 32), uint32_t(batch)), 256, 0, L.stream>>>(
-        a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad);
+    const dim3 grid(uint32_t(k_pad / 32), uint32_t(dm_pad / 32), uint32_t(batch));
+    if (vec_ok(a, lda, batch > 1 ? sa : 0))
+      split_tf32_vec<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad);
+    else
+      split_tf32<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad);
     ++L.kernels;
   }
-  split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(b_rows_each / 32), uint32_t(batch_b)), 256, 0, L.stream>>>(
-      b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each);
-  ++L.kernels;
+  {
+    const dim3 grid(uint32_t(k_pad / 32), uint32_t(b_rows_each / 32), uint32_t(batch_b));
+    if (vec_ok(b, ldb, sb))
+      split_tf32_vec<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each);
+    else
+      split_tf32<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each);
+    ++L.kernels;
+  }
   TileArgs t{c, dm, dn, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
   if (batch > 1) {
     t.tiles_per_batch = int(tiles_m * tiles_n);

@@ -129,6 +129,20 @@ __device__ __forceinline__ void tmem_load_32(uint32_t taddr, float (&v)[32]) {
     v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_load_16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+               "%14, %15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                 "=r"(r[15])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -437,10 +451,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 // few tiles re-read it. TOUT computes C^T: the kernel's M side is C's columns and
 // its N side C's rows, and the epilogue stores D[i][j] to C[j][i] (a narrow C runs
 // this way, since a tcgen05 MMA of N = 64 costs about as much as one of N = 256).
-constexpr int EPI_PITCH = 36;
-constexpr int EPI_TILE_FLOATS = 32 * EPI_PITCH;
+// Eight epilogue warps: warps 2..5 and 6..9 each cover the four TMEM lane quarters,
+// the first group the left half of the tile's columns, the second the right half,
+// staged 32 rows x 16 columns at a time.
+constexpr int EPI_WARPS = 8, EPI_PITCH16 = 20;
+constexpr int EPI_STAGE_FLOATS = 32 * EPI_PITCH16;
 constexpr int RING_BYTES = 192 * 1024, BARRIER_BYTES = 512;
-constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + 4 * EPI_TILE_FLOATS * 4;
+constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + EPI_WARPS * EPI_STAGE_FLOATS * 4;
+constexpr int THREADS_PLAIN = 64 + 32 * EPI_WARPS, THREADS_RAW = THREADS_PLAIN + 128; // + 4 converter warps
 constexpr int STATUS_TIMEOUT_CONVERT = 0x7f3204;
 constexpr int RAW_NONE = 0, RAW_A = 1, RAW_B = 2;
 
@@ -476,7 +494,7 @@ __device__ __forceinline__ float4 tf32_hi(float4 v) {
 }
 
 template <int BN, int RAW, bool TOUT>
-__global__ void __launch_bounds__(RAW ? 320 : 192, 1)
+__global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
     gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                            const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                            const TileArgs args) {
@@ -530,7 +548,7 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], 4);
+      mbar_init(&tmem_empty[b], EPI_WARPS);
     }
     mbar_init(drained, 1);
     *abort_flag = 0;
@@ -632,8 +650,8 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
       // Fires once every MMA issued above has finished (TMEM quiet before it is freed).
       mma_commit(drained);
     }
-  } else if (warp >= 6) { // RAW converter warps 6..9: raw box -> hi in place, lo beside it
-    const int t = threadIdx.x - 192;
+  } else if (warp >= 2 + EPI_WARPS) { // RAW converter warps 10..13: raw box -> hi in place, lo beside it
+    const int t = threadIdx.x - THREADS_PLAIN;
     constexpr int RAW_OFFSET = RAW == RAW_B ? 2 * A_BYTES : 0, RAW_BYTES = RAW == RAW_B ? C::B_BYTES : A_BYTES;
     int g = 0;
     for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x) {
@@ -663,8 +681,8 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&converted[s])) : "memory");
       }
     }
-  } else { // epilogue warps 2..5: TMEM lanes 32*(warp % 4) ..
-    const int sub = warp % 4;
+  } else { // epilogue warps 2..9: TMEM lanes 32*(warp % 4) .., column half (warp - 2) / 4
+    const int sub = warp % 4, half = (warp - 2) / 4;
     int j = 0;
     for (int u = blockIdx.x; u < args.units_total; u += gridDim.x, ++j) {
       int tile, kb0, kb1;
@@ -693,13 +711,13 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
       const int64_t col0 = whole ? int64_t(n0) : 0;
       const int64_t left = m_lim - row0;
       const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
-      float *tile_s = epi_tiles + sub * EPI_TILE_FLOATS;
+      float *tile_s = epi_tiles + (warp - 2) * EPI_STAGE_FLOATS;
       const uint32_t acc = tmem + uint32_t(b) * C::COLUMNS + (uint32_t(32 * sub) << 16);
       const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
-      for (int col = 0; col < BN; col += 32) {
-        float v[32];
-        tmem_load_32(acc + uint32_t(col), v); // thread = row 32*sub + lane, 32 columns
+      for (int col = half * (BN / 2); col < (half + 1) * (BN / 2); col += 16) {
+        float v[16];
+        tmem_load_16(acc + uint32_t(col), v); // thread = row 32*sub + lane, 16 columns
         const int64_t first = col0 + col;
         if (first >= n_lim)
           break; // the remaining columns of the tile are past n
@@ -708,7 +726,7 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
           if (c_col < m_lim) {
             float *cptr = c_base + first * ldc + c_col;
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
+            for (int q = 0; q < 16; ++q)
               if (first + q < n_lim)
                 cptr[q * ldc] = (args.bias || args.activation)
                                     ? bias_activate(v[q], args.bias, c_col, args.activation)
@@ -718,30 +736,31 @@ __global__ void __launch_bounds__(RAW ? 320 : 192, 1)
         }
         if (whole && (args.bias || args.activation)) {
 #pragma unroll
-          for (int q = 0; q < 32; ++q)
+          for (int q = 0; q < 16; ++q)
             if (first + q < n_lim)
               v[q] = bias_activate(v[q], args.bias, first + q, args.activation);
         }
 #pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH + q]) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+        for (int q = 0; q < 16; q += 4)
+          *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH16 + q]) =
+              make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         __syncwarp();
-        if (vec_c && rows_here == 32 && first + 31 < n_lim) {
-          const int r_in = lane / 8, c4 = 4 * (lane % 8); // 4 rows x 8 float4 per instruction
-          float4 w[8];
+        if (vec_c && rows_here == 32 && first + 15 < n_lim) {
+          const int r_in = lane / 4, c4 = 4 * (lane % 4); // 8 rows x 4 float4 per instruction
+          float4 w[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            w[i] = *reinterpret_cast<const float4 *>(&tile_s[(4 * i + r_in) * EPI_PITCH + c4]);
+          for (int i = 0; i < 4; ++i)
+            w[i] = *reinterpret_cast<const float4 *>(&tile_s[(8 * i + r_in) * EPI_PITCH16 + c4]);
           float *cptr = c_base + (row0 + r_in) * ldc + first + c4;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4 *>(cptr + int64_t(4 * i) * ldc) = w[i];
-        } else {
-          const int64_t column = first + lane; // thread = column: one row segment per store
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float4 *>(cptr + int64_t(8 * i) * ldc) = w[i];
+        } else { // lanes 0..15 / 16..31: one column each, even / odd rows
+          const int64_t column = first + (lane & 15);
           if (column < n_lim) {
             float *cptr = c_base + row0 * ldc + column;
-            for (int r = 0; r < rows_here; ++r)
-              cptr[r * ldc] = tile_s[r * EPI_PITCH + lane];
+            for (int r = lane >> 4; r < rows_here; r += 2)
+              cptr[r * ldc] = tile_s[r * EPI_PITCH16 + (lane & 15)];
           }
         }
         __syncwarp();
@@ -936,7 +955,7 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
   t.full_units = plan.full_units;
   t.split = plan.split;
   t.partials = partials;
-  gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? 320 : 192, SMEM_BYTES_PERSISTENT,
+  gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? THREADS_RAW : THREADS_PLAIN, SMEM_BYTES_PERSISTENT,
                                           L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
     split_fixup<BN><<<dim3(TM / (1024 / BN), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);

@@ -746,7 +746,9 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
               make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         __syncwarp();
         if (vec_c && rows_here == 32 && first + 15 < n_lim) {
-          const int r_in = lane / 4, c4 = 4 * (lane % 4); // 8 rows x 4 float4 per instruction
+          // 8 rows x 4 float4 per instruction; each group of 8 lanes reads one column
+          // chunk of 8 rows (row pitch 20 floats): eight distinct 4-bank groups
+          const int r_in = lane % 8, c4 = 4 * (lane / 8);
           float4 w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i)

@@ -10,21 +10,29 @@
 // infinite product into NaN (inf - inf in the split).
 //
 // Structure:
-//  1. split kernel: op(A) -> A_hi, A_lo [M_pad][K_pad] and op(B)^T -> B_hi, B_lo
+//  1. split kernels: op(A) -> A_hi, A_lo [M_pad][K_pad] and op(B)^T -> B_hi, B_lo
 //     [N_pad][K_pad] in the context workspace, K contiguous, zero padded (one read,
-//     two writes of each operand; a 32x32 shared-memory transpose for the
-//     transposed layouts).
-//  2. GEMM kernel (the one-tile form below serves the allocation-free entry point;
-//     the persistent form further down serves the tensor provider), one 128x256
-//     output tile per CTA, 6 warps:
-//     warp 0 lane 0: TMA producer. Each 16-deep k-slice is four 2-D boxes
-//       (A_hi, A_lo 128x16; B_hi, B_lo 256x16; 64-byte rows, SWIZZLE_64B) into a
-//       4-stage ring of 48 KB stages, signalled by mbarrier transaction counts.
-//     warp 1: allocates 256 TMEM columns; lane 0 issues per 8-deep step three
-//       tcgen05.mma.kind::tf32 (128x256x8, both operands K-major from shared
-//       memory descriptors) and releases each stage with tcgen05.commit.
-//     warps 2-5: epilogue. tcgen05.ld 32 lanes x 32 columns per warp, masked
-//       stores to C (row stride ldc).
+//     two writes of each operand; 128-bit accesses, a 32x32 shared-memory transpose
+//     for the transposed layouts). An operand loaded raw by the GEMM is not split.
+//  2. persistent GEMM kernel (gemm_tf32x3_persistent, for the tensor provider): one
+//     CTA per SM walks work units, 128 x BN output tiles (BN = 64, 128, 256) and the
+//     k-ranges of the tiles of a short last round.
+//     warp 0 lane 0: TMA producer. Each 16-deep k-slice is four 2-D boxes (A_hi,
+//       A_lo 128x16; B_hi, B_lo BNx16; 64-byte rows, SWIZZLE_64B), or one raw FP32
+//       box in place of a pair, into a 192 KB ring signalled by mbarrier transaction
+//       counts.
+//     warp 1: allocates 2 x BN TMEM columns; lane 0 issues per 8-deep step three
+//       tcgen05.mma.kind::tf32 (128xBNx8, both operands K-major from shared memory
+//       descriptors) into one of two accumulators and releases each stage with
+//       tcgen05.commit.
+//     warps 2-9: epilogue, two warps per TMEM lane quarter (one per column half):
+//       tcgen05.ld 32 lanes x 16 columns, fused bias/ReLU, 128-bit stores staged
+//       through shared memory; then the accumulator is handed back.
+//     warps 10-13 (raw forms only): split the raw box of each stage into its TF32
+//       pair in shared memory.
+//     A separate kernel adds the partial tiles of split tiles (split_fixup).
+//  3. one-tile GEMM kernel (gemm_tf32x3, 6 warps, one 128x256 tile per CTA) for the
+//     allocation-free entry point at the end of this file.
 //  Every wait is bounded (about two seconds of SM clock); on expiry the kernel
 //  records a status code in host-mapped memory, stops issuing, frees its TMEM and
 //  returns, and the engine reports PR_EXECUTION_FAILED.

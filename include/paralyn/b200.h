@@ -150,7 +150,7 @@ pr_status pr_b200_matmul_tf32x3_static_f32(const float *a, const float *b, float
  * would, and writes "kernel=implementation;" for each entry into report
  * (NUL-terminated, truncated to capacity). Same statuses as pr_module_load:
  * PR_COMPILATION_FAILED for malformed or unverifiable IR, PR_UNSUPPORTED for a
- * kernel this build has no native implementation of. */
+ * kernel this library has no native implementation of. */
 pr_status pr_b200_module_inspect(const void *data, uint64_t bytes, char *report, uint64_t capacity);
 
 #ifdef __cplusplus

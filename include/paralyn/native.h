@@ -138,7 +138,7 @@ typedef struct pr_backend_status_v1 {
 uint32_t pr_abi_version(void);
 pr_status pr_backend_status_get(const char *backend, pr_backend_status_v1 *out);
 pr_status pr_last_error(pr_error *out);
-/* Devices: CUDA devices in driver ordinal order (no Metal in this build).
+/* Devices: CUDA devices in driver ordinal order (no Metal in this library).
  * Contexts are selected with "cuda:K" or "auto" (= cuda:0). */
 pr_status pr_device_count(uint32_t *out);
 pr_status pr_device_get(uint32_t index, pr_device_info *out);
@@ -160,7 +160,7 @@ pr_status pr_view_create(pr_buffer buffer, uint64_t offset, uint64_t bytes, uint
 pr_status pr_buffer_write(pr_buffer buffer, uint64_t offset, const void *source, uint64_t bytes);
 pr_status pr_buffer_read(pr_buffer buffer, uint64_t offset, void *destination, uint64_t bytes);
 /* Loads a verified-IR module (.prk, format 1, numerical policy 1). Kernels whose
- * IR this build maps to a native sm_100a kernel load; others are PR_UNSUPPORTED. */
+ * IR this library maps to a native sm_100a kernel load; others are PR_UNSUPPORTED. */
 pr_status pr_module_load(pr_context context, const void *data, uint64_t bytes, pr_module *out);
 pr_status pr_module_load_file(pr_context context, const char *path, pr_module *out);
 pr_status pr_module_kernel(pr_module module, const char *name, pr_kernel *out);

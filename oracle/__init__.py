@@ -2,7 +2,7 @@
 restates from the reference and where).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import
-this package, and only as the checker or the timed CPU baseline; the product
+this package, and only as the parity oracle or the timed CPU baseline; the product
 (paralyn_b200 and libparalyn_native.so) never does.
 
 liboracle.so is built by `make -C oracle`; `make -C oracle ref` also builds

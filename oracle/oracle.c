@@ -2,7 +2,7 @@
  * CPU oracle for the FP32 operator path: TEST INFRASTRUCTURE ONLY.
  *
  * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may load
- * this library, and only as the checker or the timed CPU baseline. The product
+ * this library, and only as the parity oracle or the timed CPU baseline. The product
  * (libparalyn_native.so) never calls it and has no CPU fallback.
  *
  * Every function restates the arithmetic the reference specifies, in the

@@ -4,7 +4,7 @@ Mirrors the reference's array API (bindings/python/paralyn/array.py): asarray,
 Array (shape/size/nbytes/wait/to_host/close), add and affine, launched through
 pr_launch from the verified-IR operators module (array_add / array_affine, grid
 ceil(n/256) x 256) on the context's queue. affine_scalar(a, scale, bias) is an
-addition of this build: the affine map with a scalar addend, from the same
+addition of this library: the affine map with a scalar addend, from the same
 module. Sequence input is rounded to binary32 and copied; buffer input must be
 native FP32 and C-contiguous; there is no broadcasting and no CPU fallback.
 """

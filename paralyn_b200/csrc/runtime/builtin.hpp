@@ -35,7 +35,7 @@ struct BoundArg {
 // Per-context matmul summation modes (paralyn/b200.h).
 enum MatmulMode : uint32_t {
   matmul_auto = 0,
-  matmul_reference = 1, // fl(fl(a*b) + sum), strictly increasing k: bit-exact with the checker
+  matmul_reference = 1, // fl(fl(a*b) + sum), strictly increasing k: bit-exact with the reference's sequential checker
   matmul_ffma = 2,      // fma(a, b, sum), strictly increasing k
   matmul_tf32x3 = 3,    // 3xTF32 split products on tcgen05, FP32 accumulation in TMEM
 };

@@ -1076,7 +1076,7 @@ std::shared_ptr<Engine> create_engine(const std::string &selector) {
     throw Error(Code::invalid_device, "The HIP/ROCm backend is not implemented.");
   } else if (selector != "auto") {
     throw Error(Code::invalid_device,
-                "This build has no Metal backend; select a CUDA device with cuda:INDEX or auto. "
+                "This library has no Metal backend; select a CUDA device with cuda:INDEX or auto. "
                 "There is no CPU fallback.");
   }
   const auto &status = backend_status();
@@ -1089,7 +1089,7 @@ std::shared_ptr<Engine> create_engine(const std::string &selector) {
                                           " device(s) reported by the driver)");
   const auto &d = list[ordinal];
   if (d.cc_major != 10 || d.cc_minor != 0)
-    throw Error(Code::unsupported, "This build carries sm_100a kernels only; device " + d.name +
+    throw Error(Code::unsupported, "This library carries sm_100a kernels only; device " + d.name +
                                        " has compute capability " + std::to_string(d.cc_major) +
                                        "." + std::to_string(d.cc_minor));
   return std::make_shared<Engine>(d);

@@ -183,7 +183,7 @@ private:
   uint32_t matmul_mode_ = matmul_auto;
 };
 
-// "cuda:K" or "auto" (cuda:0). Metal/HIP selectors are unavailable in this build.
+// "cuda:K" or "auto" (cuda:0). Metal/HIP selectors are unavailable in this library.
 std::shared_ptr<Engine> create_engine(const std::string &selector);
 
 // JSON-lines runtime events to PARALYN_EVENT_LOG, progress to PARALYN_RUNTIME_LOG

@@ -1,7 +1,7 @@
 """Writer for the verified-IR module container (.prk) used by the array operators.
 
 The reference builds operators.prk by compiling bindings/python/operators.cu with
-its Clang frontend (bindings/python/operators.cu:3-16). This build has no frontend:
+its Clang frontend (bindings/python/operators.cu:3-16). This library has no frontend:
 the same kernels are constructed here as IR trees, exactly as the reference's
 codegen tests build them by hand (tests/cuda/codegen_tests.cpp:53-76), and written
 in container format 1 (compiler/ir/artifact.cpp:248-273: magic "PARALYN\\0",

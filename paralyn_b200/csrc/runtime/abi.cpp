@@ -797,6 +797,65 @@ PB_EXPORT pr_status pr_launch(pr_queue q, pr_kernel h, pr_dim3 grid, pr_dim3 blo
   });
 }
 
+namespace pb {
+pr_status launch_entry(pr_queue q, pr_module m, const char *name, pr_dim3 grid, pr_dim3 block,
+                       const RangeArgument *args, uint32_t count, pr_event *out) noexcept {
+  return api("launch", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    auto queue = get<QueueObj>(q, HandleKind::queue);
+    auto module = get<ModuleObj>(m, HandleKind::module);
+    require(queue->owner == module->owner, PR_CONTEXT_MISMATCH, "Queue and kernel belong to different contexts");
+    const Entry *entry = nullptr;
+    for (const auto &e : module->entries)
+      if (e.name == name) {
+        entry = &e;
+        break;
+      }
+    require(entry, PR_INVALID_ARGUMENT, "Module has no entrypoint with that name");
+    require(count == entry->params.size(), PR_INVALID_ARGUMENT, "Kernel argument count mismatch");
+    require(args || !count, PR_INVALID_ARGUMENT, "Missing kernel arguments");
+    std::vector<BoundArg> bound(count);
+    std::vector<std::shared_ptr<Allocation>> retained;
+    retained.reserve(count);
+    for (uint32_t i = 0; i < count; ++i) {
+      const auto &p = entry->params[i];
+      const auto &a = args[i];
+      if (p.buffer) {
+        require(a.arg.type == PR_BUFFER, PR_INVALID_ARGUMENT, "Expected a buffer-view argument");
+        auto buffer = get<BufferObj>(a.buffer, HandleKind::buffer);
+        require(buffer->owner == queue->owner, PR_CONTEXT_MISMATCH, "View belongs to a different context");
+        range(buffer->allocation->bytes, a.offset, a.bytes);
+        require(a.offset % 4 == 0 && a.bytes % 4 == 0 && a.bytes >= 4, PR_INVALID_ARGUMENT,
+                "Typed kernel view must have four-byte alignment and size");
+        require((a.access & p.access) == p.access, PR_INVALID_ARGUMENT,
+                "View access does not allow the kernel's reads/writes");
+        bound[i].buffer = true;
+        bound[i].writes = (p.access & PR_WRITE) != 0;
+        bound[i].ptr = static_cast<char *>(buffer->allocation->ptr) + a.offset;
+        bound[i].bytes = bytes(a.bytes);
+        retained.push_back(buffer->allocation);
+      } else {
+        require(a.arg.type == public_type(p.type), PR_INVALID_ARGUMENT, "Kernel scalar type mismatch");
+        if (a.arg.type == PR_I32)
+          std::memcpy(&bound[i].bits, &a.arg.i32, 4);
+        else if (a.arg.type == PR_U32)
+          bound[i].bits = a.arg.u32;
+        else
+          std::memcpy(&bound[i].bits, &a.arg.f32, 4);
+      }
+    }
+    const Builtin &b = *entry->builtin;
+    if (b.required_block[0])
+      require(block.x == b.required_block[0] && block.y == b.required_block[1] && block.z == b.required_block[2],
+              PR_INVALID_ARGUMENT, "Launch block does not match the entry's required block");
+    const Dim3 g{grid.x, grid.y, grid.z}, bl{block.x, block.y, block.z};
+    queue->owner->engine->check_geometry(g, bl);
+    *out = submit_locked(queue, entry->name, b.launch, g, bl, std::move(bound), std::move(retained), entry->jit);
+  });
+}
+} // namespace pb
+
 PB_EXPORT pr_status pr_event_wait(pr_event h, pr_event_info *out) {
   return api("event_wait", [&] {
     auto event = get<EventObj>(h, HandleKind::event);

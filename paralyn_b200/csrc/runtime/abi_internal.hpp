@@ -61,6 +61,18 @@ pr_event submit_marker(pr_queue queue);
 pr_event submit_transfer(pr_queue queue, pr_buffer buffer, uint64_t offset, void *host,
                          uint64_t bytes, bool to_device);
 double event_elapsed(pr_event first, pr_event second);
+// pr_launch for in-library callers without view or kernel handles: the entry is
+// named in `module`, and each buffer argument is a (buffer, offset, bytes, access)
+// range checked as pr_view_create would (alignment 4) and bound like a view. One
+// lock for the whole submission.
+struct RangeArgument {
+  pr_argument arg{};      // type and, for scalars, the value
+  pr_buffer buffer = 0;   // buffer arguments
+  uint64_t offset = 0, bytes = 0;
+  pr_access access = PR_READ;
+};
+pr_status launch_entry(pr_queue queue, pr_module module, const char *name, pr_dim3 grid, pr_dim3 block,
+                       const RangeArgument *args, uint32_t count, pr_event *out) noexcept;
 pr_handle add_object(std::shared_ptr<void> object, HandleKind kind, const void *context);
 std::shared_ptr<void> get_object(pr_handle handle, HandleKind kind, const void **context);
 

@@ -53,16 +53,16 @@ template <class F> pr_status boundary(const char *operation, F &&fn) noexcept {
   }
 }
 
-// Provider-owned temporary handle (views, kernels); the launch retains what it needs.
+// A kernel entry of the provider module, or a buffer range bound as a kernel
+// argument. Neither holds a library handle: launch_entry resolves both under one
+// lock, checking each range as pr_view_create would (the launch retains the
+// allocations it uses).
 struct Owned {
-  pr_handle handle = 0;
-  Owned() = default;
-  Owned(const Owned &) = delete;
-  Owned &operator=(const Owned &) = delete;
-  ~Owned() {
-    if (handle)
-      pr_release(handle);
-  }
+  pr_module module = 0;
+  const char *name = nullptr;
+  pr_buffer buffer = 0;
+  uint64_t offset = 0, bytes = 0;
+  pr_access access = PR_READ;
 };
 
 struct Layout {
@@ -237,43 +237,73 @@ void same_context(pr_queue queue, pr_module operators,
       fail(PR_CONTEXT_MISMATCH, std::string(t.second) + ": tensor buffer belongs to a different context");
 }
 
-// Resolves an entry and checks its schema against the provider table.
+// Resolves an entry and checks its schema against the provider table, once per
+// (module, entry): module handles are never reused, so a checked pair stays valid
+// for as long as the handle is live (launch_entry rejects it once released).
+std::mutex schema_mutex;
+std::vector<std::pair<pr_module, const char *>> &checked_schemas() {
+  static std::vector<std::pair<pr_module, const char *>> value;
+  return value;
+}
 void kernel(pr_module operators, const char *name, Owned &out) {
+  out.module = operators;
+  out.name = name;
+  {
+    std::lock_guard<std::mutex> lock(schema_mutex);
+    for (const auto &c : checked_schemas())
+      if (c.first == operators && !std::strcmp(c.second, name))
+        return;
+  }
+  struct Handle {
+    pr_kernel value = 0;
+    ~Handle() {
+      if (value)
+        pr_release(value);
+    }
+  } fn;
   const Builtin *entry = find_builtin(name);
-  call(pr_module_kernel(operators, name, &out.handle));
+  call(pr_module_kernel(operators, name, &fn.value));
   uint32_t count = 0;
-  call(pr_kernel_parameter_count(out.handle, &count));
+  call(pr_kernel_parameter_count(fn.value, &count));
   bool same = entry && count == entry->params.size();
   for (uint32_t i = 0; same && i < count; ++i) {
     pr_parameter_info info{};
-    call(pr_kernel_parameter(out.handle, i, &info));
+    call(pr_kernel_parameter(fn.value, i, &info));
     const auto &p = entry->params[i];
     same = !std::strcmp(info.name, p.name.c_str()) && info.is_buffer == uint32_t(p.buffer) &&
            info.type == (p.type == Scalar::F32 ? PR_F32 : PR_U32);
   }
   require(same, PR_INVALID_ARGUMENT,
           "Module is not the tensor operator provider (load it with pr_tensor_operators_load)");
+  std::lock_guard<std::mutex> lock(schema_mutex);
+  checked_schemas().emplace_back(operators, entry->name);
 }
 
 void view(const pr_tensor_desc_v1 *d, const Layout &l, pr_access access, Owned &out) {
-  call(pr_view_create(d->buffer, d->byte_offset, l.bytes, 4, access, &out.handle));
+  out.buffer = d->buffer;
+  out.offset = d->byte_offset;
+  out.bytes = l.bytes;
+  out.access = access;
 }
-pr_argument buffer(const Owned &v) {
-  pr_argument a{};
-  a.type = PR_BUFFER;
-  a.view = v.handle;
+RangeArgument buffer(const Owned &v) {
+  RangeArgument a;
+  a.arg.type = PR_BUFFER;
+  a.buffer = v.buffer;
+  a.offset = v.offset;
+  a.bytes = v.bytes;
+  a.access = v.access;
   return a;
 }
-pr_argument u32(uint64_t value) {
-  pr_argument a{};
-  a.type = PR_U32;
-  a.u32 = uint32_t(value);
+RangeArgument u32(uint64_t value) {
+  RangeArgument a;
+  a.arg.type = PR_U32;
+  a.arg.u32 = uint32_t(value);
   return a;
 }
-pr_argument f32(float value) {
-  pr_argument a{};
-  a.type = PR_F32;
-  a.f32 = value;
+RangeArgument f32(float value) {
+  RangeArgument a;
+  a.arg.type = PR_F32;
+  a.arg.f32 = value;
   return a;
 }
 pr_dim3 linear(uint64_t count) { return {uint32_t((count + group - 1) / group), 1, 1}; }
@@ -419,17 +449,17 @@ PB_EXPORT pr_status pr_matmul_f32(pr_queue queue, pr_module operators, const pr_
     Owned cv;
     view(op->c, c, PR_READ_WRITE, cv);
     if (!k) {
-      const std::array<pr_argument, 3> args{buffer(cv), u32(m * n), f32(0.0f)};
-      call(pr_launch(queue, fn.handle, linear(m * n), {group, 1, 1}, args.data(), 3, out));
+      const std::array<RangeArgument, 3> args{buffer(cv), u32(m * n), f32(0.0f)};
+      call(launch_entry(queue, fn.module, fn.name, linear(m * n), {group, 1, 1}, args.data(), 3, out));
       return;
     }
     Owned av, bv;
     view(op->a, a, PR_READ, av);
     view(op->b, b, PR_READ, bv);
-    const std::array<pr_argument, 8> args{buffer(av), buffer(bv), buffer(cv), u32(m), u32(n), u32(k),
+    const std::array<RangeArgument, 8> args{buffer(av), buffer(bv), buffer(cv), u32(m), u32(n), u32(k),
                                           u32(op->transpose_a), u32(op->transpose_b)};
     const pr_dim3 grid{uint32_t((n + tile - 1) / tile), uint32_t((m + tile - 1) / tile), 1};
-    call(pr_launch(queue, fn.handle, grid, {tile, tile, 1}, args.data(), 8, out));
+    call(launch_entry(queue, fn.module, fn.name, grid, {tile, tile, 1}, args.data(), 8, out));
   });
 }
 
@@ -471,12 +501,12 @@ PB_EXPORT pr_status pr_bias_activation_f32(pr_queue queue, pr_module operators,
     view(op->out, o, PR_READ_WRITE, ov);
     if (op->bias) {
       view(op->bias, bias, PR_READ, bv);
-      const std::array<pr_argument, 6> args{buffer(xv), buffer(bv), buffer(ov), u32(count),
+      const std::array<RangeArgument, 6> args{buffer(xv), buffer(bv), buffer(ov), u32(count),
                                             u32(columns), u32(op->activation)};
-      call(pr_launch(queue, fn.handle, linear(count), {group, 1, 1}, args.data(), 6, out));
+      call(launch_entry(queue, fn.module, fn.name, linear(count), {group, 1, 1}, args.data(), 6, out));
     } else {
-      const std::array<pr_argument, 4> args{buffer(xv), buffer(ov), u32(count), u32(op->activation)};
-      call(pr_launch(queue, fn.handle, linear(count), {group, 1, 1}, args.data(), 4, out));
+      const std::array<RangeArgument, 4> args{buffer(xv), buffer(ov), u32(count), u32(op->activation)};
+      call(launch_entry(queue, fn.module, fn.name, linear(count), {group, 1, 1}, args.data(), 4, out));
     }
   });
 }
@@ -510,20 +540,20 @@ PB_EXPORT pr_status pr_batched_matmul_f32(pr_queue queue, pr_module operators,
     view(op->c, c, PR_READ_WRITE, cv);
     const pr_dim3 grid{uint32_t((n + tile - 1) / tile), uint32_t((m + tile - 1) / tile), uint32_t(batch)};
     if (!k) { // the empty sum: +0.0 at every addressed output element
-      const std::array<pr_argument, 7> args{buffer(cv), u32(m), u32(n), u32(op->c->strides[0]),
+      const std::array<RangeArgument, 7> args{buffer(cv), u32(m), u32(n), u32(op->c->strides[0]),
                                             u32(op->c->strides[1]), u32(op->c->strides[2]), f32(0.0f)};
-      call(pr_launch(queue, fn.handle, grid, {tile, tile, 1}, args.data(), 7, out));
+      call(launch_entry(queue, fn.module, fn.name, grid, {tile, tile, 1}, args.data(), 7, out));
       return;
     }
     Owned av, bv;
     view(op->a, a, PR_READ, av);
     view(op->b, b, PR_READ, bv);
-    const std::array<pr_argument, 15> args{
+    const std::array<RangeArgument, 15> args{
         buffer(av), buffer(bv), buffer(cv), u32(m), u32(n), u32(k),
         u32(op->a->strides[0]), u32(op->a->strides[1]), u32(op->a->strides[2]),
         u32(op->b->strides[0]), u32(op->b->strides[1]), u32(op->b->strides[2]),
         u32(op->c->strides[0]), u32(op->c->strides[1]), u32(op->c->strides[2])};
-    call(pr_launch(queue, fn.handle, grid, {tile, tile, 1}, args.data(), 15, out));
+    call(launch_entry(queue, fn.module, fn.name, grid, {tile, tile, 1}, args.data(), 15, out));
   });
 }
 
@@ -550,14 +580,14 @@ PB_EXPORT pr_status pr_reduce_rows_f32(pr_queue queue, pr_module operators, cons
     view(op->out, o, PR_READ_WRITE, ov);
     if (!columns) { // empty rows: +0.0 (sum) or -inf (max), written on the GPU
       const float identity = op->op == PR_REDUCE_MAX ? -std::numeric_limits<float>::infinity() : 0.0f;
-      const std::array<pr_argument, 3> args{buffer(ov), u32(rows), f32(identity)};
-      call(pr_launch(queue, fn.handle, linear(rows), {group, 1, 1}, args.data(), 3, out));
+      const std::array<RangeArgument, 3> args{buffer(ov), u32(rows), f32(identity)};
+      call(launch_entry(queue, fn.module, fn.name, linear(rows), {group, 1, 1}, args.data(), 3, out));
       return;
     }
     Owned xv;
     view(op->x, x, PR_READ, xv);
-    const std::array<pr_argument, 4> args{buffer(xv), buffer(ov), u32(columns), u32(op->op)};
-    call(pr_launch(queue, fn.handle, {uint32_t(rows), 1, 1}, {group, 1, 1}, args.data(), 4, out));
+    const std::array<RangeArgument, 4> args{buffer(xv), buffer(ov), u32(columns), u32(op->op)};
+    call(launch_entry(queue, fn.module, fn.name, {uint32_t(rows), 1, 1}, {group, 1, 1}, args.data(), 4, out));
   });
 }
 
@@ -596,9 +626,9 @@ PB_EXPORT pr_status pr_softmax_rows_f32(pr_queue queue, pr_module operators, con
     Owned xv, ov;
     view(op->x, x, PR_READ, xv);
     view(op->out, o, PR_READ_WRITE, ov);
-    const std::array<pr_argument, 6> args{buffer(xv), buffer(ov), u32(columns), u32(rows), u32(op->causal),
+    const std::array<RangeArgument, 6> args{buffer(xv), buffer(ov), u32(columns), u32(rows), u32(op->causal),
                                           f32(op->scale)};
-    call(pr_launch(queue, fn.handle, {uint32_t(total_rows), 1, 1}, {group, 1, 1}, args.data(), 6, out));
+    call(launch_entry(queue, fn.module, fn.name, {uint32_t(total_rows), 1, 1}, {group, 1, 1}, args.data(), 6, out));
   });
 }
 
@@ -636,9 +666,9 @@ PB_EXPORT pr_status pr_layer_norm_f32(pr_queue queue, pr_module operators, const
     view(op->gamma, g, PR_READ, gv);
     view(op->beta, b, PR_READ, bv);
     view(op->out, o, PR_READ_WRITE, ov);
-    const std::array<pr_argument, 6> args{buffer(xv), buffer(gv), buffer(bv), buffer(ov),
+    const std::array<RangeArgument, 6> args{buffer(xv), buffer(gv), buffer(bv), buffer(ov),
                                           u32(columns), f32(op->epsilon)};
-    call(pr_launch(queue, fn.handle, {uint32_t(rows), 1, 1}, {group, 1, 1}, args.data(), 6, out));
+    call(launch_entry(queue, fn.module, fn.name, {uint32_t(rows), 1, 1}, {group, 1, 1}, args.data(), 6, out));
   });
 }
 
@@ -666,8 +696,8 @@ PB_EXPORT pr_status pr_add_f32(pr_queue queue, pr_module operators, const pr_add
     view(op->x, x, PR_READ, xv);
     view(op->y, y, PR_READ, yv);
     view(op->out, o, PR_READ_WRITE, ov);
-    const std::array<pr_argument, 4> args{buffer(xv), buffer(yv), buffer(ov), u32(x.count)};
-    call(pr_launch(queue, fn.handle, linear(x.count), {group, 1, 1}, args.data(), 4, out));
+    const std::array<RangeArgument, 4> args{buffer(xv), buffer(yv), buffer(ov), u32(x.count)};
+    call(launch_entry(queue, fn.module, fn.name, linear(x.count), {group, 1, 1}, args.data(), 4, out));
   });
 }
 

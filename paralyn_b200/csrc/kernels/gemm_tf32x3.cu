@@ -1038,11 +1038,15 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   const int bn = transposed ? 256 : tile_width(n);
   const int64_t k_pad = round_up(k, 32), dm_pad = round_up(dm, TM), dn_pad = round_up(dn, bn);
   const int64_t tiles_m = dm_pad / TM, tiles_n = dn_pad / bn, batch_b = sb ? batch : 1;
-  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || dm_pad / 32 > 65535 ||
-      dn_pad / 32 > 65535 || batch * dm_pad > INT32_MAX || batch_b * dn_pad > INT32_MAX)
-    return false; // grid limits and 32-bit TMA row coordinates
   const Form form = transposed ? Form::transposed : form_of(bn, raw_a && tiles_n <= 2);
   const bool a_split = !transposed && (form == Form::n64 || form == Form::n128 || form == Form::n256);
+  // Grid limits of the split passes (rows / 32 in grid.y) and 32-bit TMA row
+  // coordinates of the split operands; a raw operand is addressed by its own map.
+  const int64_t b_rows = transposed ? dm_pad : dn_pad;
+  if (tiles_m * tiles_n * batch > INT32_MAX || k_pad / TK > INT32_MAX || b_rows / 32 > 65535 ||
+      batch_b * b_rows > INT32_MAX || (a_split && (dm_pad / 32 > 65535 || batch * dm_pad > INT32_MAX)) ||
+      dm > INT32_MAX || dn > INT32_MAX)
+    return false;
   const UnitPlan plan = plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn);
   // Split operands in the workspace: A's pair [batch * m_pad][k_pad] unless A is
   // converted in shared memory; B's pair [batch_b * rows][k_pad], rows = n_pad

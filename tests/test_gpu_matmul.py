@@ -264,3 +264,26 @@ def test_a_split_in_shared_memory_equals_the_split_pass(context, m, n, k):
         assert np.all(np.abs(raw[rows].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
     finally:
         p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+def test_tallest_narrow_product_runs_on_the_tensor_cores(context, tmp_path):
+    # m = 1,048,560 (the most rows the reference's launch geometry, ceil(m/16) grid
+    # rows, admits) x 64 x 16: computed transposed, A's rows loaded raw as the 256-wide
+    # MMA side (4096 tiles of D).
+    import json
+    m, n, k = 65535 * 16, 64, 16
+    p.set_matmul_mode(context, p.MatmulMode.TF32X3)
+    try:
+        a = synthetic.uniform(9300, 0, m * k)
+        b = synthetic.uniform(9301, 0, k * n)
+        with p.tensor(a, shape=(m, k), context=context) as ta, p.tensor(b, shape=(k, n), context=context) as tb, \
+                p.matmul(ta, tb) as tc:
+            c = np.asarray(tc.to_host(), np.float32).reshape(m, n)
+        rows = np.unique(np.concatenate([np.arange(0, m, 9973), [m - 1]]))
+        exact, magnitude = oracle.matmul_exact(a.reshape(m, k)[rows].ravel(), b, len(rows), n, k)
+        assert np.all(np.abs(c[rows].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
+        context.write_evidence(str(tmp_path / "e"))
+        launches = json.loads((tmp_path / "e" / "execution.json").read_text())["launches"]
+        assert [l["variant"] for l in launches if l["kernel"] == "paralyn_matmul_f32"][-1] == "tcgen05_tf32x3"
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)

@@ -276,7 +276,10 @@ void kernel(pr_module operators, const char *name, Owned &out) {
   require(same, PR_INVALID_ARGUMENT,
           "Module is not the tensor operator provider (load it with pr_tensor_operators_load)");
   std::lock_guard<std::mutex> lock(schema_mutex);
-  checked_schemas().emplace_back(operators, entry->name);
+  auto &checked = checked_schemas();
+  if (checked.size() >= 1024) // handles of released modules accumulate: start over
+    checked.clear();
+  checked.emplace_back(operators, entry->name);
 }
 
 void view(const pr_tensor_desc_v1 *d, const Layout &l, pr_access access, Owned &out) {

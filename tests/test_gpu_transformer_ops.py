@@ -281,6 +281,37 @@ def test_softmax_specials(context, ops):
         assert np.isnan(got).all()
 
 
+@pytest.mark.parametrize("cols", [600, 1024, 2048, 2052])
+def test_softmax_specials_in_long_rows(context, ops, cols):
+    # Rows over 512 columns take the three-pass streamed kernel (the offset case the
+    # one-block-per-row kernel): a NaN or +inf in any
+    # visible column makes the row NaN, an all -inf row is NaN, -inf entries of a
+    # finite row become +0.0, and a NaN in a causally masked column never enters.
+    nan, inf = np.nan, np.inf
+    rng = np.random.default_rng(cols)
+    x = rng.uniform(-4, 4, (6, cols)).astype(np.float32)
+    x[0, cols - 3] = nan
+    x[1, 300] = inf
+    x[2, :] = -inf
+    x[3, ::3] = -inf
+    x[4, cols // 2] = nan  # row 4 of 6 with causal masking sees cols - 1 columns
+    x[5, 7] = -inf
+    for offsets in ((0, 0), (2, 1)):
+        got = softmax_case(context, ops, x, 1, 6, cols, 0.5, False, False, *offsets)
+        assert np.all(np.isnan(got[:3]))
+        assert np.all(got[3, ::3] == 0.0) and not np.any(np.signbit(got[3, ::3]))
+        value, error = oracle.softmax_bound(x[3:], np.float32(0.5))
+        assert np.all(oracle.within(got[3:6][:, :], value, error)[np.isfinite(value)])
+        # causal over 6 rows: row r keeps r + cols - 6 + 1 leading columns
+        xc = x.copy()
+        xc[4, cols - 1] = nan  # masked for row 4 (it keeps cols - 1 columns)
+        xc[4, cols // 2] = 1.0
+        got = softmax_case(context, ops, xc, 1, 6, cols, 0.5, True, False, *offsets)
+        assert not np.isnan(got[4]).any() and got[4, cols - 1] == 0.0
+        vc, ec = oracle.softmax_bound(xc, np.float32(0.5), causal=True)
+        assert np.all(oracle.within(got[4], vc[4], ec[4]))
+
+
 @pytest.mark.parametrize("scale,causal,shape,code", [
     (0.0, False, (2, 4), p.Status.INVALID_ARGUMENT), (float("inf"), False, (2, 4), p.Status.INVALID_ARGUMENT),
     (1.0, True, (4, 2), p.Status.INVALID_ARGUMENT)])

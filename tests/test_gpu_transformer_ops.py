@@ -204,6 +204,27 @@ def test_reduce_rows_mixed_magnitudes(context, ops, cols):
         reduce_case(context, ops, x, rows, cols, p.Reduce.SUM, *offsets)
 
 
+@pytest.mark.parametrize("cols", [700, 2048])
+def test_reduce_rows_specials_in_long_rows(context, ops, cols):
+    # The same special values spread over several 256-column chunks: each reference
+    # lane's chain, the tree and the NaN / signed-zero rules must hold across chunks.
+    nan, inf = np.nan, np.inf
+    rng = np.random.default_rng(cols)
+    x = rng.uniform(-2, 2, (6, cols)).astype(np.float32)
+    x[0, cols - 5] = nan
+    x[1, :] = -0.0
+    x[1, 257] = 0.0
+    x[2, :] = -0.0
+    x[3, 3] = inf
+    x[3, cols - 1] = -inf
+    x[4, :] = -inf
+    x[5, 100] = inf
+    x[5, 600 % cols] = inf
+    for offsets in ((0, 0), (1, 3)):
+        for op in (p.Reduce.SUM, p.Reduce.MAX):
+            reduce_case(context, ops, x.ravel(), 6, cols, op, *offsets)
+
+
 def test_reduce_rows_specials(context, ops):
     nan, inf = np.nan, np.inf
     x = np.array([[1, nan, -2, 3], [-0.0, 0.0, -0.0, -1], [-0.0, -0.0, -3, -1], [inf, -inf, 1, 2],

@@ -82,6 +82,31 @@ def test_nonfinite_policy(context):
     assert not np.isnan(out[3, :2]).any() and np.isnan(out[3, 2:]).all()
 
 
+@pytest.mark.parametrize("cols", [2048, 4096])
+def test_nonfinite_policy_in_wide_rows(context, cols):
+    # The same policy on the shared-memory streamed kernel (1024 < columns <= 4096):
+    # NaN / inf rows are all NaN, a constant row is exactly beta, and a NaN in gamma or
+    # beta reaches only its column; finite results equal the oracle bit for bit.
+    nan, inf = np.float32("nan"), np.float32("inf")
+    x = synthetic.normal(24, 0, 4 * cols, 0.5, 2.0).reshape(4, cols)
+    x[0, 1500] = nan
+    x[1, 3] = inf
+    x[2, :] = 5.0
+    g = synthetic.normal(25, 0, cols, 1.0, 0.25)
+    b = synthetic.normal(26, 0, cols, 0.0, 0.25)
+    g[2000 % cols] = nan
+    b[cols - 7] = nan
+    _, out = run(context, x, g, b, np.float32(1e-5))
+    want = oracle.layer_norm(x, g, b, np.float32(1e-5))
+    assert np.isnan(out[:2]).all()
+    bad = np.zeros(cols, bool)
+    bad[[2000 % cols, cols - 7]] = True
+    assert np.isnan(out[2:, bad]).all() and not np.isnan(out[2:, ~bad]).any()
+    assert out[2, ~bad].tobytes() == b[~bad].tobytes()
+    assert np.array_equal(np.isnan(out), np.isnan(want))
+    assert out[~np.isnan(want)].tobytes() == want[~np.isnan(want)].tobytes()
+
+
 def test_empty_shapes_make_no_event(context):
     for rows, cols in ((0, 8), (3, 0)):
         x = np.zeros((rows, cols), np.float32)

@@ -287,3 +287,28 @@ def test_tallest_narrow_product_runs_on_the_tensor_cores(context, tmp_path):
         assert [l["variant"] for l in launches if l["kernel"] == "paralyn_matmul_f32"][-1] == "tcgen05_tf32x3"
     finally:
         p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+@pytest.mark.parametrize("mode", (p.MatmulMode.REFERENCE, p.MatmulMode.FFMA, p.MatmulMode.TF32X3))
+def test_nonfinite_inputs_per_mode(context, mode):
+    # Row 0 of A holds +inf, row 1 a NaN, the rest finite; B is finite and nonzero.
+    # REFERENCE / FFMA: row 0 is +-inf (IEEE, sequential order), row 1 NaN. TF32X3: the
+    # infinite operand's low half is inf - inf, so row 0 is NaN as well. Rows without
+    # exceptional inputs are unaffected in every mode.
+    m, n, k = 130, 70, 64
+    a = synthetic.uniform(9400, 0, m * k).reshape(m, k)
+    b = np.abs(synthetic.uniform(9401, 0, k * n).reshape(k, n)) + np.float32(0.5)
+    a[0, 5] = np.inf
+    a[1, 9] = np.nan
+    p.set_matmul_mode(context, mode)
+    try:
+        c = aligned_matmul(context, a, b, m, n, k, False)
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)
+    assert np.isnan(c[1]).all()
+    if mode == p.MatmulMode.TF32X3:
+        assert np.isnan(c[0]).all()
+    else:
+        assert np.all(c[0] == np.inf)
+    exact, magnitude = oracle.matmul_exact(a[2:].ravel(), b.ravel(), m - 2, n, k)
+    assert np.all(np.abs(c[2:].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))

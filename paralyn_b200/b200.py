@@ -3,7 +3,7 @@ import ctypes as _c
 from enum import IntEnum
 
 from .native import Context, Event, Queue
-from .tensor import TensorDescRecord, _api
+from .tensor import TensorDescRecord, _api, _pointer
 
 UNIFORM, NORMAL = 0, 1
 
@@ -105,9 +105,9 @@ def layer_norm_gather_into(queue, operators, x, gamma, beta, out, gathered, *, r
     lib = _b200(queue._lib)
     descs = [d._native() for d in (x, gamma, beta, out)]
     record = LayerNormRecord(_c.sizeof(LayerNormRecord), TENSOR_VERSION_1, float(epsilon), 0,
-                             *(_c.pointer(d) for d in descs))
+                             *(_pointer(d) for d in descs))
     natives = [g._native() for g in gathered]
-    array = (_c.POINTER(TensorDescRecord) * max(1, len(natives)))(*(_c.pointer(d) for d in natives))
+    array = (_c.POINTER(TensorDescRecord) * max(1, len(natives)))(*(_pointer(d) for d in natives))
     handle = _c.c_uint64()
     lib.check(lib.api.pr_b200_layer_norm_gather_f32(queue.handle, operators.handle, _c.byref(record), array,
                                                     len(natives), row_offset, _c.byref(handle)))
@@ -181,7 +181,7 @@ def matmul_bias_activation_into(queue, operators, a, b, c, bias, *, m, n, k, tra
     lib = _b200(queue._lib)
     descs = [x._native() for x in (a, b, c)]
     record = MatmulRecord(_c.sizeof(MatmulRecord), TENSOR_VERSION_1, m, n, k, int(bool(transpose_a)),
-                          int(bool(transpose_b)), *(_c.pointer(d) for d in descs))
+                          int(bool(transpose_b)), *(_pointer(d) for d in descs))
     bias_native = bias._native() if bias is not None else None
     handle = _c.c_uint64()
     lib.check(lib.api.pr_b200_matmul_bias_activation_f32(

@@ -233,6 +233,14 @@ def _real(value, label):
     return float(value)
 
 
+def _pointer(record):
+    """A ctypes pointer to a descriptor record, made once per record."""
+    pointer = getattr(record, "_pointer", None)
+    if pointer is None:
+        pointer = record._pointer = _c.pointer(record)
+    return pointer
+
+
 def _submit(queue, operators, name, record):
     if not isinstance(queue, Queue) or not isinstance(operators, Module):
         raise TypeError(f"{name} requires a Queue and the tensor operator Module")
@@ -248,7 +256,7 @@ def matmul_into(queue, operators, a, b, c, *, m, n, k, transpose_a=False, transp
     record = MatmulRecord(_c.sizeof(MatmulRecord), TENSOR_VERSION_1,
                           _int(m, 0, (1 << 64) - 1, "m"), _int(n, 0, (1 << 64) - 1, "n"),
                           _int(k, 0, (1 << 64) - 1, "k"), _flag(transpose_a, "transpose_a"),
-                          _flag(transpose_b, "transpose_b"), *(_c.pointer(d) for d in descs))
+                          _flag(transpose_b, "transpose_b"), *(_pointer(d) for d in descs))
     return _submit(queue, operators, "pr_matmul_f32", record)
 
 
@@ -257,8 +265,8 @@ def bias_activation_into(queue, operators, x, bias, out, *, activation=Activatio
     xd, od = x._native(), out._native()
     bd = bias._native() if bias is not None else None
     record = BiasActivationRecord(_c.sizeof(BiasActivationRecord), TENSOR_VERSION_1,
-                                  int(Activation(activation)), 0, _c.pointer(xd),
-                                  _c.pointer(bd) if bd is not None else None, _c.pointer(od))
+                                  int(Activation(activation)), 0, _pointer(xd),
+                                  _pointer(bd) if bd is not None else None, _pointer(od))
     return _submit(queue, operators, "pr_bias_activation_f32", record)
 
 
@@ -268,7 +276,7 @@ def batched_matmul_into(queue, operators, a, b, c, *, batch, m, n, k):
     record = BatchedMatmulRecord(_c.sizeof(BatchedMatmulRecord), TENSOR_VERSION_1,
                                  *(_int(v, 0, (1 << 64) - 1, label) for v, label in
                                    ((batch, "batch"), (m, "m"), (n, "n"), (k, "k"))),
-                                 *(_c.pointer(d) for d in descs))
+                                 *(_pointer(d) for d in descs))
     return _submit(queue, operators, "pr_batched_matmul_f32", record)
 
 
@@ -276,7 +284,7 @@ def reduce_rows_into(queue, operators, x, out, *, op=Reduce.SUM):
     """out[i] = sum or max of row i of x [rows, columns] in the fixed 256-lane order."""
     xd, od = x._native(), out._native()
     record = ReduceRowsRecord(_c.sizeof(ReduceRowsRecord), TENSOR_VERSION_1, int(Reduce(op)), 0,
-                              _c.pointer(xd), _c.pointer(od))
+                              _pointer(xd), _pointer(od))
     return _submit(queue, operators, "pr_reduce_rows_f32", record)
 
 
@@ -284,7 +292,7 @@ def softmax_rows_into(queue, operators, x, out, *, scale=1.0, causal=False):
     """Row softmax of scale*x over the last dimension of a rank-2 or rank-3 descriptor."""
     xd, od = x._native(), out._native()
     record = SoftmaxRowsRecord(_c.sizeof(SoftmaxRowsRecord), TENSOR_VERSION_1, _flag(causal, "causal"),
-                               _real(scale, "scale"), _c.pointer(xd), _c.pointer(od))
+                               _real(scale, "scale"), _pointer(xd), _pointer(od))
     return _submit(queue, operators, "pr_softmax_rows_f32", record)
 
 
@@ -292,14 +300,14 @@ def layer_norm_into(queue, operators, x, gamma, beta, out, *, epsilon=1e-5):
     """LayerNorm over the last dimension of x [rows, columns] with gamma/beta [columns]."""
     descs = [d._native() for d in (x, gamma, beta, out)]
     record = LayerNormRecord(_c.sizeof(LayerNormRecord), TENSOR_VERSION_1, _real(epsilon, "epsilon"), 0,
-                             *(_c.pointer(d) for d in descs))
+                             *(_pointer(d) for d in descs))
     return _submit(queue, operators, "pr_layer_norm_f32", record)
 
 
 def add_into(queue, operators, x, y, out):
     """Elementwise out = x + y for equal-shape contiguous descriptors."""
     descs = [d._native() for d in (x, y, out)]
-    record = AddRecord(_c.sizeof(AddRecord), TENSOR_VERSION_1, *(_c.pointer(d) for d in descs))
+    record = AddRecord(_c.sizeof(AddRecord), TENSOR_VERSION_1, *(_pointer(d) for d in descs))
     return _submit(queue, operators, "pr_add_f32", record)
 
 

@@ -52,3 +52,13 @@ def test_reference_mlp_example(tmp_path, mode):
 def test_reference_transformer_block_example(tmp_path, mode):
     out = run_example("native_transformer_block", ["--artifacts", str(tmp_path)], {"PARALYN_MATMUL_MODE": mode})
     assert "Verification: PASS" in out
+
+
+def test_reference_transformer_block_example_on_tensor_cores(tmp_path):
+    # T=128, d=128, 4 heads, d_ff=512: AUTO runs the QKV and MLP up-projections on the
+    # 3xTF32 kernel. (From d_model = 256 the example's own end-to-end bound evaluates to
+    # NaN in every mode, the bit-exact reference order included, so it cannot pass.)
+    out = run_example("native_transformer_block", ["--tokens", "128", "--model", "128", "--heads", "4",
+                                                   "--ff", "512", "--artifacts", str(tmp_path)],
+                      {"PARALYN_MATMUL_MODE": "auto"}, timeout=1200)
+    assert "Verification: PASS" in out

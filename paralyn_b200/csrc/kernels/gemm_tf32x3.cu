@@ -431,23 +431,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 
-// Persistent form: one CTA per SM walks the tiles blockIdx.x, + gridDim.x, ...
-// The shared-memory ring runs continuously across tiles (one k-slice counter
-// for producer and MMA), and the accumulator is double-buffered in TMEM (2 x 256
-// of the 512 columns): the MMA thread computes tile j into buffer j % 2 while
-// the epilogue warps drain tile j - 1 from the other buffer, so stores of C
-// overlap the tensor-core work instead of following it.
-//   tmem_full[b]  MMA -> epilogue: all MMAs of the buffer's current tile are done
-//                 (tcgen05.commit); phase u = the u-th tile that used buffer b
-//   tmem_empty[b] epilogue -> MMA: the four epilogue warps have read buffer b
-//                 (one elected lane per warp arrives; count 4)
+// Persistent form: one CTA per SM walks the work units blockIdx.x, + gridDim.x, ...
+// The shared-memory ring runs continuously across units (one k-slice counter
+// for producer and MMA), and the accumulator is double-buffered in TMEM (2 x BN
+// columns): the MMA thread computes unit j into buffer j % 2 while the epilogue
+// warps drain unit j - 1 from the other buffer, so stores of C overlap the
+// tensor-core work instead of following it.
+//   tmem_full[b]  MMA -> epilogue: all MMAs of the buffer's current unit are done
+//                 (tcgen05.commit); phase u = the u-th unit that used buffer b
+//   tmem_empty[b] epilogue -> MMA: the eight epilogue warps have read buffer b
+//                 (one elected lane per warp arrives; count 8)
 // Every wait is bounded as in the one-tile kernel; before TMEM is freed the MMA
 // thread's final commit guarantees no MMA is still writing it.
-// Epilogue stores are coalesced: each warp passes its 32x32 accumulator chunk
-// (thread = row) through a shared-memory tile with 36-float rows (16-byte aligned,
-// bank-conflict-free for 128-bit accesses by each quarter warp) and writes it
-// back with 128-bit stores, eight threads per 128-byte row segment, four rows per
-// instruction.
+// Epilogue stores are coalesced: each warp passes 32 x 16 accumulator chunks
+// (thread = row) through a shared-memory tile with 20-float rows (16-byte aligned;
+// its writes and its reads by groups of eight lanes touch eight distinct 4-bank
+// groups) and writes them back with 128-bit stores, four threads per 64-byte row
+// segment, eight rows per instruction.
 // ---- persistent kernel ----
 // One CTA per SM walks work units (whole tiles, then k-ranges of the tiles of a
 // short last round). The N tile width BN is 64, 128 or 256 (the narrow tiles keep

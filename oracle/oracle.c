@@ -11,7 +11,7 @@
  *
  *   orc_add_f32            bindings/python/operators.cu:3-8 (array_add),
  *                          runtime/tensor.cpp:302-308 (paralyn_add_f32)
- *   orc_affine_f32         bindings/python/operators.cu:10-16; the checker in
+ *   orc_affine_f32         bindings/python/operators.cu:10-16; the verifier in
  *                          scripts/qualify_cuda.py:93 is f32(f32(a*s)+b)
  *   orc_layer_norm_f32     runtime/tensor.cpp:276-299 with the 256-lane tree of
  *                          runtime/tensor.cpp:200-212; the tree emulation follows

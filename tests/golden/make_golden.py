@@ -27,7 +27,7 @@ Contents (inputs are seeded synthetic data from paralyn_b200.synthetic):
   prk_emit_cuda_sha256        SHA-256 of the CUDA the reference's codegen emits for
                               paralyn_b200.prk.operators() (must equal the reference's
                               reviewed goldens tests/cuda/golden/array_{add,affine}.cu)
-The GPU box has no reference checkout, so the GPU tests read these vectors.
+GPU machines have no reference checkout, so the GPU tests read these vectors.
 """
 import ctypes
 import hashlib

@@ -4,7 +4,7 @@ The drop-in claim at the binding level: with PARALYN_LIBRARY pointing at
 libparalyn_native.so from this repository, the reference package loads it (its ABI
 check and signature tables, reference bindings/python/paralyn/__init__.py:137-177),
 and its device-free calls behave as on the reference. Runs only where the reference
-checkout exists (this container); the GPU box has no reference checkout.
+checkout exists; GPU machines have no reference checkout.
 """
 import os
 import subprocess

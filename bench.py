@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="chain: skip the other benchmark configurations measured beside the headline")
     ap.add_argument("--matmul-mode", default="auto", choices=("auto", "reference", "ffma", "tf32x3"),
                     help="summation mode of the GEMM workloads (default auto: the 3xTF32 tensor-core kernel)")
     ap.add_argument("--gather", action="store_true",
@@ -173,6 +175,63 @@ class Clocks:
                 "samples": len(mhz)}
 
 
+# ---------------------------------------------------------------- workload descriptions (no device needed)
+def describe(name, world, rank, gather=False):
+    """(metric, unit, scaling, config) of a workload for `rank` of `world`; the same
+    dict for both arms, so the two lines name one configuration."""
+    from paralyn_b200 import shard
+    if name == "chain":
+        r0, r1 = shard.row_range(65536, world, rank)
+        config = {"workload": "chain: Y = LayerNorm(X W), X[65536x4096] ~ N(0,1), W[4096x4096] ~ N(0,1/4096), "
+                              "gamma=1, beta=0, eps=1e-5, seed 4",
+                  "rows": 65536, "k": 4096, "n": 4096, "rows_per_gpu": r1 - r0, "parallelism": f"rows{world}",
+                  "l2": "inputs larger than L2 (X shard >= 128 MiB)"}
+        if gather:
+            config["gathered_output"] = "Y gathered on every GPU by the fused LayerNorm (NVLink stores)"
+        return METRICS[name], "TFLOP/s", "strong", config
+    if name == "gemm":
+        r0, r1 = shard.row_range(4096, world, rank)
+        return METRICS[name], "TFLOP/s", "strong", {
+            "workload": "gemm: C = A B, M=N=K=4096, A,B ~ U[-1,1), seed 3", "m": 4096, "n": 4096, "k": 4096,
+            "rows_per_gpu": r1 - r0, "parallelism": f"rows{world}",
+            "l2": "operands are 64 MiB each; A/B re-reads are part of the GEMM"}
+    if name == "layernorm":
+        r0, r1 = shard.row_range(16384, world, rank)
+        return METRICS[name], "GB/s", "strong", {
+            "workload": "layernorm: X[16384x4096] ~ N(0,1), gamma ~ N(1,.02), beta ~ N(0,.02), eps 1e-5, seed 2",
+            "rows_per_gpu": r1 - r0, "cols": 4096, "parallelism": f"rows{world}",
+            "l2": "inputs larger than L2 (256 MiB)"}
+    if name == "affine":
+        return METRICS[name], "GB/s", "weak", {
+            "workload": "affine: y = alpha x + beta, n = 2^26, x ~ U[-4,4), alpha 1.5, beta -0.25, seed 1",
+            "bytes_per_element": 8, "parallelism": f"replica{world}", "l2": "inputs larger than L2 (256 MiB)"}
+    if name == "add":
+        return METRICS[name], "GB/s", "weak", {
+            "workload": "add: c = a + b, n = 1,048,576, a,b ~ U[-1,1), seed 0", "bytes_per_element": 12,
+            "parallelism": f"replica{world}", "l2": "16 rotating buffer sets (192 MiB) exceed L2"}
+    if name == "softmax":
+        return METRICS[name], "GB/s", "weak", {
+            "workload": "softmax: causal row softmax of x [32, 1024, 1024] ~ U[-8,8), scale 1/8, seed 5",
+            "parallelism": f"replica{world}", "l2": "inputs larger than L2 (128 MiB)"}
+    if name == "reduce":
+        return METRICS[name], "GB/s", "weak", {
+            "workload": "reduce: row sums of x [65536 x 1024] ~ U[-4,4), seed 6", "parallelism": f"replica{world}",
+            "l2": "inputs larger than L2 (256 MiB)"}
+    if name == "block":
+        return METRICS[name], "TFLOP/s", "weak", {
+            "workload": "block: pre-LN encoder block (reference examples/native/transformer_block), T=2048, d=1024, "
+                        "16 heads of 64, d_ff=4096, causal, seeded weights; 11 launches per block (bias/GELU fused "
+                        "into the GEMM epilogues)",
+            "tokens": 2048, "d_model": 1024, "heads": 16, "d_ff": 4096, "parallelism": f"replica{world}",
+            "l2": "scores and probabilities 256 MiB each exceed L2"}
+    if name == "attention":
+        return METRICS[name], "TFLOP/s", "weak", {
+            "workload": "attention: S = Q K^T per head, Q, K [32, 2048, 128] ~ U[-1,1), seed 7; K^T is a strided "
+                        "view (no copy)", "batch": 32, "m": 2048, "n": 2048, "k": 128,
+            "parallelism": f"replica{world}", "l2": "output 512 MiB exceeds L2"}
+    raise ValueError(name)
+
+
 # ---------------------------------------------------------------- workloads (our implementation)
 class Workload:
     """Holds device inputs/outputs for one rank and runs steps through the public API."""
@@ -197,14 +256,6 @@ class Workload:
                 self.gather = shard.GatheredOutput(ctx, self.rows, self.n, group.exchange, rank)
             self.units_total = 2 * self.rows * self.n * self.k
             self.units_local = self.chain.flops()
-            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "strong"
-            self.metric = "FP32 GEMM+LayerNorm chain throughput (GEMM TFLOP/s)"
-            self.config = {"workload": "chain: Y = LayerNorm(X W), X[65536x4096] ~ N(0,1), W[4096x4096] ~ N(0,1/4096), "
-                                       "gamma=1, beta=0, eps=1e-5, seed 4",
-                           "rows": self.rows, "k": self.k, "n": self.n, "rows_per_gpu": self.chain.local_rows,
-                           "parallelism": f"rows{world}", "l2": "inputs larger than L2 (X shard >= 128 MiB)"}
-            if self.gather:
-                self.config["gathered_output"] = "Y gathered on every GPU by the fused LayerNorm (NVLink stores)"
             self.h2d = 4 * self.chain.local_rows * self.k
             self.d2h = 4 * self.chain.local_rows * self.n
         elif name == "gemm":
@@ -220,11 +271,6 @@ class Workload:
                 e.wait()
                 e.close()
             self.units_total, self.units_local = 2 * m * n * k, 2 * self.m_local * n * k
-            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "strong"
-            self.metric = "FP32 GEMM TFLOP/s (4096^3, rows sharded)"
-            self.config = {"workload": "gemm: C = A B, M=N=K=4096, A,B ~ U[-1,1), seed 3", "m": m, "n": n, "k": k,
-                           "rows_per_gpu": self.m_local, "parallelism": f"rows{world}",
-                           "l2": "operands are 64 MiB each; A/B re-reads are part of the GEMM"}
             self.h2d, self.d2h = 4 * self.m_local * k, 4 * self.m_local * n
         elif name == "layernorm":
             rows, cols = 16384, 4096
@@ -245,11 +291,6 @@ class Workload:
                 e.close()
             self.units_total = 2 * rows * cols * 4 + 2 * cols * 4 * world
             self.units_local = 2 * self.rows_local * cols * 4 + 2 * cols * 4
-            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "strong"
-            self.metric = "FP32 row LayerNorm HBM GB/s (16384x4096, rows sharded)"
-            self.config = {"workload": "layernorm: X[16384x4096] ~ N(0,1), gamma ~ N(1,.02), beta ~ N(0,.02), eps 1e-5, seed 2",
-                           "rows_per_gpu": self.rows_local, "cols": cols, "parallelism": f"rows{world}",
-                           "l2": "inputs larger than L2 (256 MiB)"}
             self.h2d = self.d2h = 4 * self.rows_local * cols
         elif name == "affine":
             self.count = 1 << 26
@@ -263,11 +304,6 @@ class Workload:
             self.xv, self.yv = self.x.view(access=p.Access.READ), self.y.view(access=p.Access.WRITE)
             self.units_local = 8 * self.count
             self.units_total = self.units_local * world
-            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
-            self.metric = "FP32 affine y = 1.5x - 0.25 HBM GB/s (n = 2^26)"
-            self.config = {"workload": "affine: y = alpha x + beta, n = 2^26, x ~ U[-4,4), alpha 1.5, beta -0.25, seed 1",
-                           "bytes_per_element": 8, "parallelism": f"replica{world}",
-                           "l2": "inputs larger than L2 (256 MiB)"}
             self.h2d = self.d2h = 4 * self.count
         elif name == "add":
             self.count, self.sets = 1 << 20, 16
@@ -285,11 +321,6 @@ class Workload:
                                   c.view(access=p.Access.WRITE)))
             self.units_local = 12 * self.count
             self.units_total = self.units_local * world
-            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
-            self.metric = "FP32 vector add HBM GB/s (n = 2^20)"
-            self.config = {"workload": "add: c = a + b, n = 1,048,576, a,b ~ U[-1,1), seed 0", "bytes_per_element": 12,
-                           "parallelism": f"replica{world}",
-                           "l2": "16 rotating buffer sets (192 MiB) exceed L2"}
             self.h2d, self.d2h = 8 * self.count, 4 * self.count
             self.turn = 0
         elif name in ("softmax", "reduce"):
@@ -298,15 +329,11 @@ class Workload:
                 self.shape = (32, 1024, 1024)
                 count = 32 * 1024 * 1024
                 self.units_local = 8 * count
-                self.config = {"workload": "softmax: causal row softmax of x [32, 1024, 1024] ~ U[-8,8), scale 1/8, "
-                                           "seed 5", "parallelism": f"replica{world}", "l2": "inputs larger than L2 (128 MiB)"}
                 self.h2d = self.d2h = 4 * count
             else:
                 self.shape = (65536, 1024)
                 count = 65536 * 1024
                 self.units_local = 4 * count + 4 * 65536
-                self.config = {"workload": "reduce: row sums of x [65536 x 1024] ~ U[-4,4), seed 6",
-                               "parallelism": f"replica{world}", "l2": "inputs larger than L2 (256 MiB)"}
                 self.h2d, self.d2h = 4 * count, 4 * 65536
             self.x = ctx.buffer(4 * count)
             self.y = ctx.buffer(self.d2h)
@@ -315,21 +342,11 @@ class Workload:
             e.wait()
             e.close()
             self.units_total = self.units_local * world
-            self.unit, self.scale, self.scaling = "GB/s", 1e-9, "weak"
-            self.metric = METRICS[name]
         elif name == "block":
             from paralyn_b200.block import EncoderBlock
             self.block = EncoderBlock(ctx, 2048, 1024, 16, 4096, causal=True, seed=2026)
             self.units_local = self.block.flops()
             self.units_total = self.units_local * world
-            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "weak"
-            self.metric = METRICS[name]
-            self.config = {"workload": "block: pre-LN encoder block (reference examples/native/transformer_block), "
-                                       "T=2048, d=1024, 16 heads of 64, d_ff=4096, causal, seeded weights; 11 launches "
-                                       "per block (bias/GELU fused into the GEMM epilogues)",
-                           "tokens": 2048, "d_model": 1024, "heads": 16, "d_ff": 4096,
-                           "gemm_flops_per_block": self.units_local, "parallelism": f"replica{world}",
-                           "l2": "scores and probabilities 256 MiB each exceed L2"}
             self.h2d = self.d2h = 4 * 2048 * 1024
         elif name == "attention":
             D = self.T.TensorDescriptor
@@ -343,12 +360,11 @@ class Workload:
                 e.close()
             self.units_local = 2 * self.heads * self.seq * self.seq * self.dh
             self.units_total = self.units_local * world
-            self.unit, self.scale, self.scaling = "TFLOP/s", 1e-12, "weak"
-            self.metric = METRICS[name]
-            self.config = {"workload": "attention: S = Q K^T per head, Q, K [32, 2048, 128] ~ U[-1,1), seed 7; "
-                                       "K^T is a strided view (no copy)", "batch": 32, "m": 2048, "n": 2048, "k": 128,
-                           "parallelism": f"replica{world}", "l2": "output 512 MiB exceeds L2"}
             self.h2d, self.d2h = 8 * count, 4 * self.heads * self.seq * self.seq
+        self.metric, self.unit, self.scaling, self.config = describe(name, world, rank, gather)
+        self.scale = 1e-12 if self.unit == "TFLOP/s" else 1e-9
+        if name == "block":
+            self.config["gemm_flops_per_block"] = self.units_local
         self.ctx.synchronize()
 
     def step(self):
@@ -476,23 +492,15 @@ class Workload:
         return [(a, 4 * self.count), (b, 4 * self.count)], (c, self.d2h)
 
 
-def run_ours(args, group):
-    import numpy as np
+def time_steps(w, ctx, group, steps, warmup):
+    """W untimed warm-up steps, then `steps` steps between two queue markers (device
+    time, max over ranks) with the clock sampler running. Returns the timed region."""
     import paralyn_b200 as p
     from paralyn_b200 import b200
-    world = group.world
-    ctx = p.Context(f"cuda:{group.local_rank}")
-    p.set_matmul_mode(ctx, {"auto": p.MatmulMode.AUTO, "reference": p.MatmulMode.REFERENCE,
-                            "ffma": p.MatmulMode.FFMA, "tf32x3": p.MatmulMode.TF32X3}[args.matmul_mode])
-    w = Workload(args.workload, ctx, group, gather=args.gather)
-    if args.matmul_mode != "auto":
-        w.config["matmul_mode"] = args.matmul_mode
-    # Sharded workloads shrink per GPU as N grows; keep the timed region near a second.
-    steps = args.steps or DEFAULT_STEPS[args.workload] * (world if w.scaling == "strong" else 1)
     warm = []
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         warm += w.step()[0]
-    ctx.synchronize()
+    w.ctx.synchronize()
     for e in warm:
         e.close()
     kernels_before = p.device_kernel_count(ctx)
@@ -511,12 +519,63 @@ def run_ours(args, group):
     group.barrier()
     kernels = p.device_kernel_count(ctx) - kernels_before  # markers launch no kernel
     durations = [e.timing().duration_seconds for e in dominant]
-    variant = last_variant(ctx, args.workload)
+    variant = last_variant(ctx, w.name)
     for e in timed + [start, stop]:
         e.close()
     worst = group.max(seconds)
-    value = w.units_total * steps / worst * w.scale
-    ms = worst / steps * 1e3
+    return {"seconds": worst, "steps": steps, "value": w.units_total * steps / worst * w.scale,
+            "ms_per_step": worst / steps * 1e3, "gpu_launches": int(group.max(kernels)),
+            "clocks": clocks.summary(), "variant": variant, "dominant_seconds": sum(durations) / len(durations)}
+
+
+def with_clock_fraction(roofline, clocks):
+    mhz = clocks.get("sm_mhz")
+    if roofline.get("bound") == "fp32_ffma" and mhz:  # the FFMA peak scales with the clock actually run
+        roofline["frac_at_median_sm_clock"] = round(roofline["achieved"] / (148 * 128 * 2 * mhz * 1e6 / 1e12), 4)
+    return roofline
+
+
+def steps_for(args, name, w, world):
+    # Sharded workloads shrink per GPU as N grows; keep the timed region near a second.
+    return args.steps or DEFAULT_STEPS[name] * (world if w.scaling == "strong" else 1)
+
+
+# The benchmark configurations measured beside the chain headline, each in its own
+# timed region of the same process (the metric's GEMM TFLOP/s and LayerNorm / affine /
+# add HBM GB/s at the configurations' sizes).
+SIDE_CONFIGS = ("gemm", "layernorm", "affine", "add")
+
+
+def side_configs(args, ctx, group):
+    out = {}
+    for name in SIDE_CONFIGS:
+        w = Workload(name, ctx, group)
+        if args.matmul_mode != "auto" and name == "gemm":
+            w.config["matmul_mode"] = args.matmul_mode
+        t = time_steps(w, ctx, group, DEFAULT_STEPS[name] * (group.world if w.scaling == "strong" else 1),
+                       args.warmup)
+        roofline = with_clock_fraction(roofline_for(w, t["dominant_seconds"], t["variant"], t["seconds"]),
+                                       t["clocks"])
+        out[name] = {"metric": w.metric, "value": round(t["value"], 3), "unit": w.unit, "steps": t["steps"],
+                     "warmup": args.warmup, "ms_per_step": round(t["ms_per_step"], 5), "scaling": w.scaling,
+                     "config": w.config, "roofline": roofline, "clocks": t["clocks"],
+                     "gpu_launches": t["gpu_launches"], "dominant_kernel_variant": t["variant"]}
+        del w
+        ctx.synchronize()
+    return out
+
+
+def run_ours(args, group):
+    import paralyn_b200 as p
+    world = group.world
+    ctx = p.Context(f"cuda:{group.local_rank}")
+    p.set_matmul_mode(ctx, {"auto": p.MatmulMode.AUTO, "reference": p.MatmulMode.REFERENCE,
+                            "ffma": p.MatmulMode.FFMA, "tf32x3": p.MatmulMode.TF32X3}[args.matmul_mode])
+    w = Workload(args.workload, ctx, group, gather=args.gather)
+    if args.matmul_mode != "auto":
+        w.config["matmul_mode"] = args.matmul_mode
+    t = time_steps(w, ctx, group, steps_for(args, args.workload, w, world), args.warmup)
+    steps = t["steps"]
 
     e2e = None
     if not args.no_e2e:
@@ -524,16 +583,15 @@ def run_ours(args, group):
         e2e_steps = max(2, min(steps, int(8e9 // (w.h2d + w.d2h))))
         e2e = end_to_end(w, ctx, group, steps=e2e_steps)
 
-    dom = sum(durations) / len(durations)
-    roofline = roofline_for(w, dom, variant, worst)
-    line = {"metric": w.metric, "value": round(value, 3), "unit": w.unit, "n_gpus": world, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": w.scaling,
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded SplitMix64 stream generated on device)",
-            "config": w.config, "e2e": e2e, "gpu_launches": int(group.max(kernels)), "roofline": roofline,
-            "clocks": clocks.summary(), "dominant_kernel_variant": variant, "headline_metric": METRIC}
-    mhz = line["clocks"].get("sm_mhz")
-    if roofline.get("bound") == "fp32_ffma" and mhz:  # the FFMA peak scales with the clock actually run
-        roofline["frac_at_median_sm_clock"] = round(roofline["achieved"] / (148 * 128 * 2 * mhz * 1e6 / 1e12), 4)
+    roofline = with_clock_fraction(roofline_for(w, t["dominant_seconds"], t["variant"], t["seconds"]), t["clocks"])
+    line = {"metric": w.metric, "value": round(t["value"], 3), "unit": w.unit, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(t["ms_per_step"], 4), "higher_is_better": True,
+            "scaling": w.scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded SplitMix64 stream generated on device)", "config": w.config, "e2e": e2e,
+            "gpu_launches": t["gpu_launches"], "roofline": roofline, "clocks": t["clocks"],
+            "dominant_kernel_variant": t["variant"], "headline_metric": METRIC}
+    if args.workload == "chain" and not args.no_configs:
+        line["configs"] = side_configs(args, ctx, group)
     if group.rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload)
     ctx.close()
@@ -548,18 +606,8 @@ DOMINANT_ENTRY = {"chain": "paralyn_matmul_f32", "gemm": "paralyn_matmul_f32",
 
 def last_variant(ctx, workload):
     """Implementation the library chose for the dominant entry (from the evidence log)."""
-    import shutil
-    import tempfile
-    root = Path(tempfile.mkdtemp(prefix="paralyn_evidence_"))
-    try:
-        ctx.write_evidence(str(root / "e"))
-        launches = json.loads((root / "e" / "execution.json").read_text())["launches"]
-    finally:
-        shutil.rmtree(root, ignore_errors=True)
-    for launch in reversed(launches):
-        if launch["kernel"] == DOMINANT_ENTRY[workload]:
-            return launch["variant"]
-    return None
+    from paralyn_b200 import b200
+    return b200.last_variant(ctx, DOMINANT_ENTRY[workload])
 
 
 def end_to_end(w, ctx, group, steps):
@@ -652,7 +700,10 @@ def roofline_for(w, seconds, variant, region_seconds):
     half a second or more are compared with the sustained (power-capped) GEMM figure,
     shorter ones with the burst figure."""
     peaks, basis = measured_peaks()
-    traffic = load_traffic().get(w.name)
+    simt = bool(variant) and "simt" in variant
+    traffic = load_traffic().get(w.name + ("_ffma" if simt and "ffma" in variant else ""))
+    if simt and "ffma" not in variant:
+        traffic = None  # no capture of the reference-order kernel
     if w.name in ("layernorm", "affine", "add", "softmax", "reduce"):
         per_launch = w.units_local
         achieved = per_launch / seconds / 1e9
@@ -689,8 +740,9 @@ def load_traffic():
 
 
 # ---------------------------------------------------------------- CPU side (oracle)
-def cpu_sample(workload, budget_seconds):
-    """Runs the oracle (all host threads) on a bounded sample; returns (units/s, sample text)."""
+def cpu_sample(workload, budget_seconds, threaded=True):
+    """Runs the oracle (all host threads, or one with threaded=False) on a bounded sample;
+    returns (units/s, unit, sample text)."""
     import numpy as np
     import oracle
     from paralyn_b200 import synthetic
@@ -698,21 +750,21 @@ def cpu_sample(workload, budget_seconds):
     if workload in ("chain", "gemm"):
         k = n = 4096
         b = synthetic.normal(4, 0, k * n, 0.0, 1.0 / 64) if workload == "chain" else synthetic.uniform(3, 0, k * n)
-        rows = max(8, oracle.threads())
+        rows = max(8, oracle.threads()) if threaded else 1
         block = synthetic.uniform(3, 1, 64 * k)  # timing does not depend on the values
         a = np.tile(block, (rows + 63) // 64)[:rows * k]
         t0 = time.perf_counter()
-        z = oracle.matmul(a, b, rows, n, k, threaded=True)
+        z = oracle.matmul(a, b, rows, n, k, threaded=threaded)
         if workload == "chain":
-            oracle.layer_norm(z, np.ones(n, np.float32), np.zeros(n, np.float32), 1e-5, threaded=True)
+            oracle.layer_norm(z, np.ones(n, np.float32), np.zeros(n, np.float32), 1e-5, threaded=threaded)
         t = time.perf_counter() - t0
         scale = max(1, int(budget_seconds / max(t, 1e-3)))
         rows2 = min(rows * scale, 65536)
         a = np.tile(block, (rows2 + 63) // 64)[:rows2 * k]
         t0 = time.perf_counter()
-        z = oracle.matmul(a, b, rows2, n, k, threaded=True)
+        z = oracle.matmul(a, b, rows2, n, k, threaded=threaded)
         if workload == "chain":
-            oracle.layer_norm(z, np.ones(n, np.float32), np.zeros(n, np.float32), 1e-5, threaded=True)
+            oracle.layer_norm(z, np.ones(n, np.float32), np.zeros(n, np.float32), 1e-5, threaded=threaded)
         t = time.perf_counter() - t0
         return 2 * rows2 * n * k / t * 1e-12, "TFLOP/s", f"{rows2} of the rows x 4096 x 4096 (reference-order sequential GEMM" + (
             " + reference-order LayerNorm)" if workload == "chain" else ")")
@@ -724,7 +776,7 @@ def cpu_sample(workload, budget_seconds):
         t0 = time.perf_counter()
         reps = 0
         while time.perf_counter() - t0 < budget_seconds or reps == 0:
-            oracle.layer_norm(x, g, bt, 1e-5, threaded=True)
+            oracle.layer_norm(x, g, bt, 1e-5, threaded=threaded)
             reps += 1
         t = time.perf_counter() - t0
         return reps * (2 * rows * cols * 4 + 2 * cols * 4) / t * 1e-9, "GB/s", f"{reps} x 4096 rows x 4096"
@@ -735,9 +787,9 @@ def cpu_sample(workload, budget_seconds):
         reps = 0
         while time.perf_counter() - t0 < budget_seconds or reps == 0:
             if workload == "softmax":
-                oracle.softmax_rows(x, np.float32(0.125), causal=True)
+                oracle.softmax_rows(x, np.float32(0.125), causal=True, threaded=threaded)
             else:
-                oracle.reduce_rows(x, 0, threaded=True)
+                oracle.reduce_rows(x, 0, threaded=threaded)
             reps += 1
         t = time.perf_counter() - t0
         per = 8 * x.size if workload == "softmax" else 4 * x.size + 4 * shape[0]
@@ -745,11 +797,11 @@ def cpu_sample(workload, budget_seconds):
     if workload == "block":  # the up-projection GEMM [T, 1024] x [1024, 4096] on a row sample
         k, n = 1024, 4096
         b = synthetic.uniform(7, 0, k * n, 0.125)
-        rows = max(8, oracle.threads())
+        rows = max(8, oracle.threads()) if threaded else 1
         while True:
             a = synthetic.uniform(7, 1 << 30, rows * k)
             t0 = time.perf_counter()
-            oracle.matmul(a, b, rows, n, k, threaded=True)
+            oracle.matmul(a, b, rows, n, k, threaded=threaded)
             t = time.perf_counter() - t0
             if t >= budget_seconds / 4 or rows >= 2048:
                 break
@@ -759,11 +811,12 @@ def cpu_sample(workload, budget_seconds):
     if workload == "attention":
         S, K = 2048, 128
         q, kk = synthetic.uniform(7, 0, S * K), synthetic.uniform(7, 1, S * K)
-        rows = max(8, oracle.threads())
+        rows = max(8, oracle.threads()) if threaded else 1
         while True:  # grow the sample (at most one head's 2048 query rows) to about a quarter of the budget
             c = np.zeros(rows * S, np.float32)
             t0 = time.perf_counter()
-            oracle.batched_matmul_threaded(q, (0, (0, K, 1)), kk, (0, (0, 1, K)), c, (0, (0, S, 1)), 1, rows, S, K)
+            (oracle.batched_matmul_threaded if threaded else oracle.batched_matmul)(q, (0, (0, K, 1)), kk, (0, (0, 1, K)), c,
+                                                                                  (0, (0, S, 1)), 1, rows, S, K)
             t = time.perf_counter() - t0
             if t >= budget_seconds / 4 or rows == S:
                 break
@@ -776,24 +829,44 @@ def cpu_sample(workload, budget_seconds):
     reps = 0
     while time.perf_counter() - t0 < budget_seconds or reps == 0:
         if workload == "affine":
-            oracle.affine_scalar(x, np.float32(1.5), np.float32(-0.25), threaded=True)
+            oracle.affine_scalar(x, np.float32(1.5), np.float32(-0.25), threaded=threaded)
         else:
-            oracle.add(x, y, threaded=True)
+            oracle.add(x, y, threaded=threaded)
         reps += 1
     t = time.perf_counter() - t0
     per = 8 * count if workload == "affine" else 12 * count
     return reps * per / t * 1e-9, "GB/s", f"{reps} passes over n = {count}"
 
 
+def host_cpu():
+    """(model name, logical CPUs) of the host, from /proc/cpuinfo and os.cpu_count()."""
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return model, os.cpu_count()
+
+
 def cpu_baseline(workload, budget=10.0):
+    """The oracle port timed on the host: all host threads (OpenMP, the headline
+    value) and one thread as the reference's verifier is written."""
     import oracle
     value, unit, sample = cpu_sample(workload, budget)
-    return {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
-            "sample": sample + "; oracle restatement of the reference's CPU verifier, -O2 -ffp-contract=off, OpenMP"}
+    one, _, one_sample = cpu_sample(workload, budget / 2, threaded=False)
+    model, nproc = host_cpu()
+    return {"value": round(value, 6), "unit": unit, "cores": oracle.threads(), "kind": "port",
+            "sample": sample + "; oracle restatement of the reference's CPU verifier, -O2 -ffp-contract=off, OpenMP",
+            "single_thread": {"value": round(one, 6), "unit": unit, "cores": 1, "sample": one_sample},
+            "cpu_model": model, "nproc": nproc}
 
 
 def run_reference(args, group):
-    """The reference's CPU computation of the path (oracle port), rank 0 only."""
+    """The reference's CPU computation of the path (oracle port), rank 0 only, on the
+    same configuration (metric, unit and config dict) as our arm."""
     if group.rank != 0:
         return None
     import oracle
@@ -807,12 +880,18 @@ def run_reference(args, group):
         v, unit, sample = cpu_sample(args.workload, budget)
         values.append(v)
     value = sorted(values)[len(values) // 2]
-    return {"impl": "reference", "metric": METRICS[args.workload], "value": round(value, 4), "unit": unit,
-            "n_gpus": int(os.environ.get("WORLD_SIZE", args.gpus)), "steps": steps, "warmup": args.warmup, "higher_is_better": True,
-            "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload, "sample": sample},
-            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    metric, unit_ours, scaling, config = describe(args.workload, world, 0, args.gather)
+    assert unit == unit_ours
+    if args.matmul_mode != "auto":
+        config["matmul_mode"] = args.matmul_mode
+    model, nproc = host_cpu()
+    return {"impl": "reference", "metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": oracle.threads(), "kind": "port",
+                             "sample": sample, "cpu_model": model, "nproc": nproc},
+            "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():

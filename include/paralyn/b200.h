@@ -129,8 +129,12 @@ pr_status pr_b200_event_elapsed(pr_event first, pr_event second, double *seconds
  * [m,k] (or [k,m] with transpose_a), B [k,n] (or [n,k] with transpose_b), C [m,n];
  * lda, ldb, ldc are the row strides in elements of the stored matrices. The work
  * is enqueued on `stream` (a cudaStream_t; NULL is the legacy default stream) and
- * the call returns without waiting. `status` (optional, device-accessible) is set
- * non-zero if a kernel abandoned a bounded wait.
+ * the call returns without waiting. `status` (optional) is a device-accessible
+ * int32 that a kernel sets non-zero if it abandoned a bounded wait (C is then only
+ * partly written); the caller clears it and reads it after the stream completes.
+ * With status NULL such a failure cannot be detected: the call has already
+ * returned PR_SUCCESS and nothing reports the timeout later, so pass a status word
+ * wherever a partly written C must not go unnoticed.
  *
  * Limits: 16 <= k, 1 <= m, n, and 8 * round_up(k,32) * (round_up(m,128) +
  * round_up(n,256)) <= 64 MiB (e.g. 1024 x 1024 x 4096 or 2048^3); larger shapes are
@@ -139,7 +143,10 @@ pr_status pr_b200_event_elapsed(pr_event first, pr_event second, double *seconds
  * calls that overlap on the GPU (other streams, other threads) race on it.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture. Results satisfy |err| <= 2*k*2^-24*sum|a||b|, like
+ * any stream capture. The address is kept for the life of the process: after
+ * cudaDeviceReset (or anything else that destroys and recreates the device's
+ * primary context) it is stale, so do not call this entry point on that device
+ * again in the same process. Results satisfy |err| <= 2*k*2^-24*sum|a||b|, like
  * PR_B200_MATMUL_TF32X3 in pr_matmul_f32. */
 pr_status pr_b200_matmul_tf32x3_static_f32(const float *a, const float *b, float *c, uint64_t m, uint64_t n,
                                            uint64_t k, uint64_t lda, uint64_t ldb, uint64_t ldc,

@@ -177,14 +177,20 @@ def reduce_rows(x, op, threaded=False):
     return out
 
 
-def softmax_rows(x, scale, causal=False):
-    """FP32 row softmax in the reference's order with the C library's expf (all threads;
-    a timing baseline: parity checks use softmax_bound)."""
+def softmax_rows(x, scale, causal=False, threaded=True):
+    """FP32 row softmax in the reference's order with the C library's expf (all threads,
+    or one with threaded=False; a timing baseline: parity checks use softmax_bound)."""
     x = _f32(x)
     rows, columns = x.shape[-2], x.shape[-1]
     out = np.empty_like(x)
-    lib().orc_softmax_rows_f32_mt(x, out, int(np.prod(x.shape[:-1])), rows, columns, int(bool(causal)),
-                                  float(scale))
+    team = threads()
+    if not threaded:
+        lib().orc_set_threads(1)
+    try:
+        lib().orc_softmax_rows_f32_mt(x, out, int(np.prod(x.shape[:-1])), rows, columns, int(bool(causal)),
+                                      float(scale))
+    finally:
+        lib().orc_set_threads(team)
     return out
 
 
@@ -258,6 +264,23 @@ def matmul_tolerance(magnitude, k):
 
 # ---- the reference's own code, compiled from its sources (oracle/_ref) ----
 _ref = None
+REF_BINDING = HERE / "_ref" / "bindings" / "python"
+REF_QUALIFY = HERE / "_ref" / "scripts" / "qualify_cuda.py"
+
+
+def reference_checkout():
+    """Path of the reference checkout the oracle recipe builds from (PARALYN_REFERENCE,
+    else the recipe's default), or None when no checkout is there."""
+    import os
+    path = os.environ.get("PARALYN_REFERENCE")
+    if not path:
+        try:
+            path = subprocess.run(["make", "-s", "--no-print-directory", "-C", str(HERE), "print-reference"],
+                                  check=True, capture_output=True, text=True).stdout.strip()
+        except (OSError, subprocess.CalledProcessError):
+            return None
+    checkout = Path(path)
+    return checkout if (checkout / "include" / "paralyn" / "native.h").exists() else None
 
 
 def reference():

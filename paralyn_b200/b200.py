@@ -215,6 +215,25 @@ def elapsed(first, second):
     return seconds.value
 
 
+def last_variant(context, entry):
+    """The implementation the library chose for the newest launch of provider entry
+    `entry` on this context (from its evidence log), or None when there is none."""
+    import json
+    import shutil
+    import tempfile
+    from pathlib import Path
+    root = Path(tempfile.mkdtemp(prefix="paralyn_evidence_"))
+    try:
+        context.write_evidence(str(root / "e"))
+        launches = json.loads((root / "e" / "execution.json").read_text())["launches"]
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
+    for launch in reversed(launches):
+        if launch["kernel"] == entry:
+            return launch["variant"]
+    return None
+
+
 def inspect_module(data, library_path=None):
     """{kernel name: native implementation} for a module artifact, without a device."""
     from .native import library

@@ -7,7 +7,6 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
-REFERENCE = Path("/root/reference")
 
 
 def pytest_configure(config):
@@ -23,9 +22,13 @@ def lib():
 
 @pytest.fixture(scope="session")
 def reference_checkout():
-    if not (REFERENCE / "include" / "paralyn" / "native.h").exists():
+    """The reference checkout (PARALYN_REFERENCE, else the oracle recipe's default);
+    skips where there is none (GPU machines have no checkout)."""
+    import oracle
+    checkout = oracle.reference_checkout()
+    if checkout is None:
         pytest.skip("reference checkout not present on this machine")
-    return REFERENCE
+    return checkout
 
 
 @pytest.fixture()

@@ -24,6 +24,18 @@ def check_reference_line(line, n_gpus):
     assert base["kind"] == "port" and base["cores"] >= 1 and base["value"] == line["value"] and base["sample"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
+    sys.path.insert(0, str(ROOT))
+    import bench
+    metric, unit, scaling, config = bench.describe("add", n_gpus, 0)
+    assert (line["metric"], line["unit"], line["scaling"], line["config"]) == (metric, unit, scaling, config)
+
+
+def test_cpu_baseline_has_all_core_and_single_thread_legs():
+    sys.path.insert(0, str(ROOT))
+    import bench
+    base = bench.cpu_baseline("add", budget=0.2)
+    assert base["value"] > 0 and base["single_thread"]["value"] > 0 and base["single_thread"]["cores"] == 1
+    assert base["nproc"] >= 1 and "cpu_model" in base
 
 
 def test_reference_arm_prints_one_line():

@@ -12,14 +12,19 @@ extern "C" {
 
 /* Summation mode of pr_matmul_f32 on one context. The initial mode comes from
  * PARALYN_MATMUL_MODE (reference | ffma | tf32x3 | auto) at context creation.
- *  AUTO:      TF32X3 where the shape qualifies (k >= 64), otherwise FFMA.
+ *  AUTO:      TF32X3 where the shape qualifies (k >= 64), otherwise FFMA. When an
+ *             operand holds +-inf (or a finite value whose TF32 high part rounds
+ *             to infinity), the command recomputes C with FFMA on the GPU (a guarded
+ *             kernel that does nothing otherwise; no host synchronization), so +-inf
+ *             propagate as in the reference's IEEE order.
  *  REFERENCE: sum = fl(sum + fl(a*b)) in increasing k, bit-exact with the
  *             reference's sequential checker (half the FFMA rate).
  *  FFMA:      sum = fma(a, b, sum) in increasing k.
  *  TF32X3:    a = a_hi + a_lo, b = b_hi + b_lo split into TF32 on the fly;
  *             a_hi*b_hi + a_hi*b_lo + a_lo*b_hi on tcgen05 tensor cores with FP32
  *             accumulation in tensor memory; declines (falls back to FFMA) for
- *             shapes it does not cover.
+ *             shapes it does not cover. An infinite operand's low half is
+ *             inf - inf, so outputs it reaches are NaN in this mode.
  * FFMA and TF32X3 results satisfy |err| <= 2*k*2^-24*sum_p |a_ip||b_pj|. */
 typedef enum pr_b200_matmul_mode {
   PR_B200_MATMUL_AUTO = 0,

@@ -15,33 +15,31 @@ class MatmulMode(IntEnum):
     TF32X3 = 3
 
 
+_B200_CALLS = """
+pr_b200_matmul_mode_set h u32
+pr_b200_matmul_mode_get h *u32
+pr_b200_device_kernel_count h *u64
+pr_b200_module_inspect ptr u64 str u64
+pr_b200_buffer_export h ptr
+pr_b200_buffer_import h ptr *h
+pr_b200_layer_norm_gather_f32 h h ptr ptr u32 u64 *h
+pr_b200_buffer_write_async h h u64 ptr u64 *h
+pr_b200_buffer_read_async h h u64 ptr u64 *h
+pr_b200_host_register ptr u64
+pr_b200_host_unregister ptr
+pr_b200_marker h *h
+pr_b200_selftest_bounded_wait h u64 *h
+pr_b200_matmul_bias_activation_f32 h h ptr ptr u32 *h
+pr_b200_event_elapsed h h *f64
+pr_b200_fill_synthetic_f32 h *TensorDescRecord u64 u64 u32 f32 f32 *h
+"""
+
+
 def _b200(lib):
+    """`lib` with the tensor and the additive B200 entry points declared."""
     lib = _api(lib)
-    if not getattr(lib, "_b200_signatures", False):
-        h, u32, u64, ptr = _c.c_uint64, _c.c_uint32, _c.c_uint64, _c.POINTER
-        signatures = {
-            "pr_b200_matmul_mode_set": (_c.c_int, [h, u32]),
-            "pr_b200_matmul_mode_get": (_c.c_int, [h, ptr(u32)]),
-            "pr_b200_device_kernel_count": (_c.c_int, [h, ptr(u64)]),
-            "pr_b200_module_inspect": (_c.c_int, [_c.c_void_p, u64, _c.c_char_p, u64]),
-            "pr_b200_buffer_export": (_c.c_int, [h, _c.c_void_p]),
-            "pr_b200_buffer_import": (_c.c_int, [h, _c.c_void_p, ptr(h)]),
-            "pr_b200_layer_norm_gather_f32": (_c.c_int, [h, h, _c.c_void_p, _c.c_void_p, u32, u64, ptr(h)]),
-            "pr_b200_buffer_write_async": (_c.c_int, [h, h, u64, _c.c_void_p, u64, ptr(h)]),
-            "pr_b200_buffer_read_async": (_c.c_int, [h, h, u64, _c.c_void_p, u64, ptr(h)]),
-            "pr_b200_host_register": (_c.c_int, [_c.c_void_p, u64]),
-            "pr_b200_host_unregister": (_c.c_int, [_c.c_void_p]),
-            "pr_b200_marker": (_c.c_int, [h, ptr(h)]),
-            "pr_b200_selftest_bounded_wait": (_c.c_int, [h, u64, ptr(h)]),
-            "pr_b200_matmul_bias_activation_f32": (_c.c_int, [h, h, _c.c_void_p, _c.c_void_p, u32, ptr(h)]),
-            "pr_b200_event_elapsed": (_c.c_int, [h, h, ptr(_c.c_double)]),
-            "pr_b200_fill_synthetic_f32": (_c.c_int, [h, ptr(TensorDescRecord), u64, u64, u32,
-                                                      _c.c_float, _c.c_float, ptr(h)]),
-        }
-        for name, (result, arguments) in signatures.items():
-            function = getattr(lib.api, name)
-            function.restype, function.argtypes = result, arguments
-        lib._b200_signatures = True
+    if not lib.declares("pr_b200_marker"):
+        lib.declare(_B200_CALLS)
     return lib
 
 

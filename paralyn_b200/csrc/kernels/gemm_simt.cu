@@ -33,6 +33,10 @@ struct GemmArgs {
   // Fused epilogue: C = activate(fl(acc + bias[column])) (activation.cuh).
   const float *bias = nullptr;
   uint32_t activation = 0;
+  // Guarded launch: the kernel does nothing unless *only_if == epoch (the AUTO
+  // mode's recomputation of a 3xTF32 command whose operands held an infinity).
+  const unsigned long long *only_if = nullptr;
+  unsigned long long epoch = 0;
 };
 
 template <int MODE> __device__ __forceinline__ float mac(float acc, float a, float b) {
@@ -128,16 +132,10 @@ template <bool TB> __device__ __forceinline__ void store_b(float (*sb)[BN], cons
 }
 
 template <int MODE, bool TA, bool TB>
-__global__ void __launch_bounds__(THREADS, 2) gemm_simt(const GemmArgs batch) {
-  GemmArgs g = batch;
-  g.a += int64_t(blockIdx.z) * batch.sa;
-  g.b += int64_t(blockIdx.z) * batch.sb;
-  g.c += int64_t(blockIdx.z) * batch.sc;
-  __shared__ __align__(16) float sa[2][BK][BM];
-  __shared__ __align__(16) float sb[2][BK][BN];
+__device__ __forceinline__ void simt_tile(const GemmArgs &g, int64_t id, int64_t tiles_m, int64_t tiles_n,
+                                          float (*sa)[BK][BM], float (*sb)[BK][BN]) {
   // Grouped raster: 8 tile-rows at a time, columns fastest within the group.
-  const int64_t tiles_m = (g.m + BM - 1) / BM, tiles_n = (g.n + BN - 1) / BN;
-  const int64_t id = blockIdx.x, group = 8;
+  const int64_t group = 8;
   const int64_t per_group = group * tiles_n;
   const int64_t first_m = (id / per_group) * group;
   const int64_t rows_in_group = min(group, tiles_m - first_m);
@@ -225,20 +223,62 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_simt(const GemmArgs batch) {
   }
 }
 
-template <int MODE, bool TA, bool TB> void run(const GemmArgs &g, cudaStream_t stream, uint32_t batch) {
-  const int64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + BN - 1) / BN);
-  gemm_simt<MODE, TA, TB><<<dim3(uint32_t(tiles), 1, batch), THREADS, 0, stream>>>(g);
+// One block per tile. GUARDED: the launch does nothing unless *only_if == epoch,
+// and fewer blocks than tiles walk the tiles id = blockIdx.x, + gridDim.x, ...
+template <int MODE, bool TA, bool TB, bool GUARDED>
+__global__ void __launch_bounds__(THREADS, 2) gemm_simt(const GemmArgs batch) {
+  if (GUARDED && *batch.only_if != batch.epoch)
+    return;
+  GemmArgs g = batch;
+  g.a += int64_t(blockIdx.z) * batch.sa;
+  g.b += int64_t(blockIdx.z) * batch.sb;
+  g.c += int64_t(blockIdx.z) * batch.sc;
+  __shared__ __align__(16) float sa[2][BK][BM];
+  __shared__ __align__(16) float sb[2][BK][BN];
+  const int64_t tiles_m = (g.m + BM - 1) / BM, tiles_n = (g.n + BN - 1) / BN;
+  if (!GUARDED) {
+    simt_tile<MODE, TA, TB>(g, blockIdx.x, tiles_m, tiles_n, sa, sb);
+    return;
+  }
+  for (int64_t id = blockIdx.x; id < tiles_m * tiles_n; id += gridDim.x)
+    simt_tile<MODE, TA, TB>(g, id, tiles_m, tiles_n, sa, sb);
 }
 
-template <int MODE> void dispatch(const GemmArgs &g, bool ta, bool tb, cudaStream_t stream, uint32_t batch = 1) {
-  if (!ta && !tb)
-    run<MODE, false, false>(g, stream, batch);
-  else if (!ta && tb)
-    run<MODE, false, true>(g, stream, batch);
-  else if (ta && !tb)
-    run<MODE, true, false>(g, stream, batch);
+// One block per tile, or (guarded launches) at most max_blocks blocks per matrix.
+template <int MODE, bool TA, bool TB>
+void run(const GemmArgs &g, cudaStream_t stream, uint32_t batch, int64_t max_blocks) {
+  const int64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + BN - 1) / BN);
+  if (g.only_if)
+    gemm_simt<MODE, TA, TB, true><<<dim3(uint32_t(std::min(tiles, max_blocks)), 1, batch), THREADS, 0, stream>>>(g);
   else
-    run<MODE, true, true>(g, stream, batch);
+    gemm_simt<MODE, TA, TB, false><<<dim3(uint32_t(tiles), 1, batch), THREADS, 0, stream>>>(g);
+}
+
+template <int MODE>
+void dispatch(const GemmArgs &g, bool ta, bool tb, cudaStream_t stream, uint32_t batch = 1, int64_t max_blocks = 0) {
+  if (!ta && !tb)
+    run<MODE, false, false>(g, stream, batch, max_blocks);
+  else if (!ta && tb)
+    run<MODE, false, true>(g, stream, batch, max_blocks);
+  else if (ta && !tb)
+    run<MODE, true, false>(g, stream, batch, max_blocks);
+  else
+    run<MODE, true, true>(g, stream, batch, max_blocks);
+}
+
+// AUTO mode after a 3xTF32 command that watched its operands: the FFMA kernel over the
+// same operands, guarded by the command's non-finite word, so it recomputes C (IEEE
+// propagation of +-inf in increasing k) only when an operand held an infinity. When
+// the word is clear every block returns at once; two blocks per SM walk the tiles.
+void recompute_if_infinite(Launch &L, const GemmArgs &g, bool ta, bool tb, uint32_t batch,
+                           const NonFiniteFlag &watch) {
+  if (!watch.word)
+    return;
+  GemmArgs guarded = g;
+  guarded.only_if = watch.word;
+  guarded.epoch = watch.epoch;
+  dispatch<matmul_ffma>(guarded, ta, tb, L.stream, batch, int64_t(2) * std::max(1, L.sm_count));
+  ++L.kernels;
 }
 
 // Any strides: one output per thread, 16x16 threads per block, k in increasing order.
@@ -271,10 +311,10 @@ bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
 
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n,
                         int64_t k, int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb,
-                        const float *bias = nullptr, uint32_t activation = 0);
+                        const float *bias, uint32_t activation, NonFiniteFlag *watch);
 bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
                            int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
-                           int64_t ldc, int64_t sc);
+                           int64_t ldc, int64_t sc, NonFiniteFlag *watch);
 
 namespace {
 // C = op(A) op(B) over the grid-bounded region, optionally with the bias/activation
@@ -321,8 +361,12 @@ void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
   g.vec_c = aligned16(g.c) && g.ldc % 4 == 0;
   uint32_t mode = L.matmul_mode;
   if (mode == matmul_auto || mode == matmul_tf32x3) {
-    if (launch_tf32x3_gemm(L, g.a, g.b, g.c, me, ne, k, g.lda, g.ldb, g.ldc, ta, tb, g.bias, g.activation))
+    NonFiniteFlag watch;
+    if (launch_tf32x3_gemm(L, g.a, g.b, g.c, me, ne, k, g.lda, g.ldb, g.ldc, ta, tb, g.bias, g.activation,
+                           mode == matmul_auto ? &watch : nullptr)) {
+      recompute_if_infinite(L, g, ta, tb, 1, watch);
       return;
+    }
     mode = matmul_ffma;
   }
   if (mode == matmul_reference) {
@@ -427,9 +471,13 @@ void launch_provider_batched_matmul(Launch &L) {
     g.vec_a = aligned16(a) && g.lda % 4 == 0 && g.sa % 4 == 0;
     g.vec_b = aligned16(b) && g.ldb % 4 == 0 && g.sb % 4 == 0;
     g.vec_c = aligned16(c) && g.ldc % 4 == 0 && g.sc % 4 == 0 && g.c_col == 1;
+    NonFiniteFlag watch;
     if ((L.matmul_mode == matmul_auto || L.matmul_mode == matmul_tf32x3) && g.c_col == 1 &&
-        launch_tf32x3_batched(L, a, b, c, int64_t(batch), m, n, k, g.lda, ta, g.sa, g.ldb, tb, g.sb, g.ldc, g.sc))
+        launch_tf32x3_batched(L, a, b, c, int64_t(batch), m, n, k, g.lda, ta, g.sa, g.ldb, tb, g.sb, g.ldc, g.sc,
+                              L.matmul_mode == matmul_auto ? &watch : nullptr)) {
+      recompute_if_infinite(L, g, ta, tb, uint32_t(batch), watch);
       return;
+    }
     if (reference)
       dispatch<matmul_reference>(g, ta, tb, L.stream, uint32_t(batch));
     else

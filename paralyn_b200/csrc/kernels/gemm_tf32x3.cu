@@ -40,6 +40,7 @@
 #include "activation.cuh"
 #include <cuda.h>
 #include <algorithm>
+#include <atomic>
 
 namespace pb {
 namespace {
@@ -161,10 +162,14 @@ __device__ __forceinline__ float tf32_rna(float x) {
 // Element (r, k) of op(X) is x[r*ld + k], or x[k*ld + r] when `transposed`.
 // Batched (grid.z > 1): matrix z starts x_batch elements after matrix z-1 and is
 // written rows_pad rows after it.
+// `nonfinite` (optional) is set to `epoch` when an element's high part is infinite
+// (an infinite input, or a finite one that rounds to infinity in TF32): its low part
+// is then inf - inf and the 3xTF32 products would turn +-inf into NaN.
 __global__ void __launch_bounds__(256) split_tf32(const float *__restrict__ x, int64_t ld, int transposed,
                                                   int64_t rows, int64_t k, float *__restrict__ hi,
                                                   float *__restrict__ lo, int64_t k_pad, int64_t x_batch,
-                                                  int64_t rows_pad) {
+                                                  int64_t rows_pad, unsigned long long *nonfinite,
+                                                  unsigned long long epoch) {
   __shared__ float tile[32][33];
   x += int64_t(blockIdx.z) * x_batch;
   hi += int64_t(blockIdx.z) * rows_pad * k_pad;
@@ -189,6 +194,8 @@ __global__ void __launch_bounds__(256) split_tf32(const float *__restrict__ x, i
     const float v = tile[a][tx];
     const float h = tf32_rna(v);
     const float l = tf32_rna(v - h);
+    if (nonfinite && isinf(h))
+      *nonfinite = epoch;
     const int64_t offset = (r0 + a) * k_pad + k0 + tx;
     hi[offset] = h;
     lo[offset] = l;
@@ -204,10 +211,12 @@ __device__ __forceinline__ void split4(float4 v, float4 &h, float4 &l) {
   h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
   l = make_float4(tf32_rna(v.x - h.x), tf32_rna(v.y - h.y), tf32_rna(v.z - h.z), tf32_rna(v.w - h.w));
 }
+__device__ __forceinline__ bool any_inf(float4 h) { return isinf(h.x) || isinf(h.y) || isinf(h.z) || isinf(h.w); }
 __global__ void __launch_bounds__(256) split_tf32_vec(const float *__restrict__ x, int64_t ld, int transposed,
                                                       int64_t rows, int64_t k, float *__restrict__ hi,
                                                       float *__restrict__ lo, int64_t k_pad, int64_t x_batch,
-                                                      int64_t rows_pad) {
+                                                      int64_t rows_pad, unsigned long long *nonfinite,
+                                                      unsigned long long epoch) {
   __shared__ float tile[32][33];
   x += int64_t(blockIdx.z) * x_batch;
   hi += int64_t(blockIdx.z) * rows_pad * k_pad;
@@ -226,6 +235,8 @@ __global__ void __launch_bounds__(256) split_tf32_vec(const float *__restrict__ 
           (&v.x)[e] = x[r * ld + kk + e];
     float4 h, l;
     split4(v, h, l);
+    if (nonfinite && any_inf(h))
+      *nonfinite = epoch;
     const int64_t offset = r * k_pad + kk;
     *reinterpret_cast<float4 *>(hi + offset) = h;
     *reinterpret_cast<float4 *>(lo + offset) = l;
@@ -250,6 +261,8 @@ __global__ void __launch_bounds__(256) split_tf32_vec(const float *__restrict__ 
     const float4 v = make_float4(tile[a][4 * q], tile[a][4 * q + 1], tile[a][4 * q + 2], tile[a][4 * q + 3]);
     float4 h, l;
     split4(v, h, l);
+    if (nonfinite && any_inf(h))
+      *nonfinite = epoch;
     const int64_t offset = (r0 + a) * k_pad + k0 + 4 * q;
     *reinterpret_cast<float4 *>(hi + offset) = h;
     *reinterpret_cast<float4 *>(lo + offset) = l;
@@ -277,6 +290,10 @@ struct TileArgs {
   uint32_t activation = 0;
   // The kernel computes D = C^T (m, n above are D's): D[i][j] is stored to C[j][i].
   bool transposed = false;
+  // Set to `epoch` by the converter warps when a raw operand's high part is infinite
+  // (as the split kernels do for the operands they split); null: not watched.
+  unsigned long long *nonfinite = nullptr;
+  unsigned long long epoch = 0;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -682,6 +699,8 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
           const float4 h = tf32_hi(v);
           lo[t + 128 * i] = tf32_hi(make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
           hi[t + 128 * i] = h;
+          if (args.nonfinite && any_inf(h))
+            *args.nonfinite = args.epoch;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // visible to the tensor cores
         __syncwarp();
@@ -1026,7 +1045,7 @@ bool raw_a_layout(const float *a, bool ta, int64_t m, int64_t lda, int64_t sa) {
 //    column tiles re-read it, else split by the split pass.
 bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m, int64_t n,
                    int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb, int64_t ldc,
-                   int64_t sc, const float *bias, uint32_t activation) {
+                   int64_t sc, const float *bias, uint32_t activation, NonFiniteFlag *watch) {
   if (!encoder() || !L.workspace)
     return false;
   if (batch == 1)
@@ -1054,13 +1073,24 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   const int64_t a_rows = a_split ? batch * dm_pad : 0;
   const int64_t b_rows_each = transposed ? dm_pad : dn_pad;
   const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_rows + batch_b * b_rows_each);
-  const size_t bytes = split_bytes + plan.partial_bytes;
+  // After the split operands and the partial tiles: the non-finite flag word (8 bytes;
+  // both regions are multiples of 8 bytes).
+  const size_t bytes = split_bytes + plan.partial_bytes + (watch ? 8 : 0);
   if (L.dry_run)
     return true;
   auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
   if (!scratch)
     return false;
   float *partials = scratch + split_bytes / sizeof(float);
+  unsigned long long *flag = nullptr, epoch = 0;
+  if (watch) {
+    static std::atomic<unsigned long long> epochs{1};
+    flag = reinterpret_cast<unsigned long long *>(reinterpret_cast<char *>(scratch) + split_bytes +
+                                                  plan.partial_bytes);
+    epoch = epochs.fetch_add(1, std::memory_order_relaxed);
+    watch->word = flag;
+    watch->epoch = epoch;
+  }
   float *ahi = scratch, *alo = ahi + a_rows * k_pad, *bhi = alo + a_rows * k_pad,
         *blo = bhi + batch_b * b_rows_each * k_pad;
   CUtensorMap maps[4];
@@ -1092,17 +1122,19 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   if (a_split) {
     const dim3 grid(uint32_t(k_pad / 32), uint32_t(dm_pad / 32), uint32_t(batch));
     if (vec_ok(a, lda, batch > 1 ? sa : 0))
-      split_tf32_vec<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad);
+      split_tf32_vec<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad, flag, epoch);
     else
-      split_tf32<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad);
+      split_tf32<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad, flag, epoch);
     ++L.kernels;
   }
   {
     const dim3 grid(uint32_t(k_pad / 32), uint32_t(b_rows_each / 32), uint32_t(batch_b));
     if (vec_ok(b, ldb, sb))
-      split_tf32_vec<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each);
+      split_tf32_vec<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each, flag,
+                                                 epoch);
     else
-      split_tf32<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each);
+      split_tf32<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each, flag,
+                                             epoch);
     ++L.kernels;
   }
   TileArgs t{c, dm, dn, ldc, int(k_pad / TK), int(tiles_m), int(tiles_n), L.status};
@@ -1119,6 +1151,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   t.bias = bias;
   t.activation = activation;
   t.transposed = transposed;
+  t.nonfinite = flag;
+  t.epoch = epoch;
   ++L.kernels;
   launch_form(form, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
   return true;
@@ -1130,14 +1164,15 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
 // shape is outside what this kernel covers or scratch is unavailable.
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                         int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb, const float *bias,
-                        uint32_t activation) {
+                        uint32_t activation, NonFiniteFlag *watch) {
   if (k < 16 || m < 1 || n < 1)
     return false;
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n < 128 * 256))
     return false;
   L.kernels = 0;
   const bool gelu_pass = activation == 2u; // tanh GELU: bias in the epilogue, GELU after
-  if (!launch_tf32x3(L, a, b, c, 1, m, n, k, lda, ta, 0, ldb, tb, 0, ldc, 0, bias, gelu_pass ? 0u : activation))
+  if (!launch_tf32x3(L, a, b, c, 1, m, n, k, lda, ta, 0, ldb, tb, 0, ldc, 0, bias, gelu_pass ? 0u : activation,
+                     watch))
     return false;
   if (gelu_pass && !L.dry_run) {
     const int64_t blocks = std::min<int64_t>((m * n / 4 + 255) / 256 + 1, int64_t(std::max(1, L.sm_count)) * 8);
@@ -1155,13 +1190,13 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
 // matrices are stacked row-wise, so no tile crosses a matrix boundary.
 bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
                            int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
-                           int64_t ldc, int64_t sc) {
+                           int64_t ldc, int64_t sc, NonFiniteFlag *watch) {
   if (k < 16 || m < 1 || n < 1 || batch < 1 || batch > 65535)
     return false;
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n * batch < 128 * 256 * 4))
     return false;
   L.kernels = 0;
-  if (!launch_tf32x3(L, a, b, c, batch, m, n, k, lda, ta, sa, ldb, tb, sb, ldc, sc, nullptr, 0))
+  if (!launch_tf32x3(L, a, b, c, batch, m, n, k, lda, ta, sa, ldb, tb, sb, ldc, sc, nullptr, 0, watch))
     return false;
   L.variant = "batched_tcgen05_tf32x3";
   return true;
@@ -1262,10 +1297,10 @@ PB_EXPORT pr_status pr_b200_matmul_tf32x3_static_f32(const float *a, const float
   // (padding included), so the previous call's contents are never read.
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(m_pad / 32)), 256, 0, s>>>(a, int64_t(lda), transpose_a ? 1 : 0,
                                                                               int64_t(m), int64_t(k), ahi, alo, k_pad,
-                                                                              0, m_pad);
+                                                                              0, m_pad, nullptr, 0);
   split_tf32<<<dim3(uint32_t(k_pad / 32), uint32_t(n_pad / 32)), 256, 0, s>>>(b, int64_t(ldb), transpose_b ? 0 : 1,
                                                                               int64_t(n), int64_t(k), bhi, blo, k_pad,
-                                                                              0, n_pad);
+                                                                              0, n_pad, nullptr, 0);
   TileArgs t{c, int64_t(m), int64_t(n), int64_t(ldc), int(k_pad / TK), int(m_pad / TM), int(n_pad / TN),
              status ? status : static_status_ptr[device]};
   gemm_tf32x3<<<uint32_t((m_pad / TM) * (n_pad / TN)), THREADS, SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], maps[3], t);

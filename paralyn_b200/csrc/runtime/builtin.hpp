@@ -40,6 +40,17 @@ enum MatmulMode : uint32_t {
   matmul_tf32x3 = 3,    // 3xTF32 split products on tcgen05, FP32 accumulation in TMEM
 };
 
+// A device word that a 3xTF32 command sets to its epoch when an operand holds a value
+// whose TF32 high part is infinite (an infinite input, or a finite one that rounds to
+// infinity). A 3xTF32 product of such a value is NaN (its low part is inf - inf),
+// where the reference's IEEE order gives +-inf; in AUTO mode the command is then
+// recomputed by a guarded FFMA kernel that runs only when the word holds the epoch.
+// Epochs are unique per process, so the word needs no reset between commands.
+struct NonFiniteFlag {
+  unsigned long long *word = nullptr;
+  unsigned long long epoch = 0;
+};
+
 struct Launch {
   cudaStream_t stream = nullptr;
   int device = 0;

@@ -1032,6 +1032,7 @@ void Engine::write_evidence(const std::string &directory) {
       << ",\n  \"cuda_runtime_version\": " << backend_status().runtime_version
       << ",\n  \"cuda_driver_version\": " << backend_status().driver_version
       << ",\n  \"os\": " << json(device_.os) << ",\n  \"cpu_fallback\": false"
+      << ",\n  \"test_double\": false"
       << ",\n  \"runtime_owned_current_buffer_bytes\": " << accounting_->current.load()
       << ",\n  \"runtime_owned_peak_buffer_bytes\": " << accounting_->peak.load()
       << ",\n  \"host_to_device_bytes\": " << counters_.h2d_bytes

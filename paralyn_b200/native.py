@@ -1,12 +1,16 @@
 """ctypes binding of the native C ABI (include/paralyn/native.h).
 
-Mirrors the reference's Python binding (bindings/python/paralyn/__init__.py): the
-same classes (Context, Buffer, View, Module, Kernel, Queue, Event), scalar
-wrappers (i32/u32/f32), status codes, error type and ownership rules (explicit
-close or context managers; a finalizer that cannot release terminates the
-process). It loads the in-tree libparalyn_native.so built by paralyn_b200.build,
-or PARALYN_LIBRARY. There is no CPU fallback: without the library or a CUDA
-device every call fails loudly.
+The Python surface has the reference binding's names and meaning (package
+`paralyn`: Context, Buffer, View, Module, Kernel, Queue, Event, i32/u32/f32,
+Status, Error), so code written against it runs here. The implementation is this
+package's own: the C records are declared from compact layout strings, every entry
+point is typed from one signature table (`_CALLS`, shared with tensor.py and
+b200.py), and every owned handle is released by `close()`, a `with` block, or a
+garbage-collection finalizer; a release that fails inside a finalizer ends the
+process, since the failure of GPU work that nobody waited for must not pass
+silently. The library is the in-tree libparalyn_native.so built by
+paralyn_b200.build, or PARALYN_LIBRARY. There is no CPU fallback: without the
+library or a CUDA device every call fails with a structured Error.
 """
 import ctypes as _c
 from dataclasses import dataclass
@@ -14,12 +18,15 @@ from enum import IntEnum
 import math
 import os
 from pathlib import Path
+import sys
+import weakref
 
 ABI_VERSION = 1
 _PACKAGE = Path(__file__).resolve().parent
 DEFAULT_LIBRARY = _PACKAGE / "libparalyn_native.so"
 
 
+# ---------------------------------------------------------------- ABI enumerations
 class Status(IntEnum):
     SUCCESS = 0
     INVALID_ARGUMENT = 1
@@ -53,131 +60,135 @@ class ClockDomain(IntEnum):
     METAL_SYSTEM_MACH = 2
 
 
+ARTIFACT_VERIFIED_IR = 1 << 0
+ARTIFACT_MSL_SOURCE = 1 << 1
+ARTIFACT_SPIRV_MSL = 1 << 2
+
+
 class Error(RuntimeError):
-    """A failed native call: status code, failing operation and message."""
+    """A native call that did not succeed: `code` (Status), the failing `operation`
+    as the library names it, and the library's `message`."""
 
     def __init__(self, code, operation, message):
-        self.code = Status(code)
-        self.operation = operation
-        self.message = message
-        super().__init__(f"{operation}: {message} [{self.code.name}]")
+        self.code, self.operation, self.message = Status(code), operation, message
+        super().__init__(f"{operation} failed with {self.code.name}: {message}")
+
+
+# ---------------------------------------------------------------- record layouts
+# Layout strings list "name:type" fields in declaration order; char[N] is a fixed
+# text field, ptr:<Record> a pointer to another record. The layouts are the C
+# headers' (the records cross the ABI by address).
+_SCALARS = {"u32": _c.c_uint32, "i32": _c.c_int32, "u64": _c.c_uint64, "i64": _c.c_int64,
+            "f32": _c.c_float, "f64": _c.c_double, "enum": _c.c_int}
+
+
+def layout(spec, **records):
+    fields = []
+    for item in spec.split():
+        name, kind = item.split(":", 1)
+        count = 1
+        if kind.endswith("]"):
+            kind, count = kind[:-1].split("[")
+            count = int(count)
+        if kind == "char":
+            ctype = _c.c_char * count
+        elif kind.startswith("ptr="):
+            ctype = _c.POINTER(records[kind[4:]])
+        else:
+            ctype = _SCALARS[kind] if count == 1 else _SCALARS[kind] * count
+        fields.append((name, ctype))
+    return fields
 
 
 class ErrorRecord(_c.Structure):
-    _fields_ = [("code", _c.c_int), ("operation", _c.c_char * 64), ("message", _c.c_char * 1024)]
+    _fields_ = layout("code:enum operation:char[64] message:char[1024]")
 
 
 class DeviceRecord(_c.Structure):
-    _fields_ = [("name", _c.c_char * 256), ("backend", _c.c_char * 32), ("os", _c.c_char * 128),
-                ("registry_id", _c.c_uint64), ("max_buffer_bytes", _c.c_uint64),
-                ("unified_memory", _c.c_uint32)]
+    _fields_ = layout("name:char[256] backend:char[32] os:char[128] registry_id:u64 max_buffer_bytes:u64 "
+                      "unified_memory:u32")
 
 
 class Dim3(_c.Structure):
-    _fields_ = [("x", _c.c_uint32), ("y", _c.c_uint32), ("z", _c.c_uint32)]
+    _fields_ = layout("x:u32 y:u32 z:u32")
 
 
 class ArgumentRecord(_c.Structure):
-    _fields_ = [("type", _c.c_int), ("view", _c.c_uint64), ("i32", _c.c_int32),
-                ("u32", _c.c_uint32), ("f32", _c.c_float)]
+    _fields_ = layout("type:enum view:u64 i32:i32 u32:u32 f32:f32")
 
 
 class ParameterRecord(_c.Structure):
-    _fields_ = [("name", _c.c_char * 4097), ("type", _c.c_int), ("is_buffer", _c.c_uint32),
-                ("access", _c.c_int)]
+    _fields_ = layout("name:char[4097] type:enum is_buffer:u32 access:enum")
 
 
 class EventRecord(_c.Structure):
-    _fields_ = [("completed", _c.c_uint32), ("gpu_start_seconds", _c.c_double),
-                ("gpu_end_seconds", _c.c_double)]
+    _fields_ = layout("completed:u32 gpu_start_seconds:f64 gpu_end_seconds:f64")
 
 
 class CapabilityRecord(_c.Structure):
-    _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32),
-                ("stable_id", _c.c_char * 128), ("backend", _c.c_char * 32),
-                ("artifact_formats", _c.c_uint64), ("scalar_types", _c.c_uint64),
-                ("max_buffer_bytes", _c.c_uint64), ("max_threadgroup_memory_bytes", _c.c_uint64),
-                ("max_block_x", _c.c_uint32), ("max_block_y", _c.c_uint32),
-                ("max_block_z", _c.c_uint32), ("max_buffer_bindings", _c.c_uint32),
-                ("unified_memory", _c.c_uint32), ("reserved", _c.c_uint32)]
+    _fields_ = layout("struct_size:u32 version:u32 stable_id:char[128] backend:char[32] artifact_formats:u64 "
+                      "scalar_types:u64 max_buffer_bytes:u64 max_threadgroup_memory_bytes:u64 max_block_x:u32 "
+                      "max_block_y:u32 max_block_z:u32 max_buffer_bindings:u32 unified_memory:u32 reserved:u32")
 
 
 class TimingRecord(_c.Structure):
-    _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32), ("completed", _c.c_uint32),
-                ("duration_valid", _c.c_uint32), ("timestamps_valid", _c.c_uint32),
-                ("clock_domain", _c.c_int), ("duration_seconds", _c.c_double),
-                ("start_seconds", _c.c_double), ("end_seconds", _c.c_double)]
+    _fields_ = layout("struct_size:u32 version:u32 completed:u32 duration_valid:u32 timestamps_valid:u32 "
+                      "clock_domain:enum duration_seconds:f64 start_seconds:f64 end_seconds:f64")
 
 
 class BackendRecord(_c.Structure):
-    _fields_ = [("struct_size", _c.c_uint32), ("version", _c.c_uint32), ("backend", _c.c_char * 32),
-                ("implemented", _c.c_uint32), ("available", _c.c_uint32),
-                ("device_count", _c.c_uint32), ("reserved", _c.c_uint32),
-                ("driver_version", _c.c_int32), ("compiler_version", _c.c_int32),
-                ("driver_library", _c.c_char * 512), ("compiler_library", _c.c_char * 512),
-                ("reason", _c.c_char * 1024)]
+    _fields_ = layout("struct_size:u32 version:u32 backend:char[32] implemented:u32 available:u32 "
+                      "device_count:u32 reserved:u32 driver_version:i32 compiler_version:i32 "
+                      "driver_library:char[512] compiler_library:char[512] reason:char[1024]")
 
 
-def versioned(record_type):
+def versioned(record_type, version=1):
+    """A zeroed record whose (struct_size, version) header is filled in."""
     record = record_type()
-    record.struct_size, record.version = _c.sizeof(record_type), 1
+    record.struct_size, record.version = _c.sizeof(record_type), version
     return record
 
 
-def _text(raw):
-    return raw.decode("utf-8", errors="replace")
+# ---------------------------------------------------------------- entry-point signatures
+# One line per entry point: name, then its parameters. h = a 64-bit handle, u32 /
+# u64 / f32 scalars, str = a NUL-terminated string, ptr = an untyped address,
+# dim3 = a Dim3 by value, *X = a pointer to X (a scalar kind or a record name).
+# Every entry point returns a pr_status, except where "-> u32" says otherwise.
+_CALLS = """
+pr_abi_version -> u32
+pr_last_error *ErrorRecord
+pr_backend_status_get str *BackendRecord
+pr_device_count *u32
+pr_device_get u32 *DeviceRecord
+pr_device_capabilities_get u32 *CapabilityRecord
+pr_context_create str *h
+pr_context_device h *DeviceRecord
+pr_context_capabilities h *CapabilityRecord
+pr_context_synchronize h
+pr_context_write_evidence h str
+pr_release h
+pr_buffer_create h u64 *h
+pr_buffer_size h *u64
+pr_view_create h u64 u64 u32 enum *h
+pr_buffer_write h u64 ptr u64
+pr_buffer_read h u64 ptr u64
+pr_module_load h ptr u64 *h
+pr_module_load_file h str *h
+pr_module_kernel h str *h
+pr_kernel_parameter_count h *u32
+pr_kernel_parameter h u32 *ParameterRecord
+pr_queue_get h *h
+pr_queue_synchronize h
+pr_launch h h dim3 dim3 *ArgumentRecord u32 *h
+pr_event_wait h *EventRecord
+pr_event_timing h *TimingRecord
+pr_event_cancel h
+"""
+_KINDS = {"h": _c.c_uint64, "u32": _c.c_uint32, "u64": _c.c_uint64, "f32": _c.c_float, "f64": _c.c_double,
+          "enum": _c.c_int, "str": _c.c_char_p, "ptr": _c.c_void_p, "dim3": Dim3}
+_RECORDS = {cls.__name__: cls for cls in (ErrorRecord, DeviceRecord, ArgumentRecord, ParameterRecord, EventRecord,
+                                          CapabilityRecord, TimingRecord, BackendRecord)}
 
-
-def _int(value, low, high, label):
-    if not isinstance(value, int) or isinstance(value, bool):
-        raise TypeError(f"{label} requires an integer")
-    if not low <= value <= high:
-        raise ValueError(f"{label} must be in [{low}, {high}]")
-    return value
-
-
-def _u64(value, label):
-    return _int(value, 0, (1 << 64) - 1, label)
-
-
-def _cstring(value, label):
-    data = os.fsencode(value)
-    if b"\0" in data:
-        raise ValueError(f"{label} contains a null byte")
-    return data
-
-
-_H, _U32, _U64, _P = _c.c_uint64, _c.c_uint32, _c.c_uint64, _c.POINTER
-_SIGNATURES = {
-    "pr_abi_version": (_U32, []),
-    "pr_last_error": (_c.c_int, [_P(ErrorRecord)]),
-    "pr_backend_status_get": (_c.c_int, [_c.c_char_p, _P(BackendRecord)]),
-    "pr_device_count": (_c.c_int, [_P(_U32)]),
-    "pr_device_get": (_c.c_int, [_U32, _P(DeviceRecord)]),
-    "pr_device_capabilities_get": (_c.c_int, [_U32, _P(CapabilityRecord)]),
-    "pr_context_create": (_c.c_int, [_c.c_char_p, _P(_H)]),
-    "pr_context_device": (_c.c_int, [_H, _P(DeviceRecord)]),
-    "pr_context_capabilities": (_c.c_int, [_H, _P(CapabilityRecord)]),
-    "pr_context_synchronize": (_c.c_int, [_H]),
-    "pr_context_write_evidence": (_c.c_int, [_H, _c.c_char_p]),
-    "pr_release": (_c.c_int, [_H]),
-    "pr_buffer_create": (_c.c_int, [_H, _U64, _P(_H)]),
-    "pr_buffer_size": (_c.c_int, [_H, _P(_U64)]),
-    "pr_view_create": (_c.c_int, [_H, _U64, _U64, _U32, _c.c_int, _P(_H)]),
-    "pr_buffer_write": (_c.c_int, [_H, _U64, _c.c_void_p, _U64]),
-    "pr_buffer_read": (_c.c_int, [_H, _U64, _c.c_void_p, _U64]),
-    "pr_module_load": (_c.c_int, [_H, _c.c_void_p, _U64, _P(_H)]),
-    "pr_module_load_file": (_c.c_int, [_H, _c.c_char_p, _P(_H)]),
-    "pr_module_kernel": (_c.c_int, [_H, _c.c_char_p, _P(_H)]),
-    "pr_kernel_parameter_count": (_c.c_int, [_H, _P(_U32)]),
-    "pr_kernel_parameter": (_c.c_int, [_H, _U32, _P(ParameterRecord)]),
-    "pr_queue_get": (_c.c_int, [_H, _P(_H)]),
-    "pr_queue_synchronize": (_c.c_int, [_H]),
-    "pr_launch": (_c.c_int, [_H, _H, Dim3, Dim3, _P(ArgumentRecord), _U32, _P(_H)]),
-    "pr_event_wait": (_c.c_int, [_H, _P(EventRecord)]),
-    "pr_event_timing": (_c.c_int, [_H, _P(TimingRecord)]),
-    "pr_event_cancel": (_c.c_int, [_H]),
-}
 # Entry points of include/paralyn/native.h and tensor.h (the reference ABI).
 REFERENCE_SYMBOLS = (
     "pr_abi_version pr_add_f32 pr_backend_status_get pr_batched_matmul_f32 pr_bias_activation_f32 "
@@ -197,44 +208,106 @@ B200_SYMBOLS = ("pr_b200_matmul_mode_set", "pr_b200_matmul_mode_get", "pr_b200_f
                 "pr_b200_selftest_bounded_wait", "pr_b200_matmul_bias_activation_f32")
 
 
+def _ctype(kind, records):
+    if kind.startswith("*"):
+        return _c.POINTER(_ctype(kind[1:], records))
+    return records[kind] if kind in records else _KINDS[kind]
+
+
 class Library:
-    """One loaded libparalyn_native.so with typed entry points."""
+    """One loaded libparalyn_native.so. `api` exposes the typed entry points;
+    `declare` adds signatures (tensor.py and b200.py declare theirs) and `check`
+    turns a status into an Error carrying the library's last-error record."""
 
     def __init__(self, path):
         self.path = str(Path(path).resolve())
         self.api = _c.CDLL(self.path)
-        for name, (result, arguments) in _SIGNATURES.items():
+        self._records = dict(_RECORDS)
+        self._declared = set()
+        self.declare(_CALLS)
+        found = self.api.pr_abi_version()
+        if found != ABI_VERSION:
+            raise RuntimeError(f"{self.path} implements ABI {found}; this binding speaks ABI {ABI_VERSION}")
+
+    def declare(self, table, **records):
+        self._records.update(records)
+        for line in table.strip().splitlines():
+            words = line.split()
+            name, params = words[0], words[1:]
+            result = _c.c_int
+            if "->" in params:
+                result = _ctype(params[-1], self._records)
+                params = params[:params.index("->")]
             function = getattr(self.api, name)
-            function.restype, function.argtypes = result, arguments
-        version = self.api.pr_abi_version()
-        if version != ABI_VERSION:
-            raise RuntimeError(f"Paralyn ABI {version} is incompatible with binding ABI {ABI_VERSION}")
+            function.argtypes = [_ctype(p, self._records) for p in params]
+            function.restype = result
+            self._declared.add(name)
+
+    def declares(self, name):
+        return name in self._declared
+
+    def last_error(self):
+        record = ErrorRecord()
+        if self.api.pr_last_error(_c.byref(record)) != Status.SUCCESS:
+            return "native call", "the library's error record could not be read"
+        return _decode(record.operation), _decode(record.message)
 
     def check(self, status):
-        if status == Status.SUCCESS:
-            return
-        record = ErrorRecord()
-        if self.api.pr_last_error(_c.byref(record)) == Status.SUCCESS:
-            raise Error(status, _text(record.operation), _text(record.message))
-        raise Error(status, "native call", "native error detail retrieval failed")
+        if status != Status.SUCCESS:
+            raise Error(status, *self.last_error())
+
+    def call(self, name, *args):
+        self.check(getattr(self.api, name)(*args))
+
+    def acquire(self, name, *args):
+        """Calls an entry point whose last parameter receives a handle; returns it."""
+        out = _c.c_uint64()
+        self.call(name, *args, _c.byref(out))
+        return out.value
 
 
-_libraries = {}
+_loaded = {}
 
 
 def library(path=None):
-    """The native library: `path`, else PARALYN_LIBRARY, else the in-tree build."""
-    if path is None:
-        path = os.environ.get("PARALYN_LIBRARY") or DEFAULT_LIBRARY
-    path = str(Path(path).resolve())
-    if path not in _libraries:
-        if not Path(path).is_file():
-            raise FileNotFoundError(f"libparalyn_native.so not found at {path}; build it with "
-                                    "`python -m paralyn_b200.build` or set PARALYN_LIBRARY")
-        _libraries[path] = Library(path)
-    return _libraries[path]
+    """The native library at `path`, else PARALYN_LIBRARY, else the in-tree build
+    (loaded once per path)."""
+    chosen = Path(path or os.environ.get("PARALYN_LIBRARY") or DEFAULT_LIBRARY).resolve()
+    key = str(chosen)
+    if key not in _loaded:
+        if not chosen.is_file():
+            raise FileNotFoundError(f"no native library at {chosen}: run `python -m paralyn_b200.build` "
+                                    "or point PARALYN_LIBRARY at libparalyn_native.so")
+        _loaded[key] = Library(chosen)
+    return _loaded[key]
 
 
+# ---------------------------------------------------------------- argument checks
+def _decode(raw):
+    return raw.decode("utf-8", errors="replace")
+
+
+def _int(value, low, high, label):
+    """`value` as an int in [low, high]; bools are not integers here."""
+    if isinstance(value, bool) or not isinstance(value, int):
+        raise TypeError(f"{label}: expected an integer, got {type(value).__name__}")
+    if value < low or value > high:
+        raise ValueError(f"{label}: {value} is outside [{low}, {high}]")
+    return value
+
+
+def _u64(value, label):
+    return _int(value, 0, 2 ** 64 - 1, label)
+
+
+def _encode(text, label):
+    raw = os.fsencode(text)
+    if 0 in raw:
+        raise ValueError(f"{label}: embedded NUL byte")
+    return raw
+
+
+# ---------------------------------------------------------------- device and backend queries
 @dataclass(frozen=True)
 class Device:
     name: str
@@ -246,8 +319,8 @@ class Device:
 
     @classmethod
     def _from(cls, r):
-        return cls(_text(r.name), _text(r.backend), _text(r.os), r.registry_id, r.max_buffer_bytes,
-                   bool(r.unified_memory))
+        return cls(_decode(r.name), _decode(r.backend), _decode(r.os), r.registry_id, r.max_buffer_bytes,
+                   r.unified_memory != 0)
 
 
 @dataclass(frozen=True)
@@ -264,15 +337,16 @@ class DeviceCapabilities:
 
     @classmethod
     def _from(cls, r):
-        return cls(_text(r.stable_id), _text(r.backend), r.artifact_formats, r.scalar_types,
-                   r.max_buffer_bytes, r.max_threadgroup_memory_bytes,
-                   (r.max_block_x, r.max_block_y, r.max_block_z), r.max_buffer_bindings,
-                   bool(r.unified_memory))
+        block = (r.max_block_x, r.max_block_y, r.max_block_z)
+        return cls(_decode(r.stable_id), _decode(r.backend), r.artifact_formats, r.scalar_types,
+                   r.max_buffer_bytes, r.max_threadgroup_memory_bytes, block, r.max_buffer_bindings,
+                   r.unified_memory != 0)
 
 
 @dataclass(frozen=True)
 class EventTiming:
-    """Duration-only on CUDA: start/end are None unless the backend marks them valid."""
+    """CUDA timing is duration-only: start/end stay None unless the record marks
+    timestamps valid."""
     completed: bool
     duration_seconds: object
     start_seconds: object
@@ -281,9 +355,9 @@ class EventTiming:
 
     @classmethod
     def _from(cls, r):
-        return cls(bool(r.completed), r.duration_seconds if r.duration_valid else None,
-                   r.start_seconds if r.timestamps_valid else None,
-                   r.end_seconds if r.timestamps_valid else None, ClockDomain(r.clock_domain))
+        stamps = (r.start_seconds, r.end_seconds) if r.timestamps_valid else (None, None)
+        return cls(r.completed != 0, r.duration_seconds if r.duration_valid else None, *stamps,
+                   ClockDomain(r.clock_domain))
 
 
 @dataclass(frozen=True)
@@ -297,106 +371,119 @@ class BackendStatus:
     reason: str
 
 
-ARTIFACT_VERIFIED_IR = 1 << 0
-ARTIFACT_MSL_SOURCE = 1 << 1
-ARTIFACT_SPIRV_MSL = 1 << 2
-
-
 def backend_status(name="cuda", path=None):
     lib = library(path)
-    record = versioned(BackendRecord)
-    lib.check(lib.api.pr_backend_status_get(_cstring(name, "backend"), _c.byref(record)))
-    return BackendStatus(_text(record.backend), bool(record.implemented), bool(record.available),
-                         record.device_count, record.driver_version, record.compiler_version,
-                         _text(record.reason))
+    r = versioned(BackendRecord)
+    lib.call("pr_backend_status_get", _encode(name, "backend name"), _c.byref(r))
+    return BackendStatus(_decode(r.backend), r.implemented != 0, r.available != 0, r.device_count,
+                         r.driver_version, r.compiler_version, _decode(r.reason))
 
 
 def devices(path=None):
     lib = library(path)
     count = _c.c_uint32()
-    lib.check(lib.api.pr_device_count(_c.byref(count)))
-    result = []
+    lib.call("pr_device_count", _c.byref(count))
+    found = []
     for index in range(count.value):
-        record = DeviceRecord()
-        lib.check(lib.api.pr_device_get(index, _c.byref(record)))
-        result.append(Device._from(record))
-    return tuple(result)
+        r = DeviceRecord()
+        lib.call("pr_device_get", index, _c.byref(r))
+        found.append(Device._from(r))
+    return tuple(found)
 
 
 def device_capabilities(index=0, path=None):
     lib = library(path)
-    record = versioned(CapabilityRecord)
-    lib.check(lib.api.pr_device_capabilities_get(_int(index, 0, (1 << 32) - 1, "device index"),
-                                                 _c.byref(record)))
-    return DeviceCapabilities._from(record)
+    r = versioned(CapabilityRecord)
+    lib.call("pr_device_capabilities_get", _int(index, 0, 2 ** 32 - 1, "device index"), _c.byref(r))
+    return DeviceCapabilities._from(r)
+
+
+# ---------------------------------------------------------------- owned handles
+def _release_at_collection(lib, handle, kind):
+    """Finalizer of an owned handle that nobody closed."""
+    status = lib.api.pr_release(handle)
+    if status != Status.SUCCESS:
+        operation, message = lib.last_error()
+        sys.stderr.write(f"paralyn_b200: releasing an unclosed {kind} failed ({Status(status).name}, "
+                         f"{operation}: {message}); a GPU failure nobody waited for ends the process\n")
+        sys.stderr.flush()
+        os._exit(1)
 
 
 class Owned:
-    """A native handle with one owned reference."""
+    """Holds one reference to a native handle until close(), the end of a `with`
+    block, or garbage collection (not interpreter exit: the library drains its own
+    work when the process ends)."""
+
+    _handle = 0
+    _finalizer = None
+
+    def _own(self, lib, handle):
+        self._lib, self._handle = lib, handle
+        self._finalizer = weakref.finalize(self, _release_at_collection, lib, handle, type(self).__name__)
+        self._finalizer.atexit = False
 
     @classmethod
     def _adopt(cls, lib, handle):
         value = cls.__new__(cls)
-        value._lib, value._handle = lib, handle
+        value._own(lib, handle)
         return value
 
     @property
-    def handle(self):
-        if not getattr(self, "_handle", 0):
-            raise Error(Status.INVALID_HANDLE, type(self).__name__, "object is closed")
-        return self._handle
+    def closed(self):
+        return not self._handle
 
     @property
-    def closed(self):
-        return not getattr(self, "_handle", 0)
+    def handle(self):
+        if not self._handle:
+            raise Error(Status.INVALID_HANDLE, type(self).__name__, "used after close()")
+        return self._handle
 
     def close(self):
-        if self.closed:
+        """Releases the handle (idempotent); raises the release's failure, if any."""
+        if not self._handle:
             return
         handle, self._handle = self._handle, 0
-        self._lib.check(self._lib.api.pr_release(handle))
+        self._finalizer.detach()
+        self._lib.call("pr_release", handle)
 
     def __enter__(self):
-        self.handle
+        self.handle  # a closed object cannot enter a block
         return self
 
     def __exit__(self, *_):
         self.close()
 
-    def __del__(self, _write=os.write, _exit=os._exit):
-        if not self.closed:
-            try:
-                self.close()
-            except Exception as error:  # a lost GPU failure must not exit 0
-                try:
-                    _write(2, f"Paralyn fatal unhandled {type(self).__name__} finalizer error: "
-                              f"{error}\n".encode("utf-8", errors="backslashreplace"))
-                finally:
-                    _exit(1)
-
 
 class Context(Owned):
-    """One device context with one ordered queue ("cuda:K" or "auto")."""
+    """A device context with its one in-order queue. `selector` is "cuda:K" or
+    "auto" (default: PARALYN_DEVICE, else "auto")."""
 
     def __init__(self, selector=None, *, library_path=None):
-        if selector is None:
-            selector = os.environ.get("PARALYN_DEVICE", "auto")
-        self._lib, self._handle = library(library_path), 0
-        handle = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_context_create(_cstring(selector, "selector"), _c.byref(handle)))
-        self._handle = handle.value
+        lib = library(library_path)
+        selector = os.environ.get("PARALYN_DEVICE", "auto") if selector is None else selector
+        self._own(lib, lib.acquire("pr_context_create", _encode(selector, "device selector")))
+        self._attached = {}  # per-context operator resources (tensor provider, array module)
+
+    def attached(self, key, factory):
+        """The context's resource under `key`, made by factory(context) on first use
+        and closed before the context itself."""
+        self.handle
+        if key not in self._attached:
+            self._attached[key] = factory(self)
+        return self._attached[key]
 
     @property
     def device(self):
-        record = DeviceRecord()
-        self._lib.check(self._lib.api.pr_context_device(self.handle, _c.byref(record)))
-        return Device._from(record)
+        r = DeviceRecord()
+        self._lib.call("pr_context_device", self.handle, _c.byref(r))
+        return Device._from(r)
 
     @property
     def capabilities(self):
-        record = versioned(CapabilityRecord)
-        self._lib.check(self._lib.api.pr_context_capabilities(self.handle, _c.byref(record)))
-        return DeviceCapabilities._from(record)
+        r = versioned(CapabilityRecord)
+        self._lib.call("pr_context_capabilities", self.handle, _c.byref(r))
+        return DeviceCapabilities._from(r)
 
     def buffer(self, size):
         return Buffer(self, size)
@@ -405,133 +492,122 @@ class Context(Owned):
         return Queue(self)
 
     def synchronize(self):
-        self._lib.check(self._lib.api.pr_context_synchronize(self.handle))
+        self._lib.call("pr_context_synchronize", self.handle)
 
     def write_evidence(self, directory):
-        self._lib.check(self._lib.api.pr_context_write_evidence(
-            self.handle, _cstring(directory, "evidence directory")))
+        self._lib.call("pr_context_write_evidence", self.handle, _encode(directory, "evidence directory"))
 
     def close(self):
-        failure = None
-        for name in ("_tensor_resources", "_array_resources"):
-            resources = getattr(self, name, None)
-            setattr(self, name, None)
-            if resources is not None:
-                try:
-                    resources.close()
-                except Exception as error:
-                    failure = failure or error
+        errors = []
+        for resource in reversed(list(getattr(self, "_attached", {}).values())):
+            try:
+                resource.close()
+            except Exception as error:
+                errors.append(error)
+        self._attached = {}
         try:
             super().close()
         except Exception as error:
-            failure = failure or error
-        if failure is not None:
-            raise failure
+            errors.append(error)
+        if errors:
+            raise errors[0]
+
+
+def _require(value, kind, what):
+    if not isinstance(value, kind):
+        raise TypeError(f"{what} requires a {kind.__name__}, got {type(value).__name__}")
+    return value
 
 
 class Buffer(Owned):
-    """Device allocation of `size` bytes owned by a context."""
+    """A device allocation of `size` bytes owned by a context."""
 
     def __init__(self, context, size):
-        if not isinstance(context, Context):
-            raise TypeError("Buffer requires a Context")
-        self._lib, self._handle = context._lib, 0
-        handle = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_buffer_create(context.handle, _u64(size, "buffer size"),
-                                                      _c.byref(handle)))
-        self._handle = handle.value
+        _require(context, Context, "Buffer")
+        self._own(context._lib, context._lib.acquire("pr_buffer_create", context.handle, _u64(size, "buffer size")))
 
     @property
     def size(self):
-        value = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_buffer_size(self.handle, _c.byref(value)))
-        return value.value
+        out = _c.c_uint64()
+        self._lib.call("pr_buffer_size", self.handle, _c.byref(out))
+        return out.value
 
     def write(self, data, *, offset=0):
-        view = memoryview(data)
-        if not view.c_contiguous:
-            raise ValueError("write requires C-contiguous host bytes; no layout conversion is performed")
-        view = view.cast("B")
-        if view.nbytes == 0:
-            storage = None
-        elif view.readonly:  # copy; writable host memory is passed without a copy
-            storage = _c.create_string_buffer(view.tobytes(), view.nbytes)
+        """Blocking copy of C-contiguous host bytes (any buffer-protocol object)."""
+        bytes_view = memoryview(data)
+        if not bytes_view.c_contiguous:
+            raise ValueError("write: host data must be C-contiguous (no layout conversion is done)")
+        bytes_view = bytes_view.cast("B")
+        size = bytes_view.nbytes
+        if size == 0:
+            source = None
+        elif bytes_view.readonly:
+            source = _c.create_string_buffer(bytes_view.tobytes(), size)
         else:
-            storage = (_c.c_char * view.nbytes).from_buffer(view)
-        self._lib.check(self._lib.api.pr_buffer_write(self.handle, _u64(offset, "write offset"),
-                                                     storage, view.nbytes))
+            source = (_c.c_char * size).from_buffer(bytes_view)
+        self._lib.call("pr_buffer_write", self.handle, _u64(offset, "write offset"), source, size)
 
     def write_from(self, address, nbytes, *, offset=0):
         """Blocking copy of nbytes from a raw host (or device) address."""
-        self._lib.check(self._lib.api.pr_buffer_write(self.handle, _u64(offset, "write offset"),
-                                                     _c.c_void_p(address), _u64(nbytes, "size")))
+        self._lib.call("pr_buffer_write", self.handle, _u64(offset, "write offset"), _c.c_void_p(address),
+                       _u64(nbytes, "byte count"))
 
     def read(self, size=None, *, offset=0):
+        """Blocking copy of `size` bytes from `offset` (default: to the end) as bytes."""
         offset = _u64(offset, "read offset")
-        capacity = self.size
-        if offset > capacity:
-            raise Error(Status.OUT_OF_BOUNDS, "Buffer.read", "read offset exceeds buffer size")
-        size = capacity - offset if size is None else _u64(size, "read size")
-        if size > capacity - offset:
-            raise Error(Status.OUT_OF_BOUNDS, "Buffer.read", "read exceeds buffer size")
-        storage = bytearray(size)
+        total = self.size
+        size = total - offset if size is None else _u64(size, "read size")
+        if offset > total or size > total - offset:
+            raise Error(Status.OUT_OF_BOUNDS, "Buffer.read",
+                        f"bytes [{offset}, {offset + max(size, 0)}) are outside the {total}-byte buffer")
+        out = bytearray(size)
         if size:
-            target = (_c.c_char * size).from_buffer(storage)
-            self._lib.check(self._lib.api.pr_buffer_read(self.handle, offset, target, size))
-        return bytes(storage)
+            self._lib.call("pr_buffer_read", self.handle, offset, (_c.c_char * size).from_buffer(out), size)
+        return bytes(out)
 
     def read_into(self, address, nbytes, *, offset=0):
         """Blocking copy of nbytes into a raw host (or device) address."""
-        self._lib.check(self._lib.api.pr_buffer_read(self.handle, _u64(offset, "read offset"),
-                                                    _c.c_void_p(address), _u64(nbytes, "size")))
+        self._lib.call("pr_buffer_read", self.handle, _u64(offset, "read offset"), _c.c_void_p(address),
+                       _u64(nbytes, "byte count"))
 
     def view(self, *, offset=0, size=None, alignment=4, access=Access.READ_WRITE):
         return View(self, offset=offset, size=size, alignment=alignment, access=access)
 
 
 class View(Owned):
+    """A byte range of a buffer with an access mode: what kernels are bound to."""
+
     def __init__(self, buffer, *, offset=0, size=None, alignment=4, access=Access.READ_WRITE):
-        if not isinstance(buffer, Buffer):
-            raise TypeError("View requires a Buffer")
-        self._lib, self._handle = buffer._lib, 0
+        _require(buffer, Buffer, "View")
         offset = _u64(offset, "view offset")
         if size is None:
             size = buffer.size - offset
             if size < 0:
-                raise Error(Status.OUT_OF_BOUNDS, "View", "view offset exceeds buffer size")
-        handle = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_view_create(
-            buffer.handle, offset, _u64(size, "view size"), _int(alignment, 0, (1 << 32) - 1, "alignment"),
-            Access(access), _c.byref(handle)))
-        self._handle = handle.value
+                raise Error(Status.OUT_OF_BOUNDS, "View", f"offset {offset} is past the end of the buffer")
+        handle = buffer._lib.acquire("pr_view_create", buffer.handle, offset, _u64(size, "view size"),
+                                     _int(alignment, 0, 2 ** 32 - 1, "alignment"), Access(access))
+        self._own(buffer._lib, handle)
 
 
 class Module(Owned):
+    """A loaded kernel module (.prk artifact)."""
+
     @classmethod
     def load_file(cls, context, path):
-        if not isinstance(context, Context):
-            raise TypeError("Module.load_file requires a Context")
-        handle = _c.c_uint64()
-        context._lib.check(context._lib.api.pr_module_load_file(
-            context.handle, _cstring(path, "module path"), _c.byref(handle)))
-        return cls._adopt(context._lib, handle.value)
+        _require(context, Context, "Module.load_file")
+        return cls._adopt(context._lib, context._lib.acquire("pr_module_load_file", context.handle,
+                                                             _encode(path, "module path")))
 
     @classmethod
     def load(cls, context, data):
-        if not isinstance(context, Context):
-            raise TypeError("Module.load requires a Context")
-        data = bytes(memoryview(data))
-        storage = _c.create_string_buffer(data, len(data)) if data else None
-        handle = _c.c_uint64()
-        context._lib.check(context._lib.api.pr_module_load(context.handle, storage, len(data),
-                                                        _c.byref(handle)))
-        return cls._adopt(context._lib, handle.value)
+        _require(context, Context, "Module.load")
+        raw = bytes(memoryview(data))
+        image = _c.create_string_buffer(raw, len(raw)) if raw else None
+        return cls._adopt(context._lib, context._lib.acquire("pr_module_load", context.handle, image, len(raw)))
 
     def kernel(self, name):
-        handle = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_module_kernel(self.handle, _cstring(name, "kernel name"),
-                                                      _c.byref(handle)))
-        return Kernel._adopt(self._lib, handle.value)
+        return Kernel._adopt(self._lib, self._lib.acquire("pr_module_kernel", self.handle,
+                                                          _encode(name, "kernel name")))
 
 
 @dataclass(frozen=True)
@@ -546,36 +622,49 @@ class Kernel(Owned):
     @property
     def parameters(self):
         count = _c.c_uint32()
-        self._lib.check(self._lib.api.pr_kernel_parameter_count(self.handle, _c.byref(count)))
-        result = []
+        self._lib.call("pr_kernel_parameter_count", self.handle, _c.byref(count))
+        found = []
         for index in range(count.value):
-            record = ParameterRecord()
-            self._lib.check(self._lib.api.pr_kernel_parameter(self.handle, index, _c.byref(record)))
-            result.append(Parameter(_text(record.name), Type(record.type), bool(record.is_buffer),
-                                    Access(record.access)))
-        return tuple(result)
+            r = ParameterRecord()
+            self._lib.call("pr_kernel_parameter", self.handle, index, _c.byref(r))
+            found.append(Parameter(_decode(r.name), Type(r.type), r.is_buffer != 0, Access(r.access)))
+        return tuple(found)
+
+
+# ---------------------------------------------------------------- scalar arguments
+_FLT_MAX = 3.4028234663852886e38
+
+
+def _as_i32(value):
+    return _int(value, -2 ** 31, 2 ** 31 - 1, "i32")
+
+
+def _as_u32(value):
+    return _int(value, 0, 2 ** 32 - 1, "u32")
+
+
+def _as_f32(value):
+    if isinstance(value, bool) or not isinstance(value, (int, float)):
+        raise TypeError(f"f32: expected an int or float, got {type(value).__name__}")
+    value = float(value)
+    if math.isfinite(value) and abs(value) > _FLT_MAX:
+        raise ValueError(f"f32: {value} overflows binary32")
+    return _c.c_float(value).value  # rounded to binary32 once, here
+
+
+_SCALAR_RULES = {Type.I32: ("i32", _as_i32), Type.U32: ("u32", _as_u32), Type.F32: ("f32", _as_f32)}
 
 
 @dataclass(frozen=True)
 class Scalar:
+    """A typed by-value kernel argument; the value is checked (and f32 rounded) once."""
     type: Type
     value: object
 
     def __post_init__(self):
-        if self.type == Type.I32:
-            value = _int(self.value, -(1 << 31), (1 << 31) - 1, "i32")
-        elif self.type == Type.U32:
-            value = _int(self.value, 0, (1 << 32) - 1, "u32")
-        elif self.type == Type.F32:
-            if not isinstance(self.value, (int, float)) or isinstance(self.value, bool):
-                raise TypeError("f32 requires an explicit integer or float value")
-            value = float(self.value)
-            if math.isfinite(value) and abs(value) > 3.4028234663852886e38:
-                raise ValueError("f32 value exceeds the finite FP32 range")
-            value = _c.c_float(value).value
-        else:
-            raise ValueError("Scalar type must be I32, U32 or F32")
-        object.__setattr__(self, "value", value)
+        if self.type not in _SCALAR_RULES:
+            raise ValueError("a Scalar is I32, U32 or F32")
+        object.__setattr__(self, "value", _SCALAR_RULES[self.type][1](self.value))
 
 
 def i32(value):
@@ -590,50 +679,46 @@ def f32(value):
     return Scalar(Type.F32, value)
 
 
-def _dim3(value):
+def _dims(value, label):
     if isinstance(value, int) and not isinstance(value, bool):
         value = (value, 1, 1)
     if not isinstance(value, (tuple, list)) or len(value) != 3:
-        raise TypeError("dimensions require an integer or an (x, y, z) tuple")
-    return Dim3(*(_int(v, 0, (1 << 32) - 1, "dimension") for v in value))
+        raise TypeError(f"{label}: expected an int or an (x, y, z) triple")
+    return Dim3(*(_int(v, 0, 2 ** 32 - 1, label) for v in value))
 
 
 class Queue(Owned):
-    """The context's single in-order queue."""
+    """A handle of the context's single in-order queue."""
 
     def __init__(self, context):
-        if not isinstance(context, Context):
-            raise TypeError("Queue requires a Context")
-        self._lib, self._handle = context._lib, 0
-        handle = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_queue_get(context.handle, _c.byref(handle)))
-        self._handle = handle.value
+        _require(context, Context, "Queue")
+        self._own(context._lib, context._lib.acquire("pr_queue_get", context.handle))
 
     def synchronize(self):
-        self._lib.check(self._lib.api.pr_queue_synchronize(self.handle))
+        self._lib.call("pr_queue_synchronize", self.handle)
 
     def launch(self, kernel, arguments, *, grid, block):
-        if not isinstance(kernel, Kernel):
-            raise TypeError("launch requires a Kernel")
+        """Enqueues `kernel` over grid x block with View and Scalar arguments in
+        parameter order; returns the command's Event."""
+        _require(kernel, Kernel, "launch")
         if kernel._lib is not self._lib:
-            raise ValueError("kernel and queue originate from different native libraries")
-        arguments = tuple(arguments)
-        native = (ArgumentRecord * len(arguments))()
-        for index, argument in enumerate(arguments):
+            raise ValueError("launch: the kernel comes from another native library")
+        arguments = list(arguments)
+        packed = (ArgumentRecord * len(arguments))()
+        for slot, argument in zip(packed, arguments):
             if isinstance(argument, View):
                 if argument._lib is not self._lib:
-                    raise ValueError("view and queue originate from different native libraries")
-                native[index].type, native[index].view = Type.BUFFER, argument.handle
+                    raise ValueError("launch: a view comes from another native library")
+                slot.type, slot.view = Type.BUFFER, argument.handle
             elif isinstance(argument, Scalar):
-                native[index].type = argument.type
-                setattr(native[index], {Type.I32: "i32", Type.U32: "u32", Type.F32: "f32"}[argument.type],
-                        argument.value)
+                slot.type = argument.type
+                setattr(slot, _SCALAR_RULES[argument.type][0], argument.value)
             else:
-                raise TypeError("kernel arguments require View or explicit i32/u32/f32 values")
-        handle = _c.c_uint64()
-        self._lib.check(self._lib.api.pr_launch(self.handle, kernel.handle, _dim3(grid), _dim3(block),
-                                               native, len(arguments), _c.byref(handle)))
-        return Event._adopt(self._lib, handle.value)
+                raise TypeError("launch: arguments are Views and i32/u32/f32 Scalars, got "
+                                f"{type(argument).__name__}")
+        handle = self._lib.acquire("pr_launch", self.handle, kernel.handle, _dims(grid, "grid"),
+                                   _dims(block, "block"), packed, len(arguments))
+        return Event._adopt(self._lib, handle)
 
 
 @dataclass(frozen=True)
@@ -644,16 +729,18 @@ class EventInfo:
 
 
 class Event(Owned):
+    """Completion of one queued command."""
+
     def wait(self):
-        record = EventRecord()
-        self._lib.check(self._lib.api.pr_event_wait(self.handle, _c.byref(record)))
-        return EventInfo(bool(record.completed), record.gpu_start_seconds, record.gpu_end_seconds)
+        r = EventRecord()
+        self._lib.call("pr_event_wait", self.handle, _c.byref(r))
+        return EventInfo(r.completed != 0, r.gpu_start_seconds, r.gpu_end_seconds)
 
     def timing(self):
-        """Waits, propagates command failure, returns the duration-only timing record."""
-        record = versioned(TimingRecord)
-        self._lib.check(self._lib.api.pr_event_timing(self.handle, _c.byref(record)))
-        return EventTiming._from(record)
+        """Waits for the command (raising its failure) and returns its timing."""
+        r = versioned(TimingRecord)
+        self._lib.call("pr_event_timing", self.handle, _c.byref(r))
+        return EventTiming._from(r)
 
     def cancel(self):
-        self._lib.check(self._lib.api.pr_event_cancel(self.handle))
+        self._lib.call("pr_event_cancel", self.handle)

@@ -292,9 +292,9 @@ def test_tallest_narrow_product_runs_on_the_tensor_cores(context, tmp_path):
 @pytest.mark.parametrize("mode", (p.MatmulMode.REFERENCE, p.MatmulMode.FFMA, p.MatmulMode.TF32X3))
 def test_nonfinite_inputs_per_mode(context, mode):
     # Row 0 of A holds +inf, row 1 a NaN, the rest finite; B is finite and nonzero.
-    # REFERENCE / FFMA: row 0 is +-inf (IEEE, sequential order), row 1 NaN. TF32X3: the
-    # infinite operand's low half is inf - inf, so row 0 is NaN as well. Rows without
-    # exceptional inputs are unaffected in every mode.
+    # REFERENCE / FFMA: row 0 is +-inf (IEEE, sequential order), row 1 NaN. An explicit
+    # TF32X3 request: the infinite operand's low half is inf - inf, so row 0 is NaN as
+    # well. Rows without exceptional inputs are unaffected in every mode.
     m, n, k = 130, 70, 64
     a = synthetic.uniform(9400, 0, m * k).reshape(m, k)
     b = np.abs(synthetic.uniform(9401, 0, k * n).reshape(k, n)) + np.float32(0.5)
@@ -312,3 +312,78 @@ def test_nonfinite_inputs_per_mode(context, mode):
         assert np.all(c[0] == np.inf)
     exact, magnitude = oracle.matmul_exact(a[2:].ravel(), b.ravel(), m - 2, n, k)
     assert np.all(np.abs(c[2:].astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
+
+
+def same_specials_and_contract(c, a, b, m, n, k):
+    """c has the reference order's +-inf / NaN pattern (oracle sequential product) and
+    its finite entries are within the FP32 contract of the float64 product."""
+    want = oracle.matmul(a, b, m, n, k)
+    special = ~np.isfinite(want)
+    assert np.array_equal(np.isnan(c), np.isnan(want))
+    assert np.array_equal(c[np.isinf(want)], want[np.isinf(want)])
+    exact, magnitude = oracle.matmul_exact(a, b, m, n, k)
+    finite = ~special
+    assert np.all(np.isfinite(c[finite]))
+    err = np.abs(c[finite].astype(np.float64) - exact[finite])
+    assert np.all(err <= oracle.matmul_tolerance(magnitude, k)[finite])
+
+
+# AUTO picks the 3xTF32 kernel for these shapes; an infinite operand (or one whose TF32
+# high part rounds to infinity) raises the command's non-finite word in the split pass
+# or in the GEMM's shared-memory converter, and the guarded FFMA kernel recomputes C in
+# IEEE order, so +-inf propagate as in the reference (docs/tensors-matmul.md:80).
+#   (300, 260, 96): A converted in shared memory (two column tiles), B split
+#   (300, 1000, 96): both operands split
+#   (4096, 100, 96): the transposed form (n <= 128: A's rows converted as the wide side)
+@pytest.mark.parametrize("m,n,k", [(300, 260, 96), (300, 1000, 96), (4096, 100, 96)])
+@pytest.mark.parametrize("where", ("a", "b", "huge"))
+def test_auto_mode_propagates_infinities_like_the_reference(context, m, n, k, where):
+    a = synthetic.uniform(9500, 0, m * k).reshape(m, k)
+    b = synthetic.uniform(9501, 0, k * n).reshape(k, n)
+    if where == "a":
+        a[0, 5], a[m - 1, k - 1], a[m // 2, 0] = np.inf, -np.inf, np.nan
+    elif where == "b":
+        b[3, 0], b[k - 1, n - 1] = np.inf, -np.inf
+    else:  # finite, but its TF32 high part rounds to infinity; every product stays finite
+        a[2, 7] = np.finfo(np.float32).max
+        b[7, :] = np.float32(0.25)
+    p.set_matmul_mode(context, p.MatmulMode.AUTO)
+    c = aligned_matmul(context, a, b, m, n, k, False)
+    assert p.b200.last_variant(context, "paralyn_matmul_f32") == "tcgen05_tf32x3"
+    same_specials_and_contract(c, a.ravel(), b.ravel(), m, n, k)
+    if where == "huge":
+        assert np.all(np.isfinite(c))
+
+
+def test_auto_mode_with_finite_operands_is_the_tf32x3_result(context):
+    # The guarded FFMA kernel leaves C alone when no operand held an infinity: AUTO and
+    # an explicit TF32X3 request give the same bits.
+    m, n, k = 300, 1000, 96
+    a = synthetic.uniform(9510, 0, m * k).reshape(m, k)
+    b = synthetic.uniform(9511, 0, k * n).reshape(k, n)
+    results = []
+    for mode in (p.MatmulMode.AUTO, p.MatmulMode.TF32X3):
+        p.set_matmul_mode(context, mode)
+        results.append(aligned_matmul(context, a, b, m, n, k, False))
+    p.set_matmul_mode(context, p.MatmulMode.AUTO)
+    assert results[0].tobytes() == results[1].tobytes()
+
+
+def test_auto_mode_batched_propagates_infinities(context):
+    batch, m, n, k = 3, 256, 256, 64
+    a = synthetic.uniform(9520, 0, batch * m * k).reshape(batch, m, k)
+    b = synthetic.uniform(9521, 0, batch * k * n).reshape(batch, k, n)
+    a[1, 4, 2] = np.inf
+    b[2, 9, 17] = -np.inf
+    p.set_matmul_mode(context, p.MatmulMode.AUTO)
+    with p.tensor(a.ravel(), shape=(batch, m, k), context=context) as ta, \
+            p.tensor(b.ravel(), shape=(batch, k, n), context=context) as tb, p.batched_matmul(ta, tb) as tc:
+        c = np.asarray(tc.to_host(), np.float32).reshape(batch, m, n)
+    assert p.b200.last_variant(context, "paralyn_batched_matmul_f32") == "batched_tcgen05_tf32x3"
+    for z in range(batch):
+        want = oracle.matmul(a[z].ravel(), b[z].ravel(), m, n, k)
+        if np.all(np.isfinite(want)):
+            exact, magnitude = oracle.matmul_exact(a[z].ravel(), b[z].ravel(), m, n, k)
+            assert np.all(np.abs(c[z] - exact) <= oracle.matmul_tolerance(magnitude, k))
+        else:
+            same_specials_and_contract(c[z], a[z].ravel(), b[z].ravel(), m, n, k)

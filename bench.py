@@ -58,7 +58,8 @@ def parse():
     ap.add_argument("--matmul-mode", default="auto", choices=("auto", "reference", "ffma", "tf32x3"),
                     help="summation mode of the GEMM workloads (default auto: the 3xTF32 tensor-core kernel)")
     ap.add_argument("--gather", action="store_true",
-                    help="chain: also gather Y on every GPU (LayerNorm writes its rows to all ranks over NVLink)")
+                    help="chain: also gather Y on every GPU (LayerNorm writes its rows to all ranks over NVLink); "
+                         "gemm: gather C on every GPU after the GEMM (peer-store kernel)")
     return ap.parse_args()
 
 
@@ -191,10 +192,12 @@ def describe(name, world, rank, gather=False):
         return METRICS[name], "TFLOP/s", "strong", config
     if name == "gemm":
         r0, r1 = shard.row_range(4096, world, rank)
-        return METRICS[name], "TFLOP/s", "strong", {
-            "workload": "gemm: C = A B, M=N=K=4096, A,B ~ U[-1,1), seed 3", "m": 4096, "n": 4096, "k": 4096,
-            "rows_per_gpu": r1 - r0, "parallelism": f"rows{world}",
-            "l2": "operands are 64 MiB each; A/B re-reads are part of the GEMM"}
+        config = {"workload": "gemm: C = A B, M=N=K=4096, A,B ~ U[-1,1), seed 3", "m": 4096, "n": 4096, "k": 4096,
+                  "rows_per_gpu": r1 - r0, "parallelism": f"rows{world}",
+                  "l2": "operands are 64 MiB each; A/B re-reads are part of the GEMM"}
+        if gather:
+            config["gathered_output"] = "C gathered on every GPU (pr_b200_gather_rows_f32: peer stores over NVLink)"
+        return METRICS[name], "TFLOP/s", "strong", config
     if name == "layernorm":
         r0, r1 = shard.row_range(16384, world, rank)
         return METRICS[name], "GB/s", "strong", {
@@ -272,6 +275,9 @@ class Workload:
                 e.close()
             self.units_total, self.units_local = 2 * m * n * k, 2 * self.m_local * n * k
             self.h2d, self.d2h = 4 * self.m_local * k, 4 * self.m_local * n
+            self.r0, self.gather = r0, None
+            if gather:  # C gathered on every GPU by a peer-store kernel after the GEMM
+                self.gather = shard.GatheredOutput(ctx, m, n, group.exchange, rank)
         elif name == "layernorm":
             rows, cols = 16384, 4096
             r0, r1 = shard.row_range(rows, world, rank)
@@ -375,9 +381,13 @@ class Workload:
             return [mm, ln], mm
         if self.name == "gemm":
             D = self.T.TensorDescriptor
+            c = D(self.c, (self.m_local, self.n))
             e = self.T.matmul_into(self.queue, self.res.module, D(self.a, (self.m_local, self.k)), D(self.b, (self.k, self.n)),
-                                   D(self.c, (self.m_local, self.n)), m=self.m_local, n=self.n, k=self.k)
-            return [e], e
+                                   c, m=self.m_local, n=self.n, k=self.k)
+            if self.gather is None:
+                return [e], e
+            g = self.b200.gather_rows_into(self.queue, c, self.gather.targets, row_offset=self.r0)
+            return [e, g], e
         if self.name == "layernorm":
             D = self.T.TensorDescriptor
             e = self.T.layer_norm_into(self.queue, self.res.module, D(self.x, (self.rows_local, self.cols)),

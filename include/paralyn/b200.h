@@ -69,6 +69,19 @@ pr_status pr_b200_buffer_import(pr_context context, const void *handle, pr_buffe
 pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module operators, const pr_layer_norm_v1 *op,
                                         const pr_tensor_desc_v1 *const *gathered, uint32_t count,
                                         uint64_t row_offset, pr_event *out);
+/* The same gathered output for any row-sharded result, e.g. a GEMM shard's C (the
+ * reference has no multi-GPU operators; this is the optional all-gather of the
+ * row-sharded path): one kernel reads `local` [rows, columns] once and writes it at
+ * rows [row_offset, row_offset + rows) of every tensor of `gathered` (contiguous
+ * [R_total, columns], local or imported) with plain stores, 128-bit where aligned.
+ * A gathered tensor may hold `local` exactly at those rows; any other overlap of
+ * `local` or between gathered tensors is rejected (PR_INVALID_ARGUMENT for
+ * overlapping bytes, PR_UNSUPPORTED for a shared allocation). Completion as for the
+ * gathered LayerNorm: the kernel ends with a system-scope fence and the ranks
+ * synchronize on the host before reading. */
+pr_status pr_b200_gather_rows_f32(pr_queue queue, const pr_tensor_desc_v1 *local,
+                                  const pr_tensor_desc_v1 *const *gathered, uint32_t count, uint64_t row_offset,
+                                  pr_event *out);
 
 /* ---- Stream-ordered host copies (no counterpart in the reference) ----
  * pr_buffer_write / pr_buffer_read drain the queue and block, as the reference

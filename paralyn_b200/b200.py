@@ -23,6 +23,7 @@ pr_b200_module_inspect ptr u64 str u64
 pr_b200_buffer_export h ptr
 pr_b200_buffer_import h ptr *h
 pr_b200_layer_norm_gather_f32 h h ptr ptr u32 u64 *h
+pr_b200_gather_rows_f32 h ptr ptr u32 u64 *h
 pr_b200_buffer_write_async h h u64 ptr u64 *h
 pr_b200_buffer_read_async h h u64 ptr u64 *h
 pr_b200_host_register ptr u64
@@ -109,6 +110,19 @@ def layer_norm_gather_into(queue, operators, x, gamma, beta, out, gathered, *, r
     handle = _c.c_uint64()
     lib.check(lib.api.pr_b200_layer_norm_gather_f32(queue.handle, operators.handle, _c.byref(record), array,
                                                     len(natives), row_offset, _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
+
+
+def gather_rows_into(queue, local, gathered, *, row_offset):
+    """Write the rows of `local` (a [rows, columns] descriptor) at row row_offset + i of
+    every descriptor in `gathered` (local or imported); returns the Event or None."""
+    lib = _b200(queue._lib)
+    source = local._native()
+    natives = [g._native() for g in gathered]
+    array = (_c.POINTER(TensorDescRecord) * max(1, len(natives)))(*(_pointer(d) for d in natives))
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_gather_rows_f32(queue.handle, _c.byref(source), array, len(natives), row_offset,
+                                              _c.byref(handle)))
     return Event._adopt(lib, handle.value) if handle.value else None
 
 

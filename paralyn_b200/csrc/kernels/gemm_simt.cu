@@ -14,6 +14,7 @@
 // in L2.
 #include "../runtime/builtin.hpp"
 #include "activation.cuh"
+#include "tma.cuh"
 #include <algorithm>
 
 namespace pb {
@@ -223,6 +224,221 @@ __device__ __forceinline__ void simt_tile(const GemmArgs &g, int64_t id, int64_t
   }
 }
 
+// ---- TMA-fed form (A not transposed or transposed, B not transposed) ----
+// The same 128 x 128 tiles, 8 x 8 register tiles and per-output k order, with the
+// operands moved by the tensor memory accelerator instead of the threads: 32-deep
+// k-slices of A and B land in a three-stage shared-memory ring (96 KB, two CTAs per
+// SM), each stage tracked by a `full` barrier (TMA transaction bytes) and an `empty`
+// barrier (one arrival per warp once it has read the stage). Thread 0 refills a
+// stage one slice after the warps released it, so the warps only load shared
+// memory and multiply: no global loads, shared stores or block barriers in the
+// k loop. Layouts in shared memory:
+//   A stored [m][k] (row-major): each stage holds A[m0..+128][k0..+32] as 128-byte
+//     rows with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)).
+//     Thread (tx, ty) owns rows ty + 16 i (i < 8), which share one swizzle phase, so
+//     one chunk offset per k pair serves all eight; the two rows a warp reads per
+//     instruction (ty and ty + 1) fall in different banks. A thread reads float2
+//     along k for each of its rows and uses them for 2 k.
+//   A stored [k][m] (transposed): A[k0..+32][m0..+128] as 512-byte rows; float4
+//     along m, as in the register-staged kernel.
+//   B stored [k][n]: B[k0..+32][n0..+128] as 512-byte rows; float4 along n.
+// Rows and columns past the matrix and k past K read as zero (TMA fill), adding
+// exact +0.0 products that leave every sum unchanged.
+constexpr int TBK = 32, TSTAGES = 3;
+constexpr int TA_BYTES = BM * TBK * 4, TB_BYTES = TBK * BN * 4, TSTAGE = TA_BYTES + TB_BYTES;
+constexpr int TSMEM = 1024 + TSTAGES * TSTAGE + 256;
+constexpr int STATUS_TIMEOUT_SIMT = 0x7f3205;
+
+template <int MODE, bool TA>
+__global__ void __launch_bounds__(THREADS, 2)
+    gemm_simt_tma(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, const GemmArgs g,
+                  int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned (the 128-byte swizzle repeats every 1024 bytes); an offset from
+  // the shared array keeps the accesses in the shared state space.
+  uint8_t *smem = smem_raw + ((1024u - (tma::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + TSTAGES * TSTAGE);
+  uint64_t *empty = full + TSTAGES;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + TSTAGES);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+
+  const int64_t tiles_m = (g.m + BM - 1) / BM, tiles_n = (g.n + BN - 1) / BN;
+  const int64_t id = blockIdx.x, group = 8, per_group = group * tiles_n;
+  const int64_t first_m = (id / per_group) * group;
+  const int64_t rows_in_group = min(group, tiles_m - first_m);
+  const int m0 = int((first_m + (id % per_group) % rows_in_group) * BM);
+  const int n0 = int(((id % per_group) / rows_in_group) * BN);
+  const int slices = int((g.k + TBK - 1) / TBK);
+
+  auto issue = [&](int slice) { // thread 0: slice -> stage slice % TSTAGES
+    const int st = slice % TSTAGES;
+    uint8_t *stage = smem + st * TSTAGE;
+    tma::mbar_expect_tx(&full[st], TSTAGE);
+    if (TA)
+      tma::tma_load_2d(stage, &amap, &full[st], m0, slice * TBK);
+    else
+      tma::tma_load_2d(stage, &amap, &full[st], slice * TBK, m0);
+    tma::tma_load_2d(stage + TA_BYTES, &bmap, &full[st], n0, slice * TBK);
+  };
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < TSTAGES; ++st) {
+      tma::mbar_init(&full[st], 1);
+      tma::mbar_init(&empty[st], THREADS / 32);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  int issued = 0;
+  if (threadIdx.x == 0)
+    for (; issued < min(TSTAGES, slices); ++issued)
+      issue(issued);
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      acc[i][j] = 0.0f;
+
+  int done = 0; // slices this thread consumed
+  for (int slice = 0; slice < slices; ++slice) {
+    const int st = slice % TSTAGES;
+    // Thread 0 refills the stage released one slice ago (all eight warps read it).
+    if (threadIdx.x == 0 && slice >= 1 && issued < slices && !*abort_flag) {
+      const int prev = (slice - 1) % TSTAGES;
+      if (tma::mbar_wait(&empty[prev], ((slice - 1) / TSTAGES) & 1)) {
+        issue(issued);
+        ++issued;
+      } else {
+        atomicExch(status, STATUS_TIMEOUT_SIMT);
+        *abort_flag = 1;
+      }
+    }
+    if (!tma::mbar_wait(&full[st], (slice / TSTAGES) & 1)) {
+      atomicExch(status, STATUS_TIMEOUT_SIMT);
+      *abort_flag = 1;
+    }
+    if (*abort_flag)
+      break;
+    const float *As = reinterpret_cast<const float *>(smem + st * TSTAGE);
+    const float *Bs = reinterpret_cast<const float *>(smem + st * TSTAGE + TA_BYTES);
+#pragma unroll
+    for (int kq = 0; kq < TBK / 2; ++kq) {
+      float a4[8][2]; // this thread's 8 rows x 2 consecutive k
+      if (!TA) { // rows ty + 16 i: all in swizzle phase ty % 8, one chunk offset per kq
+        const int offset = ((((kq >> 1) ^ ty) & 7) << 2) + 2 * (kq & 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 v = *reinterpret_cast<const float2 *>(As + (ty + 16 * i) * TBK + offset);
+          a4[i][0] = v.x, a4[i][1] = v.y;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const float4 v0 = *reinterpret_cast<const float4 *>(As + (kq * 2 + q) * BM + ty * 4);
+          const float4 v1 = *reinterpret_cast<const float4 *>(As + (kq * 2 + q) * BM + 64 + ty * 4);
+          a4[0][q] = v0.x, a4[1][q] = v0.y, a4[2][q] = v0.z, a4[3][q] = v0.w;
+          a4[4][q] = v1.x, a4[5][q] = v1.y, a4[6][q] = v1.z, a4[7][q] = v1.w;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int kk = kq * 2 + q;
+        const float4 b0 = *reinterpret_cast<const float4 *>(Bs + kk * BN + tx * 4);
+        const float4 b1 = *reinterpret_cast<const float4 *>(Bs + kk * BN + 64 + tx * 4);
+        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            acc[i][j] = mac<MODE>(acc[i][j], a4[i][q], b[j]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0)
+      tma::mbar_arrive(&empty[st]);
+    done = slice + 1;
+  }
+  __syncthreads();
+  if (*abort_flag) {
+    if (threadIdx.x == 0) // copies requested but not consumed land before the block ends
+      for (int slice = done; slice < issued; ++slice)
+        (void)tma::mbar_wait(&full[slice % TSTAGES], (slice / TSTAGES) & 1);
+    return; // C is left as it was; the command reports the status
+  }
+  (void)warp;
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t m = m0 + (TA ? (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4)) : ty + 16 * i);
+    if (m >= g.m)
+      continue;
+    float *row = g.c + m * g.ldc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t n = n0 + h * 64 + tx * 4;
+      float v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
+      if (g.bias || g.activation) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < g.n)
+            v[j] = bias_activate(v[j], g.bias, n + j, g.activation);
+      }
+      if (g.vec_c && n + 3 < g.n) {
+        *reinterpret_cast<float4 *>(row + n) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < g.n)
+            row[n + j] = v[j];
+      }
+    }
+  }
+}
+
+template <int MODE, bool TA> bool configure_simt_tma(int device) {
+  static bool configured[64] = {};
+  if (device < 0 || device >= 64)
+    return false;
+  if (!configured[device]) {
+    if (cudaFuncSetAttribute(gemm_simt_tma<MODE, TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    configured[device] = true;
+  }
+  return true;
+}
+
+// The TMA-fed kernel for one (non-batched) product when its operands can be tensor
+// maps: B not transposed, 16-byte aligned bases and row strides, dimensions that fit
+// the maps' 32-bit coordinates. Returns false (nothing enqueued) otherwise.
+template <int MODE>
+bool launch_simt_tma(Launch &L, const GemmArgs &g, bool ta, bool tb) {
+  if (tb || g.c_col != 1 || g.m > INT32_MAX - BM || g.n > INT32_MAX - BN || g.k > INT32_MAX - TBK)
+    return false;
+  if ((reinterpret_cast<uintptr_t>(g.a) & 15u) || (reinterpret_cast<uintptr_t>(g.b) & 15u) || g.lda % 4 ||
+      g.ldb % 4)
+    return false;
+  CUtensorMap amap, bmap;
+  const bool a_ok = ta ? encode_map_2d(&amap, g.a, uint64_t(g.m), uint64_t(g.k), uint64_t(g.lda) * 4, BM, TBK, false)
+                       : encode_map_2d(&amap, g.a, uint64_t(g.k), uint64_t(g.m), uint64_t(g.lda) * 4, TBK, BM, true);
+  if (!a_ok || !encode_map_2d(&bmap, g.b, uint64_t(g.n), uint64_t(g.k), uint64_t(g.ldb) * 4, BN, TBK, false))
+    return false;
+  if (!(ta ? configure_simt_tma<MODE, true>(L.device) : configure_simt_tma<MODE, false>(L.device)))
+    return false;
+  const int64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + BN - 1) / BN);
+  if (ta)
+    gemm_simt_tma<MODE, true><<<uint32_t(tiles), THREADS, TSMEM, L.stream>>>(amap, bmap, g, L.status);
+  else
+    gemm_simt_tma<MODE, false><<<uint32_t(tiles), THREADS, TSMEM, L.stream>>>(amap, bmap, g, L.status);
+  return true;
+}
+
 // One block per tile. GUARDED: the launch does nothing unless *only_if == epoch,
 // and fewer blocks than tiles walk the tiles id = blockIdx.x, + gridDim.x, ...
 template <int MODE, bool TA, bool TB, bool GUARDED>
@@ -369,14 +585,20 @@ void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
     }
     mode = matmul_ffma;
   }
+  L.kernels = 1;
   if (mode == matmul_reference) {
+    // The register-staged kernel: in the reference order (a separate multiply and add
+    // per step) it measured 29.8 TFLOP/s at 4096^3 against 21.7 for the TMA-fed form.
     dispatch<matmul_reference>(g, ta, tb, L.stream);
     L.variant = "simt_reference_order";
   } else {
+    if (launch_simt_tma<matmul_ffma>(L, g, ta, tb)) {
+      L.variant = "simt_tma_ffma";
+      return;
+    }
     dispatch<matmul_ffma>(g, ta, tb, L.stream);
     L.variant = "simt_ffma";
   }
-  L.kernels = 1;
 }
 } // namespace
 

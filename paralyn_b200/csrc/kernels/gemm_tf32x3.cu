@@ -38,9 +38,11 @@
 //  returns, and the engine reports PR_EXECUTION_FAILED.
 #include "../runtime/builtin.hpp"
 #include "activation.cuh"
+#include "tma.cuh"
 #include <cuda.h>
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 
 namespace pb {
 namespace {
@@ -50,50 +52,16 @@ constexpr int A_BYTES = TM * TK * 4, B_BYTES = TN * TK * 4;
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr uint32_t TMEM_COLUMNS = 256;
-constexpr long long WAIT_CYCLES = 4000000000ll; // ~2 s at 1.9 GHz
+constexpr long long WAIT_CYCLES = tma::kWaitCycles;
 constexpr int STATUS_TIMEOUT_PRODUCER = 0x7f3201, STATUS_TIMEOUT_MMA = 0x7f3202,
               STATUS_TIMEOUT_EPILOGUE = 0x7f3203;
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Bounded wait: false when the phase did not complete within WAIT_CYCLES.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity))
-    return true;
-  const long long start = clock64();
-  while (!mbar_try_wait(bar, parity))
-    if (clock64() - start > WAIT_CYCLES)
-      return false;
-  return true;
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
+using tma::mbar_expect_tx;
+using tma::mbar_init;
+using tma::mbar_try_wait;
+using tma::mbar_wait;
+using tma::smem_u32;
+using tma::tma_load_2d;
 
 // Shared-memory matrix descriptor: K-major, SWIZZLE_64B (64-byte rows, 8-row
 // 512-byte atoms): start >> 4, leading byte offset 16 (unused for swizzled
@@ -294,6 +262,10 @@ struct TileArgs {
   // (as the split kernels do for the operands they split); null: not watched.
   unsigned long long *nonfinite = nullptr;
   unsigned long long epoch = 0;
+  // Tile rows per raster group (consecutive tiles walk the columns of `group` tile
+  // rows, so they share B's tiles in L2); the persistent kernels and split_fixup
+  // read it, the one-tile kernel uses 8.
+  int group = 8;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -543,7 +515,7 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
   auto locate = [&](int tile, int &a_y, int &b_y, int &m0, int &n0, int &z) {
     z = tile / per_batch;
-    const int id = tile % per_batch, group = 8, per_group = group * args.tiles_n;
+    const int id = tile % per_batch, group = args.group, per_group = group * args.tiles_n;
     const int first_m = (id / per_group) * group;
     const int rows_in_group = min(group, args.tiles_m - first_m);
     m0 = (first_m + (id % per_group) % rows_in_group) * TM;
@@ -816,26 +788,409 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
   }
 }
 
+// ---- CTA-pair persistent kernel (tcgen05.mma.cta_group::2) ----
+// A cluster of two CTAs on two SMs computes 256 x 256 output tiles: CTA r holds rows
+// [128 r, 128 r + 128) of the tile's A pair and rows [128 r, 128 r + 128) of its B
+// pair (the B^T side) in its own shared memory, and one MMA issued by CTA 0 reads
+// both CTAs' operands and writes each CTA's 128 x 256 accumulator into that CTA's
+// tensor memory. Each SM therefore stages and reads half of B instead of all of it:
+// per 16-deep slice an SM's shared memory takes 32 KB of TMA writes and feeds 48 KB
+// to the tensor cores (80 KB), against 48 KB + 72 KB for the one-SM 128 x 256 tile,
+// which was bound by that traffic rather than by the MMAs.
+//  warp 0 lane 0 (both CTAs): TMA producer. It waits for its own stage to be free
+//    (`empty`, signalled by CTA 0's MMA commit in both CTAs), CTA 0 arms its `full`
+//    barrier with both CTAs' bytes, and both CTAs' copies complete on CTA 0's
+//    barrier (cta_group::2 TMA, no multicast).
+//  warp 1 (both CTAs): allocates 512 TMEM columns as a pair (two 256-column
+//    accumulators); lane 0 of CTA 0 issues the MMAs and commits stages and
+//    accumulators to the barriers of both CTAs.
+//  warps 2-9 (both CTAs): drain the CTA's own accumulator as in the one-SM kernel and
+//    report to CTA 0's `tmem_empty` (16 arrivals: eight warps of each CTA).
+// Every wait is bounded. Before either CTA releases its shared and tensor memory,
+// CTA 0 waits for its last MMA to finish and both CTAs meet at a cluster barrier.
+constexpr int PAIR_HALF = 128, PAIR_M = 2 * PAIR_HALF, PAIR_N = 256;
+constexpr int PAIR_A_BYTES = PAIR_HALF * TK * 4, PAIR_B_BYTES = PAIR_HALF * TK * 4;
+constexpr int PAIR_STAGE = 2 * PAIR_A_BYTES + 2 * PAIR_B_BYTES; // 32 KB per CTA
+constexpr int PAIR_STAGES = RING_BYTES / PAIR_STAGE;            // 6
+constexpr uint32_t PAIR_COLUMNS = PAIR_N;                       // TMEM columns of one accumulator
+// D f32, A and B tf32, both K-major, N = 256, M = 256 (the pair's rows).
+constexpr uint32_t PAIR_IDESC =
+    (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(PAIR_N >> 3) << 17) | (uint32_t(PAIR_M >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of `p` (a shared-memory object of this CTA) in CTA `rank`.
+__device__ __forceinline__ uint32_t in_cta(const void *p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// One arrival on the barrier at `cluster_bar` (this CTA's or the peer's). Default
+// (release, CTA scope) semantics: the data a converter wrote is ordered for the
+// tensor cores by its fence.proxy.async, and a cluster-scope release here would put
+// a full memory barrier on every stage (measured: 2.5x slower pair kernel).
+__device__ __forceinline__ void arrive_at(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// A 2-D tile into this CTA's shared memory whose byte count completes on the barrier
+// at `cluster_bar` (CTA 0's, for both CTAs of the pair).
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t cluster_bar, int x,
+                                                 int y) {
+  asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+               " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+               : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(PAIR_IDESC), "r"(accumulate)
+      : "memory");
+}
+// Arrives (once) on the barrier at `cluster_bar` when every MMA this thread issued so
+// far has completed; called once per destination CTA.
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// RAW: A is read raw (FP32 boxes of its own rows, from the caller's matrix) and four
+// converter warps per CTA form its TF32 pair in shared memory with the split pass's
+// own conversion, so no split pass runs over A. The raw box of a stage completes on
+// the CTA's own `raw_full` barrier; the converters of both CTAs report to CTA 0's
+// `converted` barrier, which the MMA waits for besides `full` (now B's bytes only).
+template <bool RAW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
+    gemm_tf32x3_pair(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                     const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                     const TileArgs args) {
+  constexpr int S = PAIR_STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + RING_BYTES); // used in CTA 0
+  uint64_t *empty = full + S;
+  uint64_t *tmem_full = empty + S;
+  uint64_t *tmem_empty = tmem_full + 2; // used in CTA 0
+  uint64_t *drained = tmem_empty + 2;   // used in CTA 0
+  uint64_t *raw_full = drained + 1;     // RAW: this CTA's raw A box of the stage landed
+  uint64_t *converted = raw_full + S;   // RAW, CTA 0: both CTAs' A pairs of the stage are formed
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(converted + S);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *issued = abort_flag + 1;   // k-slices the producer has requested
+  volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received (CTA 0)
+  float *epi_tiles = reinterpret_cast<float *>(smem + RING_BYTES + BARRIER_BYTES);
+
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+  const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
+  auto locate = [&](int tile, int &m0, int &n0, int &z) { // m0 in rows of PAIR_M tiles
+    z = tile / per_batch;
+    const int id = tile % per_batch, group = args.group, per_group = group * args.tiles_n;
+    const int first_m = (id / per_group) * group;
+    const int rows_in_group = min(group, args.tiles_m - first_m);
+    m0 = (first_m + (id % per_group) % rows_in_group) * PAIR_M;
+    n0 = ((id % per_group) / rows_in_group) * PAIR_N;
+  };
+  auto unit = [&](int u, int &tile, int &kb0, int &kb1) {
+    if (u < args.full_units) {
+      tile = u;
+      kb0 = 0;
+      kb1 = args.k_blocks;
+    } else {
+      const int v = u - args.full_units, part = v % args.split;
+      tile = args.full_units + v / args.split;
+      kb0 = part * args.k_blocks / args.split;
+      kb1 = (part + 1) * args.k_blocks / args.split;
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 2 * EPI_WARPS);
+    }
+    mbar_init(drained, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&converted[s], 2 * 4); // the four converter warps of each CTA
+    }
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * PAIR_COLUMNS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  }
+  // Both CTAs' barriers are initialized and both hold the TMEM allocation before any
+  // copy or MMA of the pair reaches the other CTA.
+  cluster_sync_all();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t full0 = in_cta(full, 0), tmem_empty0 = in_cta(tmem_empty, 0);
+
+  if (warp == 0) {
+    if (lane == 0) { // TMA producer, both CTAs
+      int g = 0;
+      for (int u = pair; u < args.units_total && !*abort_flag; u += pairs) {
+        int tile, kb0, kb1, m0, n0, z;
+        unit(u, tile, kb0, kb1);
+        locate(tile, m0, n0, z);
+        const int a_y = z * args.a_rows + m0 + int(rank) * PAIR_HALF;
+        const int b_y = z * args.b_rows + n0 + int(rank) * PAIR_HALF;
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1)) {
+            atomicExch(args.status, STATUS_TIMEOUT_PRODUCER);
+            *abort_flag = 1;
+          }
+          if (*abort_flag)
+            break;
+          uint8_t *stage = smem + s * PAIR_STAGE;
+          const uint32_t bar = full0 + uint32_t(s) * 8u;
+          if (RAW) { // this CTA's raw rows of A, then both CTAs' B halves on CTA 0's barrier
+            mbar_expect_tx(&raw_full[s], PAIR_A_BYTES);
+            tma_load_3d(stage, &a_hi, &raw_full[s], kb * TK, m0 + int(rank) * PAIR_HALF, z);
+            if (leader)
+              mbar_expect_tx(&full[s], 2 * 2 * PAIR_B_BYTES);
+          } else {
+            if (leader)
+              mbar_expect_tx(&full[s], 2 * PAIR_STAGE);
+            tma_load_2d_pair(stage, &a_hi, bar, kb * TK, a_y);
+            tma_load_2d_pair(stage + PAIR_A_BYTES, &a_lo, bar, kb * TK, a_y);
+          }
+          tma_load_2d_pair(stage + 2 * PAIR_A_BYTES, &b_hi, bar, kb * TK, b_y);
+          tma_load_2d_pair(stage + 2 * PAIR_A_BYTES + PAIR_B_BYTES, &b_lo, bar, kb * TK, b_y);
+          *issued = g + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) { // MMA issuer for the pair
+      const uint32_t empty1 = in_cta(empty, 1), tmem_full1 = in_cta(tmem_full, 1);
+      const uint32_t empty0 = in_cta(empty, 0), tmem_full0 = in_cta(tmem_full, 0);
+      int g = 0, j = 0;
+      for (int u = pair; u < args.units_total && !*abort_flag; u += pairs, ++j) {
+        int tile, kb0, kb1;
+        unit(u, tile, kb0, kb1);
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1)) {
+          atomicExch(args.status, STATUS_TIMEOUT_MMA);
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + uint32_t(b) * PAIR_COLUMNS;
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(&full[s], (g / S) & 1) || (RAW && !mbar_wait(&converted[s], (g / S) & 1))) {
+            atomicExch(args.status, STATUS_TIMEOUT_MMA);
+            *abort_flag = 1;
+            break;
+          }
+          *consumed = g + 1;
+          if (*abort_flag)
+            break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t stage = smem_u32(smem + s * PAIR_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < TK / 8; ++kk) {
+            const uint32_t step = kk * 32;
+            const uint64_t ah = desc_k_sw64(stage + step), al = desc_k_sw64(stage + PAIR_A_BYTES + step);
+            const uint64_t bh = desc_k_sw64(stage + 2 * PAIR_A_BYTES + step);
+            const uint64_t bl = desc_k_sw64(stage + 2 * PAIR_A_BYTES + PAIR_B_BYTES + step);
+            mma_tf32_pair(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
+            mma_tf32_pair(acc, ah, bl, 1u);
+            mma_tf32_pair(acc, al, bh, 1u);
+          }
+          mma_commit_pair(empty0 + uint32_t(s) * 8u);
+          mma_commit_pair(empty1 + uint32_t(s) * 8u);
+        }
+        if (*abort_flag)
+          break;
+        mma_commit_pair(tmem_full0 + uint32_t(b) * 8u);
+        mma_commit_pair(tmem_full1 + uint32_t(b) * 8u);
+      }
+      // Fires once every MMA issued above has finished (both CTAs' TMEM quiet).
+      mma_commit_pair(in_cta(drained, 0));
+    }
+  } else if (warp >= 2 + EPI_WARPS) { // RAW converter warps 10..13 of both CTAs
+    const int t = threadIdx.x - THREADS_PLAIN;
+    const uint32_t converted0 = in_cta(converted, 0);
+    int g = 0;
+    for (int u = pair; u < args.units_total && !*abort_flag; u += pairs) {
+      int tile, kb0, kb1;
+      unit(u, tile, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb, ++g) {
+        const int s = g % S;
+        if (!mbar_wait(&raw_full[s], (g / S) & 1)) {
+          atomicExch(args.status, STATUS_TIMEOUT_CONVERT);
+          *abort_flag = 1;
+        }
+        if (*abort_flag)
+          break;
+        float4 *hi = reinterpret_cast<float4 *>(smem + s * PAIR_STAGE);
+        float4 *lo = reinterpret_cast<float4 *>(smem + s * PAIR_STAGE + PAIR_A_BYTES);
+        // Same swizzle in both boxes: the pair is formed position by position.
+#pragma unroll
+        for (int i = 0; i < PAIR_A_BYTES / 16 / 128; ++i) {
+          const float4 v = hi[t + 128 * i];
+          const float4 h = tf32_hi(v);
+          lo[t + 128 * i] = tf32_hi(make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
+          hi[t + 128 * i] = h;
+          if (args.nonfinite && any_inf(h))
+            *args.nonfinite = args.epoch;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // visible to the tensor cores
+        __syncwarp();
+        if (lane == 0)
+          arrive_at(converted0 + uint32_t(s) * 8u);
+      }
+    }
+  } else { // epilogue warps 2..9 of both CTAs: TMEM lanes 32*(warp % 4) .., column half (warp - 2) / 4
+    const int sub = warp % 4, half = (warp - 2) / 4;
+    int j = 0;
+    for (int u = pair; u < args.units_total; u += pairs, ++j) {
+      int tile, kb0, kb1;
+      unit(u, tile, kb0, kb1);
+      const int b = j & 1;
+      bool ready = mbar_try_wait(&tmem_full[b], (j >> 1) & 1);
+      const long long start = clock64(), budget = WAIT_CYCLES + 100000ll * args.k_blocks;
+      while (!ready && !*abort_flag && clock64() - start < budget)
+        ready = mbar_try_wait(&tmem_full[b], (j >> 1) & 1);
+      if (!ready || *abort_flag) {
+        if (!ready && !*abort_flag)
+          atomicExch(args.status, STATUS_TIMEOUT_EPILOGUE);
+        *abort_flag = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int m0, n0, z;
+      locate(tile, m0, n0, z);
+      // Whole tiles go to C; the k-range parts of split tiles to their own 256 x 256
+      // partial tile (row stride 256), all of it written.
+      const bool whole = u < args.full_units;
+      float *const c_base = whole ? args.c + int64_t(z) * args.c_batch
+                                  : args.partials + int64_t(u - args.full_units) * (PAIR_M * PAIR_N);
+      const int64_t ldc = whole ? args.ldc : PAIR_N, m_lim = whole ? args.m : PAIR_M, n_lim = whole ? args.n : PAIR_N;
+      const int64_t row0 = (whole ? int64_t(m0) : 0) + int64_t(rank) * PAIR_HALF + 32 * sub; // this warp's rows
+      const int64_t col0 = whole ? int64_t(n0) : 0;
+      const int64_t left = m_lim - row0;
+      const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
+      float *tile_s = epi_tiles + (warp - 2) * EPI_STAGE_FLOATS;
+      const uint32_t acc = tmem + uint32_t(b) * PAIR_COLUMNS + (uint32_t(32 * sub) << 16);
+      const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
+#pragma unroll 1
+      for (int col = half * (PAIR_N / 2); col < (half + 1) * (PAIR_N / 2); col += 16) {
+        float v[16];
+        tmem_load_16(acc + uint32_t(col), v); // thread = row 32*sub + lane, 16 columns
+        const int64_t first = col0 + col;
+        if (first >= n_lim)
+          break;
+        if (whole && (args.bias || args.activation)) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (first + q < n_lim)
+              v[q] = bias_activate(v[q], args.bias, first + q, args.activation);
+        }
+#pragma unroll
+        for (int q = 0; q < 16; q += 4)
+          *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH16 + q]) =
+              make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+        __syncwarp();
+        if (vec_c && rows_here == 32 && first + 15 < n_lim) {
+          const int r_in = lane % 8, c4 = 4 * (lane / 8);
+          float4 w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            w[i] = *reinterpret_cast<const float4 *>(&tile_s[(8 * i + r_in) * EPI_PITCH16 + c4]);
+          float *cptr = c_base + (row0 + r_in) * ldc + first + c4;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float4 *>(cptr + int64_t(8 * i) * ldc) = w[i];
+        } else {
+          const int64_t column = first + (lane & 15);
+          if (column < n_lim) {
+            float *cptr = c_base + row0 * ldc + column;
+            for (int r = lane >> 4; r < rows_here; r += 2)
+              cptr[r * ldc] = tile_s[r * EPI_PITCH16 + (lane & 15)];
+          }
+        }
+        __syncwarp();
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        arrive_at(tmem_empty0 + uint32_t(b) * 8u);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (*abort_flag) {
+      // Copies requested but never consumed must land before shared memory is
+      // released: CTA 0 waits (bounded) for those phases; CTA 1, whose copies complete
+      // on CTA 0's barriers, waits a fixed ~1 ms for its own.
+      if (leader) {
+        for (int g = *consumed; g < *issued; ++g)
+          (void)mbar_wait(&full[g % S], (g / S) & 1);
+      }
+      const long long start = clock64(); // copies that complete on another CTA's barrier
+      while (clock64() - start < 2000000ll) {
+      }
+    }
+    if (leader)
+      (void)mbar_wait(drained, 0); // bounded: every MMA of the pair has finished
+  }
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * PAIR_COLUMNS)
+                 : "memory");
+  }
+}
+
 // C of every split tile = its partial tiles added in k order: one thread per four
 // columns of a tile row (128-bit loads), 1024 / BN rows per 256-thread block.
-template <int BN> __global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
+// TMR: rows of a tile (128 for the one-SM kernel, 256 for the CTA pair).
+template <int BN, int TMR = TM> __global__ void __launch_bounds__(256) split_fixup(const TileArgs args) {
   constexpr int PER_ROW = BN / 4, ROWS = 256 / PER_ROW;
   const int t = blockIdx.y;                                     // remaining tile
   const int i = blockIdx.x * ROWS + threadIdx.x / PER_ROW;      // row in the tile
   const int j = 4 * (threadIdx.x % PER_ROW);                    // first of four columns
   const int tile = args.full_units + t;
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
-  const int z = tile / per_batch, id = tile % per_batch, group = 8, per_group = group * args.tiles_n;
+  const int z = tile / per_batch, id = tile % per_batch, group = args.group, per_group = group * args.tiles_n;
   const int first_m = (id / per_group) * group;
   const int rows_in_group = min(group, args.tiles_m - first_m);
-  const int64_t row = int64_t(first_m + (id % per_group) % rows_in_group) * TM + i;
+  const int64_t row = int64_t(first_m + (id % per_group) % rows_in_group) * TMR + i;
   const int64_t col = int64_t((id % per_group) / rows_in_group) * BN + j;
   if (row >= args.m || col >= args.n)
     return;
-  const float4 *p = reinterpret_cast<const float4 *>(args.partials + int64_t(t) * args.split * (TM * BN) + i * BN + j);
+  const float4 *p =
+      reinterpret_cast<const float4 *>(args.partials + int64_t(t) * args.split * (TMR * BN) + i * BN + j);
   float4 s4 = p[0];
   for (int q = 1; q < args.split; ++q) {
-    const float4 v = p[int64_t(q) * (TM * BN / 4)];
+    const float4 v = p[int64_t(q) * (TMR * BN / 4)];
     s4 = make_float4(__fadd_rn(s4.x, v.x), __fadd_rn(s4.y, v.y), __fadd_rn(s4.z, v.z), __fadd_rn(s4.w, v.w));
   }
   const float sum[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -959,7 +1314,7 @@ struct UnitPlan {
   int ctas, full_units, split, units, remaining;
   size_t partial_bytes;
 };
-UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks, int bn) {
+UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks, int bn, int tile_rows = TM) {
   UnitPlan p{};
   const int64_t g = std::max(1, sm_count);
   const int64_t r = tiles % g;
@@ -972,7 +1327,7 @@ UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks, int bn) {
   p.full_units = int(tiles - p.remaining);
   p.units = p.full_units + p.remaining * p.split;
   p.ctas = int(std::min<int64_t>(p.units, g));
-  p.partial_bytes = size_t(p.remaining) * p.split * TM * bn * sizeof(float);
+  p.partial_bytes = size_t(p.remaining) * p.split * tile_rows * bn * sizeof(float);
   return p;
 }
 
@@ -990,6 +1345,69 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
     split_fixup<BN><<<dim3(TM / (1024 / BN), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);
     ++L.kernels;
   }
+}
+
+// CTA pairs the device can hold at once with the pair kernel's shared memory (the
+// persistent grid), set up once per device; 0 when the pair kernel cannot run.
+template <bool RAW> int pair_capacity(int device) {
+  static int capacity[64] = {};
+  static bool known[64] = {};
+  if (device < 0 || device >= 64)
+    return 0;
+  if (!known[device]) {
+    known[device] = true;
+    if (cudaFuncSetAttribute(gemm_tf32x3_pair<RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES_PERSISTENT) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(2, 1, 1);
+    config.blockDim = dim3(RAW ? THREADS_RAW : THREADS_PLAIN, 1, 1);
+    config.dynamicSmemBytes = SMEM_BYTES_PERSISTENT;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tf32x3_pair<RAW>, &config) != cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    capacity[device] = clusters;
+  }
+  return capacity[device];
+}
+
+void launch_pair(Launch &L, bool raw, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
+                 float *partials) {
+  t.tiles_total = int(tiles);
+  t.units_total = plan.units;
+  t.full_units = plan.full_units;
+  t.split = plan.split;
+  t.partials = partials;
+  if (raw)
+    gemm_tf32x3_pair<true><<<uint32_t(2 * plan.ctas), THREADS_RAW, SMEM_BYTES_PERSISTENT, L.stream>>>(
+        maps[0], maps[1], maps[2], maps[3], t);
+  else
+    gemm_tf32x3_pair<false><<<uint32_t(2 * plan.ctas), THREADS_PLAIN, SMEM_BYTES_PERSISTENT, L.stream>>>(
+        maps[0], maps[1], maps[2], maps[3], t);
+  if (plan.remaining) {
+    split_fixup<PAIR_N, PAIR_M><<<dim3(PAIR_M / (1024 / PAIR_N), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);
+    ++L.kernels;
+  }
+}
+
+// The CTA-pair kernel serves the wide (BN = 256) forms; PARALYN_GEMM_PAIR=0 selects
+// the one-SM kernel instead. With A stored [m][k] in 16-byte rows the pair reads A
+// raw and converts it in shared memory (PARALYN_GEMM_PAIR_RAW=0: split A first).
+bool env_flag(const char *name) {
+  const char *v = std::getenv(name);
+  return !(v && v[0] == '0');
+}
+bool pair_enabled() {
+  static const bool enabled = env_flag("PARALYN_GEMM_PAIR");
+  return enabled;
+}
+bool pair_raw_enabled() {
+  static const bool enabled = env_flag("PARALYN_GEMM_PAIR_RAW");
+  return enabled;
 }
 
 // The kernel forms: N tile width x (which operand, if any, is split in shared
@@ -1055,10 +1473,18 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // The kernel's D [dm, dn]: C itself, or C^T in the transposed form.
   const int64_t dm = transposed ? n : m, dn = transposed ? m : n;
   const int bn = transposed ? 256 : tile_width(n);
-  const int64_t k_pad = round_up(k, 32), dm_pad = round_up(dm, TM), dn_pad = round_up(dn, bn);
-  const int64_t tiles_m = dm_pad / TM, tiles_n = dn_pad / bn, batch_b = sb ? batch : 1;
-  const Form form = transposed ? Form::transposed : form_of(bn, raw_a && tiles_n <= 2);
+  const int64_t k_pad = round_up(k, 32), dn_pad = round_up(dn, bn), tiles_n = dn_pad / bn;
+  Form form = transposed ? Form::transposed : form_of(bn, raw_a && tiles_n <= 2);
+  // Wide products run on CTA pairs (256 x 256 tiles), reading A raw when its layout
+  // allows (then no split pass runs over A).
+  const bool wide = (form == Form::n256 || form == Form::n256_raw_a) && dm >= PAIR_M && pair_enabled();
+  const bool pair_raw = wide && raw_a && pair_raw_enabled();
+  const int pairs = !wide ? 0 : (pair_raw ? pair_capacity<true>(L.device) : pair_capacity<false>(L.device));
+  if (pairs)
+    form = pair_raw ? Form::n256_raw_a : Form::n256;
   const bool a_split = !transposed && (form == Form::n64 || form == Form::n128 || form == Form::n256);
+  const int64_t m_tile = pairs ? PAIR_M : TM;
+  const int64_t dm_pad = round_up(dm, m_tile), tiles_m = dm_pad / m_tile, batch_b = sb ? batch : 1;
   // Grid limits of the split passes (rows / 32 in grid.y) and 32-bit TMA row
   // coordinates of the split operands; a raw operand is addressed by its own map.
   const int64_t b_rows = transposed ? dm_pad : dn_pad;
@@ -1066,7 +1492,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
       batch_b * b_rows > INT32_MAX || (a_split && (dm_pad / 32 > 65535 || batch * dm_pad > INT32_MAX)) ||
       dm > INT32_MAX || dn > INT32_MAX)
     return false;
-  const UnitPlan plan = plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn);
+  const UnitPlan plan = pairs ? plan_units(tiles_m * tiles_n * batch, pairs, int(k_pad / TK), bn, PAIR_M)
+                              : plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn);
   // Split operands in the workspace: A's pair [batch * m_pad][k_pad] unless A is
   // converted in shared memory; B's pair [batch_b * rows][k_pad], rows = n_pad
   // (or, transposed, n padded to 128: the kernel's M side).
@@ -1108,11 +1535,11 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
         return false;
       maps[1] = maps[0]; // unused
     }
-    if (!make_map(&maps[2], bhi, batch_b * dn_pad, k_pad, uint32_t(bn)) ||
-        !make_map(&maps[3], blo, batch_b * dn_pad, k_pad, uint32_t(bn)))
+    const uint32_t b_box = pairs ? PAIR_HALF : uint32_t(bn); // a CTA of a pair holds half of B's rows
+    if (!make_map(&maps[2], bhi, batch_b * dn_pad, k_pad, b_box) || !make_map(&maps[3], blo, batch_b * dn_pad, k_pad, b_box))
       return false;
   }
-  if (!configure_form(form, L.device))
+  if (!pairs && !configure_form(form, L.device))
     return false;
   // op(A) [m, k] and op(B)^T [n, k]: B^T is B read transposed unless B is stored [n, k].
   // 128-bit split when the operand's rows (or columns) start on 16-byte boundaries.
@@ -1153,12 +1580,32 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   t.transposed = transposed;
   t.nonfinite = flag;
   t.epoch = epoch;
+  if (pairs && pair_raw)
+    t.group = 16; // 16 tile rows of raw A (16 MB at k = 4096) stay in L2 while B's tiles stream
   ++L.kernels;
-  launch_form(form, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
+  if (pairs)
+    launch_pair(L, pair_raw, maps, t, tiles_m * tiles_n * batch, plan, partials);
+  else
+    launch_form(form, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
   return true;
 }
 
 } // namespace
+
+bool encode_map_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                   uint32_t box_inner, uint32_t box_outer, bool swizzle_128b) {
+  const EncodeTiled encode = encoder();
+  if (!encode || row_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return false;
+  const cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
+  const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t element[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, element,
+                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                swizzle_128b ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 // Plans and enqueues the 3xTF32 GEMM; returns false (nothing enqueued) when the
 // shape is outside what this kernel covers or scratch is unavailable.

@@ -861,6 +861,7 @@ PB_EXPORT pr_status pr_add_f32(pr_queue queue, pr_module operators, const pr_add
 namespace pb {
 void launch_layer_norm_gather(Launch &);
 void launch_matmul_bias_activation(Launch &);
+void launch_gather_rows(Launch &);
 
 namespace {
 // Binds operands as raw device ranges of one submitted command (for entries that
@@ -1011,6 +1012,71 @@ PB_EXPORT pr_status pr_b200_layer_norm_gather_f32(pr_queue queue, pr_module oper
       for (const Operand &t : targets)
         d.tensor(t, true);
       *out = submit_command(queue, "b200_layer_norm_gather_f32", launch_layer_norm_gather, Dim3{uint32_t(rows), 1, 1},
+                            Dim3{kLanes, 1, 1}, std::move(d.args), std::move(d.retained));
+    }));
+  });
+}
+
+// A rank's row shard written into every gathered tensor (its own and imported
+// peers'): `local` is a contiguous [rows, columns] tensor; each gathered tensor is
+// contiguous [R_total, columns] and receives rows [row_offset, row_offset + rows)
+// (PR_OUT_OF_BOUNDS past R_total). A gathered tensor may contain `local` exactly at
+// those rows (the rank's own rows of its own gathered tensor) but may not otherwise
+// overlap it or another gathered tensor. No provider entry is involved: the queue
+// and every tensor must belong to one context.
+PB_EXPORT pr_status pr_b200_gather_rows_f32(pr_queue queue, const pr_tensor_desc_v1 *local,
+                                            const pr_tensor_desc_v1 *const *gathered, uint32_t count,
+                                            uint64_t row_offset, pr_event *out) {
+  return guarded("gather_rows_f32", [&] {
+    if (!out)
+      reject(PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    if (!local)
+      reject(PR_INVALID_ARGUMENT, "Missing local tensor");
+    if (count > PR_B200_MAX_GATHER)
+      reject(PR_INVALID_ARGUMENT, "At most 8 gathered tensors");
+    if (count && !gathered)
+      reject(PR_INVALID_ARGUMENT, "Missing gathered tensors");
+    Operand mine{local, operand_extent(local, {"local", 2}, 2), "local", false};
+    const uint64_t rows = mine.dim(0), columns = mine.dim(1);
+    if (columns > kMaxElements || rows > kMaxElements)
+      reject(PR_UNSUPPORTED, "local: dimensions must not exceed INT32_MAX");
+    std::vector<Operand> targets(count);
+    for (uint32_t i = 0; i < count; ++i) {
+      if (!gathered[i])
+        reject(PR_INVALID_ARGUMENT, "Missing gathered tensor");
+      targets[i] = Operand{gathered[i], operand_extent(gathered[i], {"gathered", 2}, 2), "gathered", true};
+      if (gathered[i]->shape[1] != columns)
+        reject(PR_INVALID_ARGUMENT, "gathered: column count differs from local");
+      if (row_offset > gathered[i]->shape[0] || rows > gathered[i]->shape[0] - row_offset)
+        reject(PR_OUT_OF_BOUNDS, "gathered: rows [row_offset, row_offset + rows) exceed the tensor");
+      const uint64_t mirror = gathered[i]->byte_offset + 4 * row_offset * columns;
+      const bool exact = local->buffer == gathered[i]->buffer && local->byte_offset == mirror;
+      if (!exact)
+        separate(targets[i], mine);
+      for (uint32_t j = 0; j < i; ++j) {
+        Operand earlier = targets[j];
+        earlier.output = false;
+        separate(targets[i], earlier);
+      }
+    }
+    const void *context = context_of(queue, HandleKind::queue, "queue");
+    if (context_of(local->buffer, HandleKind::buffer, "local") != context)
+      reject(PR_CONTEXT_MISMATCH, "local: the tensor's buffer belongs to another context");
+    for (const Operand &t : targets)
+      if (context_of(t.desc->buffer, HandleKind::buffer, "gathered") != context)
+        reject(PR_CONTEXT_MISMATCH, "gathered: the tensor's buffer belongs to another context");
+    if (!mine.extent.elements || !count)
+      return;
+    forward(api("gather_rows_f32", [&] {
+      const QueueAccess q = queue_access(queue);
+      DirectArguments d{q, {}, {}};
+      d.tensor(mine, false);
+      for (uint64_t v : {columns, rows, row_offset & 0xffffffffu, row_offset >> 32, uint64_t(count)})
+        d.bits(uint32_t(v));
+      for (const Operand &t : targets)
+        d.tensor(t, true);
+      *out = submit_command(queue, "b200_gather_rows_f32", launch_gather_rows, Dim3{uint32_t(rows), 1, 1},
                             Dim3{kLanes, 1, 1}, std::move(d.args), std::move(d.retained));
     }));
   });

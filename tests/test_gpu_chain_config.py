@@ -6,9 +6,11 @@ persistent 3xTF32 tcgen05 kernel, whose last round of tiles runs as k-ranges add
 the split fixup), exactly as bench.py's chain workload runs it: ChainShard with
 device-generated inputs, one rank.
 
-Sampled rows (every 128-row tile boundary of the tile rows whose tiles are cut into
-k-ranges, the first and last rows of the matrix and of the first tile, and seeded
-random rows, 64 in all) are read back with their X rows and the whole W, and checked:
+Sampled rows (the first and last row of every tile row whose tiles are cut into
+k-ranges, for each tile geometry the GEMM may use: 128-row tiles on one SM or 256-row
+tiles on a CTA pair; the first and last rows of the matrix and of the first tiles;
+seeded random rows; at least 64 in all) are read back with their X rows and the whole
+W, and checked:
   * Z within the FP32 GEMM contract |Z - Z_exact| <= 2*k*2^-24*sum|x||w| of the
     float64 product (reference tests/native/tensor_tests.cpp:62-85,
     docs/tensors-matmul.md:75-77);
@@ -31,31 +33,35 @@ from paralyn_b200 import shard
 pytestmark = pytest.mark.gpu
 
 ROWS, K, N = 65536, 4096, 4096
-TM, BN, GROUP = 128, 256, 8
+BN = 256
+# The tile geometries the GEMM may use here: (tile rows, raster group, concurrent
+# units): the one-SM kernel (128-row tiles, one per SM) and the CTA-pair kernel
+# (256-row tiles, one per pair of SMs, raster group 16 when A is read raw).
+GEOMETRIES = lambda sm_count: ((128, 8, sm_count), (256, 16, sm_count // 2), (256, 8, sm_count // 2))
 
 
-def split_tile_rows(sm_count):
-    """Row blocks (multiples of 128) of the tiles the persistent kernel cuts into
-    k-ranges: tiles = R*G + r with 2r <= G puts the last r tiles (in the kernel's
-    grouped raster order) into k-ranges."""
-    tiles_m, tiles_n = ROWS // TM, N // BN
+def split_tile_rows(tm, group, units):
+    """First rows of the tiles the persistent kernel cuts into k-ranges: tiles = R*G + r
+    with 2r <= G puts the last r tiles (in the grouped raster order) into k-ranges."""
+    tiles_m, tiles_n = ROWS // tm, N // BN
     tiles = tiles_m * tiles_n
-    r = tiles % sm_count
-    if r == 0 or 2 * r > sm_count:
+    r = tiles % units
+    if r == 0 or 2 * r > units:
         return set()
     out = set()
-    per_group = GROUP * tiles_n
+    per_group = group * tiles_n
     for tile in range(tiles - r, tiles):
-        first_m = (tile // per_group) * GROUP
-        rows_in_group = min(GROUP, tiles_m - first_m)
-        out.add(first_m + (tile % per_group) % rows_in_group)
+        first_m = (tile // per_group) * group
+        rows_in_group = min(group, tiles_m - first_m)
+        out.add((first_m + (tile % per_group) % rows_in_group) * tm)
     return out
 
 
 def sampled_rows(sm_count):
-    rows = {0, 1, TM - 1, TM, ROWS - 1}
-    for tm in split_tile_rows(sm_count):
-        rows |= {tm * TM, tm * TM + TM - 1}
+    rows = {0, 1, 127, 128, 255, 256, ROWS - 1}
+    for tm, group, units in GEOMETRIES(sm_count):
+        for first in split_tile_rows(tm, group, units):
+            rows |= {first, first + tm - 1}
     rng = np.random.default_rng(2026)
     while len(rows) < 64:
         rows.add(int(rng.integers(0, ROWS)))
@@ -94,7 +100,7 @@ def test_chain_configuration_auto_mode(context):
         ln.close()
         assert variant is not None and "tf32x3" in variant, variant
         rows = sampled_rows(sm_count)
-        assert split_tile_rows(sm_count), "the configuration has a split last round on this GPU"
+        assert any(split_tile_rows(*geometry) for geometry in GEOMETRIES(sm_count))
         w = np.frombuffer(chain.w.read(), np.float32)
         x = np.stack([np.frombuffer(chain.x.read(4 * K, offset=4 * r * K), np.float32) for r in rows])
         z = np.stack([np.frombuffer(chain.z.read(4 * N, offset=4 * r * N), np.float32) for r in rows])

@@ -1,11 +1,14 @@
-"""Row-sharded LayerNorm with the output gathered over NVLink (pr_b200_layer_norm_gather_f32).
+"""Row-sharded results gathered over NVLink.
 
-Each rank normalizes its rows [r0, r1) and the same kernel writes every output row
-into each rank's gathered [rows, columns] tensor (its own and the peers', mapped
-with pr_b200_buffer_export / pr_b200_buffer_import). After all ranks' commands have
-completed, every gathered tensor must equal the unsharded LayerNorm of the oracle,
-bit for bit. One-GPU cases gather into local buffers; the two-GPU case spawns one
-process per GPU (needs a box with at least two B200s, skipped otherwise).
+pr_b200_layer_norm_gather_f32: each rank normalizes its rows [r0, r1) and the same
+kernel writes every output row into each rank's gathered [rows, columns] tensor (its
+own and the peers', mapped with pr_b200_buffer_export / pr_b200_buffer_import).
+pr_b200_gather_rows_f32: the same gathered output for any row shard, here a GEMM
+shard's C (reference-order matmul, so the gathered product is checkable bit for bit).
+After all ranks' commands have completed, every gathered tensor must equal the
+unsharded oracle result, bit for bit. One-GPU cases gather into local buffers; the
+two-GPU case spawns one process per GPU (needs a box with at least two B200s,
+skipped otherwise).
 """
 import importlib
 import multiprocessing as mp
@@ -69,13 +72,58 @@ def test_gather_into_local_buffers(context, rows, cols):
         buf.close()
 
 
+@pytest.mark.parametrize("rows,cols,k", [(96, 4096, 64), (50, 2001, 33), (7, 12, 5)])
+def test_gemm_shards_gathered_into_local_buffers(context, rows, cols, k):
+    a = synthetic.uniform(41, 0, rows * k).reshape(rows, k)
+    b = synthetic.uniform(42, 0, k * cols).reshape(k, cols)
+    p.set_matmul_mode(context, p.MatmulMode.REFERENCE)
+    want = oracle.matmul(a.ravel(), b.ravel(), rows, cols, k)
+    res = T.operators_of(context)
+    gathered = [context.buffer(rows * cols * 4), context.buffer((rows + 2) * cols * 4)]
+    try:
+        for world in (1, 2, 3):
+            for buf in gathered:
+                buf.write(np.full(buf.size // 4, np.nan, np.float32))
+            with p.tensor(b.ravel(), shape=(k, cols), context=context) as tb:
+                for rank in range(world):
+                    r0, r1 = shard.row_range(rows, world, rank)
+                    with p.tensor(a[r0:r1].ravel(), shape=(r1 - r0, k), context=context) as ta, \
+                            p.matmul(ta, tb) as c:
+                        event = p.b200.gather_rows_into(
+                            res.queue, c.descriptor(),
+                            [T.TensorDescriptor(gathered[0], (rows, cols)),
+                             T.TensorDescriptor(gathered[1], (rows, cols), 2 * cols * 4)], row_offset=r0)
+                        event.wait()
+                        assert p.b200.last_variant(context, "b200_gather_rows_f32") in ("vec4", "scalar")
+                        event.close()
+            first = np.frombuffer(gathered[0].read(), np.float32).reshape(rows, cols)
+            second = np.frombuffer(gathered[1].read(), np.float32)[2 * cols:].reshape(rows, cols)
+            assert first.tobytes() == want.tobytes() and second.tobytes() == want.tobytes()
+        with pytest.raises(p.Error) as error:  # rows past the end of the gathered tensor
+            with p.tensor(a.ravel(), shape=(rows, k), context=context) as ta, \
+                    p.tensor(b.ravel(), shape=(k, cols), context=context) as tb, p.matmul(ta, tb) as c:
+                p.b200.gather_rows_into(res.queue, c.descriptor(), [T.TensorDescriptor(gathered[0], (rows, cols))],
+                                        row_offset=1)
+        assert error.value.code == p.Status.OUT_OF_BOUNDS
+        with pytest.raises(p.Error) as error:  # two gathered tensors over the same bytes
+            with p.tensor(a.ravel(), shape=(rows, k), context=context) as ta, \
+                    p.tensor(b.ravel(), shape=(k, cols), context=context) as tb, p.matmul(ta, tb) as c:
+                target = T.TensorDescriptor(gathered[0], (rows, cols))
+                p.b200.gather_rows_into(res.queue, c.descriptor(), [target, target], row_offset=0)
+        assert error.value.code == p.Status.INVALID_ARGUMENT
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)
+        for buf in gathered:
+            buf.close()
+
+
 ROWS, COLS = 257, 4096
 
 
 def _rank(rank, world, handles, barrier, results):
     import numpy as np
     import paralyn_b200 as p
-    from paralyn_b200 import shard
+    from paralyn_b200 import shard, synthetic
     T = importlib.import_module("paralyn_b200.tensor")
     try:
         ctx = p.Context(f"cuda:{rank}")
@@ -99,7 +147,22 @@ def _rank(rank, world, handles, barrier, results):
         barrier.wait(timeout=120)  # every rank's rows have landed everywhere
         gathered = np.frombuffer(mine.read(), np.float32).reshape(ROWS, COLS)
         want = oracle.layer_norm(x, g, b, np.float32(1e-5))
-        results.put((rank, gathered.tobytes() == want.tobytes()))
+        ok_ln = gathered.tobytes() == want.tobytes()
+        barrier.wait(timeout=120)  # everyone has read the LayerNorm before it is overwritten
+        # A GEMM shard (reference order) gathered with pr_b200_gather_rows_f32.
+        k = 64
+        am = synthetic.uniform(43, 0, ROWS * k).reshape(ROWS, k)
+        bm = synthetic.uniform(44, 0, k * COLS).reshape(k, COLS)
+        p.set_matmul_mode(ctx, p.MatmulMode.REFERENCE)
+        with p.tensor(am[r0:r1].ravel(), shape=(r1 - r0, k), context=ctx) as ta, \
+                p.tensor(bm.ravel(), shape=(k, COLS), context=ctx) as tbm, p.matmul(ta, tbm) as c:
+            gevent = p.b200.gather_rows_into(res.queue, c.descriptor(), targets, row_offset=r0)
+            gevent.wait()
+            gevent.close()
+        barrier.wait(timeout=120)
+        gathered = np.frombuffer(mine.read(), np.float32).reshape(ROWS, COLS)
+        ok_mm = gathered.tobytes() == oracle.matmul(am.ravel(), bm.ravel(), ROWS, COLS, k).tobytes()
+        results.put((rank, ok_ln and ok_mm))
         barrier.wait(timeout=120)  # nobody unmaps while a peer may still read
         for obj in [event, out, tx, tg, tb] + peers:
             obj.close()

@@ -387,3 +387,43 @@ def test_auto_mode_batched_propagates_infinities(context):
             assert np.all(np.abs(c[z] - exact) <= oracle.matmul_tolerance(magnitude, k))
         else:
             same_specials_and_contract(c[z], a[z].ravel(), b[z].ravel(), m, n, k)
+
+
+# The TMA-fed SIMT kernel (gemm_simt_tma, FFMA mode): operands with 16-byte aligned
+# bases and row strides (k % 4 == 0 for A stored [m][k], m % 4 == 0 for A stored
+# [k][m], n % 4 == 0 for B) and B not transposed. Its k loop runs in 32-deep slices
+# with zero-filled tails, every output adding its products in increasing k.
+TMA_SHAPES = {False: ((1, 4, 4), (17, 132, 36), (129, 260, 100), (300, 128, 64), (257, 300, 1000), (128, 128, 32)),
+              True: ((4, 4, 1), (20, 132, 33), (132, 260, 100), (300, 128, 17), (256, 300, 1000), (128, 128, 32))}
+
+
+@pytest.mark.parametrize("ta", (False, True))
+def test_aligned_operands_reference_order(context, ta):
+    # The aligned shapes the TMA-fed kernel takes in FFMA mode, in the reference order.
+    p.set_matmul_mode(context, p.MatmulMode.REFERENCE)
+    try:
+        for i, (m, n, k) in enumerate(TMA_SHAPES[ta]):
+            a = synthetic.uniform(9600 + i, 0, m * k).reshape(k, m).T.copy() if ta else \
+                synthetic.uniform(9600 + i, 0, m * k).reshape(m, k)
+            b = synthetic.uniform(9700 + i, 0, k * n).reshape(k, n)
+            c = aligned_matmul(context, a, b, m, n, k, ta)
+            assert p.b200.last_variant(context, "paralyn_matmul_f32") == "simt_reference_order", (m, n, k)
+            want = oracle.matmul(np.ascontiguousarray(a.T if ta else a).ravel(), b.ravel(), m, n, k, ta, False)
+            assert c.tobytes() == want.tobytes(), (m, n, k, ta)
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+@pytest.mark.parametrize("ta", (False, True))
+def test_tma_fed_simt_kernel_ffma_contract(context, ta):
+    p.set_matmul_mode(context, p.MatmulMode.FFMA)
+    try:
+        for i, (m, n, k) in enumerate(TMA_SHAPES[ta]):
+            a = synthetic.uniform(9800 + i, 0, m * k).reshape(m, k)
+            b = synthetic.uniform(9900 + i, 0, k * n).reshape(k, n)
+            c = aligned_matmul(context, a, b, m, n, k, ta)
+            assert p.b200.last_variant(context, "paralyn_matmul_f32") == "simt_tma_ffma", (m, n, k)
+            exact, magnitude = oracle.matmul_exact(a.ravel(), b.ravel(), m, n, k)
+            assert np.all(np.abs(c.astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)

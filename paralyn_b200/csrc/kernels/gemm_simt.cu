@@ -47,6 +47,13 @@ template <int MODE> __device__ __forceinline__ float mac(float acc, float a, flo
     return __fmaf_rn(a, b, acc);
 }
 
+// Two accumulators at once: the sm_100 paired FP32 FMA (each component rounded as a
+// scalar FMA) halves the issue slots the multiply-adds take. The reference order has
+// no paired form: a paired multiply followed by a paired add, even written as PTX with
+// explicit rounding, came out as fused multiply-adds (results one ulp off the
+// reference's), so that order stays on scalar `__fmul_rn`/`__fadd_rn`.
+__device__ __forceinline__ float2 ffma2(float2 acc, float2 a, float2 b) { return __ffma2_rn(a, b, acc); }
+
 // Loads this thread's 4 values of the A slice [m0, m0+128) x [k0, k0+8).
 //  !TA: A[m][k] at a[m*lda + k]; thread t reads row t/2, k (t%2)*4 .. +3
 //   TA: A[m][k] at a[k*lda + m]; thread t reads k t/32, m (t%32)*4 .. +3
@@ -253,6 +260,7 @@ template <int MODE, bool TA>
 __global__ void __launch_bounds__(THREADS, 2)
     gemm_simt_tma(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, const GemmArgs g,
                   int *status) {
+  static_assert(MODE == matmul_ffma, "the TMA-fed kernel accumulates with paired FMAs");
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned (the 128-byte swizzle repeats every 1024 bytes); an offset from
   // the shared array keeps the accesses in the shared state space.
@@ -296,12 +304,16 @@ __global__ void __launch_bounds__(THREADS, 2)
     for (; issued < min(TSTAGES, slices); ++issued)
       issue(issued);
 
-  float acc[8][8];
+  // acc[i][p]: row i, columns (2p, 2p + 1) of the thread's eight (tx*4 + 0..3,
+  // 64 + tx*4 + 0..3), updated with paired FP32 operations (two lanes' worth of FMA
+  // per instruction, each component rounded as a scalar FMA), which halves the
+  // issue slots the multiply-adds take.
+  float2 acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      acc[i][j] = 0.0f;
+    for (int p = 0; p < 4; ++p)
+      acc[i][p] = make_float2(0.0f, 0.0f);
 
   int done = 0; // slices this thread consumed
   for (int slice = 0; slice < slices; ++slice) {
@@ -349,12 +361,15 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int kk = kq * 2 + q;
         const float4 b0 = *reinterpret_cast<const float4 *>(Bs + kk * BN + tx * 4);
         const float4 b1 = *reinterpret_cast<const float4 *>(Bs + kk * BN + 64 + tx * 4);
-        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                             make_float2(b1.z, b1.w)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i) {
+          const float2 a = make_float2(a4[i][q], a4[i][q]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            acc[i][j] = mac<MODE>(acc[i][j], a4[i][q], b[j]);
+          for (int p = 0; p < 4; ++p)
+            acc[i][p] = ffma2(acc[i][p], a, b[p]);
+        }
       }
     }
     __syncwarp();
@@ -380,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int64_t n = n0 + h * 64 + tx * 4;
-      float v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
+      float v[4] = {acc[i][2 * h].x, acc[i][2 * h].y, acc[i][2 * h + 1].x, acc[i][2 * h + 1].y};
       if (g.bias || g.activation) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -587,8 +602,10 @@ void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
   }
   L.kernels = 1;
   if (mode == matmul_reference) {
-    // The register-staged kernel: in the reference order (a separate multiply and add
-    // per step) it measured 29.8 TFLOP/s at 4096^3 against 21.7 for the TMA-fed form.
+    // The register-staged kernel: the reference order (a rounded multiply, then a
+    // rounded add, per step) takes two FP32 operations per product, so its ceiling is
+    // half the FFMA peak; it measured 29.8 TFLOP/s at 4096^3 (0.80 of that ceiling)
+    // against 21.7 for the TMA-fed kernel in this order.
     dispatch<matmul_reference>(g, ta, tb, L.stream);
     L.variant = "simt_reference_order";
   } else {

@@ -1395,8 +1395,9 @@ void launch_pair(Launch &L, bool raw, const CUtensorMap (&maps)[4], TileArgs t, 
 }
 
 // The CTA-pair kernel serves the wide (BN = 256) forms; PARALYN_GEMM_PAIR=0 selects
-// the one-SM kernel instead. With A stored [m][k] in 16-byte rows the pair reads A
-// raw and converts it in shared memory (PARALYN_GEMM_PAIR_RAW=0: split A first).
+// the one-SM kernel instead. Where the one-SM kernel would convert A in shared memory
+// (A stored [m][k] in 16-byte rows, at most two column tiles) the pair does too
+// (PARALYN_GEMM_PAIR_RAW=0: split A first).
 bool env_flag(const char *name) {
   const char *v = std::getenv(name);
   return !(v && v[0] == '0');
@@ -1408,6 +1409,19 @@ bool pair_enabled() {
 bool pair_raw_enabled() {
   static const bool enabled = env_flag("PARALYN_GEMM_PAIR_RAW");
   return enabled;
+}
+// Tile rows per raster group of the pair kernel: the A rows of one group (256 rows
+// each) are re-read by every column tile while B's tiles stream past them, so they
+// should stay in L2 beside the B tiles in use. Two tile rows (16 MB of split A at
+// k = 4096) measured best on the 65536 x 4096 x 4096 chain (1, 2, 3, 4, 8 and 16
+// tried); PARALYN_GEMM_RASTER_GROUP (1..64) overrides the default.
+int pair_group(bool raw) {
+  static const int forced = [] {
+    const char *v = std::getenv("PARALYN_GEMM_RASTER_GROUP");
+    const int g = v ? std::atoi(v) : 0;
+    return g >= 1 && g <= 64 ? g : 0;
+  }();
+  return forced ? forced : (raw ? 8 : 2);
 }
 
 // The kernel forms: N tile width x (which operand, if any, is split in shared
@@ -1478,7 +1492,9 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // Wide products run on CTA pairs (256 x 256 tiles), reading A raw when its layout
   // allows (then no split pass runs over A).
   const bool wide = (form == Form::n256 || form == Form::n256_raw_a) && dm >= PAIR_M && pair_enabled();
-  const bool pair_raw = wide && raw_a && pair_raw_enabled();
+  // Converting A in shared memory repeats its TF32 conversions once per column tile,
+  // so (as for the one-SM kernel) it pays only while few column tiles re-read A.
+  const bool pair_raw = wide && form == Form::n256_raw_a && pair_raw_enabled();
   const int pairs = !wide ? 0 : (pair_raw ? pair_capacity<true>(L.device) : pair_capacity<false>(L.device));
   if (pairs)
     form = pair_raw ? Form::n256_raw_a : Form::n256;
@@ -1580,8 +1596,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   t.transposed = transposed;
   t.nonfinite = flag;
   t.epoch = epoch;
-  if (pairs && pair_raw)
-    t.group = 16; // 16 tile rows of raw A (16 MB at k = 4096) stay in L2 while B's tiles stream
+  if (pairs)
+    t.group = pair_group(pair_raw);
   ++L.kernels;
   if (pairs)
     launch_pair(L, pair_raw, maps, t, tiles_m * tiles_n * batch, plan, partials);

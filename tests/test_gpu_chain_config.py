@@ -36,8 +36,8 @@ ROWS, K, N = 65536, 4096, 4096
 BN = 256
 # The tile geometries the GEMM may use here: (tile rows, raster group, concurrent
 # units): the one-SM kernel (128-row tiles, one per SM) and the CTA-pair kernel
-# (256-row tiles, one per pair of SMs, raster group 16 when A is read raw).
-GEOMETRIES = lambda sm_count: ((128, 8, sm_count), (256, 16, sm_count // 2), (256, 8, sm_count // 2))
+# (256-row tiles, one per pair of SMs, with any of its raster group sizes).
+GEOMETRIES = lambda sm_count: ((128, 8, sm_count),) + tuple((256, g, sm_count // 2) for g in (1, 2, 4, 8, 16))
 
 
 def split_tile_rows(tm, group, units):

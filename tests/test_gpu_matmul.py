@@ -399,7 +399,9 @@ TMA_SHAPES = {False: ((1, 4, 4), (17, 132, 36), (129, 260, 100), (300, 128, 64),
 
 @pytest.mark.parametrize("ta", (False, True))
 def test_aligned_operands_reference_order(context, ta):
-    # The aligned shapes the TMA-fed kernel takes in FFMA mode, in the reference order.
+    # The aligned shapes the TMA-fed kernel takes in FFMA mode, in the reference order
+    # (the register-staged kernel): a rounded product, then a rounded sum, per k, bit
+    # for bit as the oracle's loop.
     p.set_matmul_mode(context, p.MatmulMode.REFERENCE)
     try:
         for i, (m, n, k) in enumerate(TMA_SHAPES[ta]):

@@ -57,6 +57,9 @@ def parse():
                     help="chain: skip the other benchmark configurations measured beside the headline")
     ap.add_argument("--matmul-mode", default="auto", choices=("auto", "reference", "ffma", "tf32x3"),
                     help="summation mode of the GEMM workloads (default auto: the 3xTF32 tensor-core kernel)")
+    ap.add_argument("--split-w-per-step", action="store_true",
+                    help="chain: split W in every step (pr_matmul_f32) instead of preparing it once "
+                         "(pr_b200_matmul_prepare_f32) before the timed steps")
     ap.add_argument("--gather", action="store_true",
                     help="chain: also gather Y on every GPU (LayerNorm writes its rows to all ranks over NVLink); "
                          "gemm: gather C on every GPU after the GEMM (peer-store kernel)")
@@ -239,7 +242,7 @@ def describe(name, world, rank, gather=False):
 class Workload:
     """Holds device inputs/outputs for one rank and runs steps through the public API."""
 
-    def __init__(self, name, ctx, group, gather=False):
+    def __init__(self, name, ctx, group, gather=False, prepare_w=True):
         import numpy as np
         import importlib
         import paralyn_b200 as p
@@ -254,6 +257,8 @@ class Workload:
             self.rows, self.k, self.n = 65536, 4096, 4096
             self.chain = shard.ChainShard(ctx, self.rows, self.k, self.n, world, rank, seed=4, w_std=1.0 / 64.0)
             self.chain.fill_synthetic()
+            if prepare_w:  # W is the same in every step: its TF32 pair is made once
+                self.chain.prepare_weights()
             self.gather = None
             if gather:
                 self.gather = shard.GatheredOutput(ctx, self.rows, self.n, group.exchange, rank)
@@ -581,7 +586,7 @@ def run_ours(args, group):
     ctx = p.Context(f"cuda:{group.local_rank}")
     p.set_matmul_mode(ctx, {"auto": p.MatmulMode.AUTO, "reference": p.MatmulMode.REFERENCE,
                             "ffma": p.MatmulMode.FFMA, "tf32x3": p.MatmulMode.TF32X3}[args.matmul_mode])
-    w = Workload(args.workload, ctx, group, gather=args.gather)
+    w = Workload(args.workload, ctx, group, gather=args.gather, prepare_w=not args.split_w_per_step)
     if args.matmul_mode != "auto":
         w.config["matmul_mode"] = args.matmul_mode
     t = time_steps(w, ctx, group, steps_for(args, args.workload, w, world), args.warmup)
@@ -600,6 +605,10 @@ def run_ours(args, group):
             "data": "synthetic (seeded SplitMix64 stream generated on device)", "config": w.config, "e2e": e2e,
             "gpu_launches": t["gpu_launches"], "roofline": roofline, "clocks": t["clocks"],
             "dominant_kernel_variant": t["variant"], "headline_metric": METRIC}
+    if args.workload == "chain":
+        line["w_operand"] = ("split in every step (pr_matmul_f32)" if args.split_w_per_step else
+                             "prepared once before the timed steps (pr_b200_matmul_prepare_f32); every step "
+                             "splits X, multiplies (pr_b200_matmul_prepared_f32) and normalizes")
     if args.workload == "chain" and not args.no_configs:
         line["configs"] = side_configs(args, ctx, group)
     if group.rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -608,7 +617,7 @@ def run_ours(args, group):
     return line
 
 
-DOMINANT_ENTRY = {"chain": "paralyn_matmul_f32", "gemm": "paralyn_matmul_f32",
+DOMINANT_ENTRY = {"chain": ("b200_matmul_prepared_f32", "paralyn_matmul_f32"), "gemm": "paralyn_matmul_f32",
                   "layernorm": "paralyn_layer_norm_f32", "affine": "array_affine_scalar", "add": "array_add",
                   "softmax": "paralyn_softmax_rows_f32", "reduce": "paralyn_reduce_rows_f32",
                   "attention": "paralyn_batched_matmul_f32", "block": "b200_matmul_bias_activation_f32"}
@@ -617,7 +626,12 @@ DOMINANT_ENTRY = {"chain": "paralyn_matmul_f32", "gemm": "paralyn_matmul_f32",
 def last_variant(ctx, workload):
     """Implementation the library chose for the dominant entry (from the evidence log)."""
     from paralyn_b200 import b200
-    return b200.last_variant(ctx, DOMINANT_ENTRY[workload])
+    entries = DOMINANT_ENTRY[workload]
+    for entry in (entries,) if isinstance(entries, str) else entries:
+        variant = b200.last_variant(ctx, entry)
+        if variant is not None:
+            return variant
+    return None
 
 
 def end_to_end(w, ctx, group, steps):

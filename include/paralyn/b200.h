@@ -116,6 +116,39 @@ pr_status pr_b200_matmul_bias_activation_f32(pr_queue queue, pr_module operators
                                              const pr_tensor_desc_v1 *bias, uint32_t activation,
                                              pr_event *event);
 
+/* Prepared right-hand operands (no counterpart in the reference, whose
+ * pr_matmul_f32, runtime/tensor.cpp:755-798, reads B as given on every call). A
+ * product C = op(A) B whose B is reused across many calls (a weight matrix) can give
+ * B once to pr_b200_matmul_prepare_f32, which writes B's prepared form (the TF32 pair
+ * the tensor-core kernels read, plus B itself as [k][n]) into a caller-owned tensor,
+ * and then call pr_b200_matmul_prepared_f32 instead of pr_matmul_f32: the call then
+ * skips the per-call split pass over B.
+ *
+ * pr_b200_matmul_prepared_bytes(k, n): the prepared form's size in bytes (a multiple
+ * of 4), 0 when k or n is 0 or above INT32_MAX.
+ *
+ * pr_b200_matmul_prepare_f32: b is a contiguous [k, n] tensor ([n, k] with
+ * transpose_b = 1); `prepared` is a contiguous 1-D tensor of exactly
+ * prepared_bytes(k, n) / 4 elements whose byte offset is a multiple of 256, in an
+ * allocation other than b's (PR_INVALID_ARGUMENT otherwise; PR_UNSUPPORTED for
+ * non-contiguous views, as pr_matmul_f32). It enqueues one command that writes the
+ * prepared form; later changes to b do not reach it.
+ *
+ * pr_b200_matmul_prepared_f32: pr_matmul_f32's record, validation order and statuses,
+ * except that op->b is the prepared tensor (prepared for op->k and op->n) and
+ * op->transpose_b must be 0. The result equals pr_matmul_f32 with the B the tensor was
+ * prepared from, bit for bit, in every matmul mode (REFERENCE and FFMA read the [k][n]
+ * copy; AUTO propagates infinities of B as pr_matmul_f32 does). A tensor prepared for
+ * another (k, n), or not prepared at all, makes the command fail with
+ * PR_EXECUTION_FAILED when it runs (C is then undefined). The prepared tensor may be
+ * read by any number of products at once; writing into it while products that read
+ * it are queued is ordered like any other buffer access on the queue. */
+uint64_t pr_b200_matmul_prepared_bytes(uint64_t k, uint64_t n);
+pr_status pr_b200_matmul_prepare_f32(pr_queue queue, pr_module operators, const pr_tensor_desc_v1 *b,
+                                     uint32_t transpose_b, const pr_tensor_desc_v1 *prepared, pr_event *event);
+pr_status pr_b200_matmul_prepared_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
+                                      pr_event *event);
+
 /* Failure-path probe (no counterpart in the reference). Enqueues a one-thread
  * kernel that waits on a shared-memory barrier nothing completes and gives up after
  * `cycles` SM clock cycles (1 .. 4e9), exactly as the library's TMA and tensor-core

@@ -31,6 +31,8 @@ pr_b200_host_unregister ptr
 pr_b200_marker h *h
 pr_b200_selftest_bounded_wait h u64 *h
 pr_b200_matmul_bias_activation_f32 h h ptr ptr u32 *h
+pr_b200_matmul_prepare_f32 h h ptr u32 ptr *h
+pr_b200_matmul_prepared_f32 h h ptr *h
 pr_b200_event_elapsed h h *f64
 pr_b200_fill_synthetic_f32 h *TensorDescRecord u64 u64 u32 f32 f32 *h
 """
@@ -41,6 +43,8 @@ def _b200(lib):
     lib = _api(lib)
     if not lib.declares("pr_b200_marker"):
         lib.declare(_B200_CALLS)
+        sizing = lib.api.pr_b200_matmul_prepared_bytes  # returns a size, not a status
+        sizing.restype, sizing.argtypes = _c.c_uint64, [_c.c_uint64, _c.c_uint64]
     return lib
 
 
@@ -200,6 +204,61 @@ def matmul_bias_activation_into(queue, operators, a, b, c, bias, *, m, n, k, tra
         queue.handle, operators.handle, _c.byref(record),
         _c.byref(bias_native) if bias_native is not None else None, int(Activation(activation)), _c.byref(handle)))
     return Event._adopt(lib, handle.value) if handle.value else None
+
+
+def matmul_prepared_bytes(lib, k, n):
+    """Bytes of B's prepared form for a [k, n] B (0: k or n is 0 or above INT32_MAX)."""
+    return int(_b200(lib).api.pr_b200_matmul_prepared_bytes(int(k), int(n)))
+
+
+def matmul_prepare_into(queue, operators, b, prepared, *, transpose_b=False):
+    """Enqueue B ([k, n], or [n, k] with transpose_b) into its prepared form in the
+    1-D descriptor `prepared`; returns the Event."""
+    lib = _b200(queue._lib)
+    source, target = b._native(), prepared._native()
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_matmul_prepare_f32(queue.handle, operators.handle, _c.byref(source),
+                                                 int(bool(transpose_b)), _c.byref(target), _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
+
+
+def matmul_prepared_into(queue, operators, a, prepared, c, *, m, n, k, transpose_a=False):
+    """C = op(A) B from B's prepared form (equal to matmul_into with that B, bit for
+    bit in every matmul mode); returns the Event or None."""
+    from .tensor import MatmulRecord, TENSOR_VERSION_1
+    lib = _b200(queue._lib)
+    descs = [x._native() for x in (a, prepared, c)]
+    record = MatmulRecord(_c.sizeof(MatmulRecord), TENSOR_VERSION_1, m, n, k, int(bool(transpose_a)), 0,
+                          *(_pointer(d) for d in descs))
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_matmul_prepared_f32(queue.handle, operators.handle, _c.byref(record),
+                                                  _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
+
+
+class PreparedMatrix:
+    """A right-hand matmul operand B prepared once for many products, in a buffer of
+    its own (see pr_b200_matmul_prepare_f32). `descriptor` is what
+    matmul_prepared_into takes; later changes to B do not reach it."""
+
+    def __init__(self, queue, operators, context, b, *, k, n, transpose_b=False):
+        from .tensor import TensorDescriptor
+        self.k, self.n = int(k), int(n)
+        size = matmul_prepared_bytes(queue._lib, self.k, self.n)
+        if not size:
+            raise ValueError("a prepared operand needs 1 <= k, n <= INT32_MAX")
+        self.buffer = context.buffer(size)
+        self.descriptor = TensorDescriptor(self.buffer, (size // 4,))
+        try:
+            event = matmul_prepare_into(queue, operators, b, self.descriptor, transpose_b=transpose_b)
+            event.wait()
+            event.close()
+        except BaseException:
+            self.buffer.close()
+            raise
+
+    def close(self):
+        self.buffer.close()
 
 
 def selftest_bounded_wait(queue, cycles):

@@ -14,6 +14,7 @@
 // in L2.
 #include "../runtime/builtin.hpp"
 #include "activation.cuh"
+#include "prepared.hpp"
 #include "tma.cuh"
 #include <algorithm>
 
@@ -542,19 +543,24 @@ bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
 
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n,
                         int64_t k, int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb,
-                        const float *bias, uint32_t activation, NonFiniteFlag *watch);
+                        const float *bias, uint32_t activation, NonFiniteFlag *watch, const PreparedB *prep);
+void launch_prepared_check(Launch &L, const PreparedB &prep);
 bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
                            int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
                            int64_t ldc, int64_t sc, NonFiniteFlag *watch);
 
 namespace {
 // C = op(A) op(B) over the grid-bounded region, optionally with the bias/activation
-// epilogue fused (bias: view of n values or absent; activation 0..2).
-void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
+// epilogue fused (bias: view of n values or absent; activation 0..2). With `prepared`,
+// L.args[1] is B's prepared form (prepared.hpp) and transpose_b is 0: the tensor-core
+// path reads its TF32 pair, the SIMT kernels its [k][n] copy.
+void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation, bool prepared = false) {
   const uint32_t m = L.args[3].u32(), n = L.args[4].u32(), k = L.args[5].u32();
   const uint32_t ta = L.args[6].u32(), tb = L.args[7].u32();
   if (ta > 1 || tb > 1)
     throw Failure(PR_INVALID_ARGUMENT, "Transpose flags must be 0 or 1");
+  if (prepared && (tb || !prepared::bytes(k, n)))
+    throw Failure(PR_INVALID_ARGUMENT, "A prepared operand needs transpose_b = 0 and 1 <= k, n <= INT32_MAX");
   if (activation > 2)
     throw Failure(PR_INVALID_ARGUMENT, "Unknown activation");
   const int64_t me = std::min<int64_t>(m, int64_t(L.grid.y) * 16);
@@ -565,21 +571,34 @@ void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
   }
   // Highest element index + 1 each operand is read or written at.
   const uint64_t a_need = ta ? uint64_t(k ? k - 1 : 0) * m + me : uint64_t(me) * k;
-  const uint64_t b_need = tb ? uint64_t(ne) * k : uint64_t(k ? k - 1 : 0) * n + ne;
+  const uint64_t b_need = prepared ? prepared::bytes(k, n) / 4
+                                   : (tb ? uint64_t(ne) * k : uint64_t(k ? k - 1 : 0) * n + ne);
   if (k) {
     need_elements(L.args[0], a_need, "a");
-    need_elements(L.args[1], b_need, "b");
+    need_elements(L.args[1], b_need, prepared ? "prepared" : "b");
   }
+  if (prepared && reinterpret_cast<uintptr_t>(L.args[1].ptr) % prepared::kHeaderBytes)
+    throw Failure(PR_INVALID_ARGUMENT, "The prepared tensor must start on a 256-byte boundary");
   need_elements(L.args[2], uint64_t(me - 1) * n + ne, "c");
   if (bias_view)
     need_elements(*bias_view, ne, "bias");
   if (L.dry_run)
     return;
+  PreparedB prep;
+  if (prepared) {
+    const char *base = static_cast<const char *>(L.args[1].ptr);
+    prep.header = reinterpret_cast<const prepared::Header *>(base);
+    prep.raw = reinterpret_cast<const float *>(base + prepared::raw_offset());
+    prep.hi = reinterpret_cast<const float *>(base + prepared::hi_offset(k, n));
+    prep.lo = reinterpret_cast<const float *>(base + prepared::lo_offset(k, n));
+    prep.k = k;
+    prep.n = n;
+  }
   GemmArgs g;
   g.bias = bias_view ? static_cast<const float *>(bias_view->ptr) : nullptr;
   g.activation = activation;
   g.a = static_cast<const float *>(L.args[0].ptr);
-  g.b = static_cast<const float *>(L.args[1].ptr);
+  g.b = prepared ? prep.raw : static_cast<const float *>(L.args[1].ptr);
   g.c = static_cast<float *>(L.args[2].ptr);
   g.m = me;
   g.n = ne;
@@ -594,13 +613,16 @@ void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
   if (mode == matmul_auto || mode == matmul_tf32x3) {
     NonFiniteFlag watch;
     if (launch_tf32x3_gemm(L, g.a, g.b, g.c, me, ne, k, g.lda, g.ldb, g.ldc, ta, tb, g.bias, g.activation,
-                           mode == matmul_auto ? &watch : nullptr)) {
+                           mode == matmul_auto ? &watch : nullptr, prepared ? &prep : nullptr)) {
       recompute_if_infinite(L, g, ta, tb, 1, watch);
       return;
     }
     mode = matmul_ffma;
   }
-  L.kernels = 1;
+  L.kernels = 0;
+  if (prepared)
+    launch_prepared_check(L, prep);
+  ++L.kernels;
   if (mode == matmul_reference) {
     // The register-staged kernel: the reference order (a rounded multiply, then a
     // rounded add, per step) takes two FP32 operations per product, so its ceiling is
@@ -622,6 +644,10 @@ void run_matmul(Launch &L, const BoundArg *bias_view, uint32_t activation) {
 // (a, b, c, m, n, k, transpose_a, transpose_b) with a 16x16 block per 16x16 output
 // tile: the grid bounds the computed region to min(m, 16*grid.y) x min(n, 16*grid.x).
 void launch_provider_matmul(Launch &L) { run_matmul(L, nullptr, 0); }
+
+// pr_b200_matmul_prepared_f32: (a, prepared, c, m, n, k, transpose_a, transpose_b =
+// 0), the matmul launch with B's prepared form in place of B.
+void launch_matmul_prepared(Launch &L) { run_matmul(L, nullptr, 0, true); }
 
 // pr_b200_matmul_bias_activation_f32: (a, b, c, m, n, k, transpose_a, transpose_b,
 // bias or an empty view, activation, has_bias) -- the matmul launch with the

@@ -38,6 +38,7 @@
 //  returns, and the engine reports PR_EXECUTION_FAILED.
 #include "../runtime/builtin.hpp"
 #include "activation.cuh"
+#include "prepared.hpp"
 #include "tma.cuh"
 #include <cuda.h>
 #include <algorithm>
@@ -1258,7 +1259,7 @@ EncodeTiled encoder() {
   return fn;
 }
 
-bool make_map(CUtensorMap *map, float *base, int64_t rows_pad, int64_t k_pad, uint32_t box_rows) {
+bool make_map(CUtensorMap *map, const float *base, int64_t rows_pad, int64_t k_pad, uint32_t box_rows) {
   const EncodeTiled encode = encoder();
   if (!encode)
     return false;
@@ -1266,7 +1267,7 @@ bool make_map(CUtensorMap *map, float *base, int64_t rows_pad, int64_t k_pad, ui
   const cuuint64_t strides[1] = {cuuint64_t(k_pad) * 4};
   const cuuint32_t box[2] = {TK, box_rows};
   const cuuint32_t element[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, element,
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, element,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1424,6 +1425,76 @@ int pair_group(bool raw) {
   return forced ? forced : (raw ? 8 : 2);
 }
 
+// ---- prepared right-hand operands (layout in prepared.hpp)
+
+// Header of a prepared operand, written before its split pass (which may set the
+// infinity mark).
+__global__ void prepared_init(prepared::Header *h, uint64_t k, uint64_t n, uint64_t k_pad, uint64_t n_pad) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    h->magic = prepared::kMagic;
+    h->version = prepared::kVersion;
+    h->k = k;
+    h->n = n;
+    h->k_pad = k_pad;
+    h->n_pad = n_pad;
+    h->nonfinite = 0;
+  }
+}
+
+// A product given a prepared operand: its header must describe (k, n), else the
+// command fails (status_prepared_mismatch) and C is undefined. The operand's
+// infinity mark is copied to the command's watch word (AUTO mode), so that the
+// guarded FFMA recomputation runs as it would after splitting B.
+__global__ void prepared_check(const prepared::Header *h, uint64_t k, uint64_t n, int *status,
+                               unsigned long long *nonfinite, unsigned long long epoch) {
+  if (threadIdx.x != 0 || blockIdx.x != 0)
+    return;
+  if (h->magic != prepared::kMagic || h->version != prepared::kVersion || h->k != k || h->n != n) {
+    if (status)
+      atomicExch(status, prepared::status_mismatch);
+    return;
+  }
+  if (nonfinite && h->nonfinite)
+    *nonfinite = epoch;
+}
+
+// B stored [k][n] copied to the prepared [k][n] copy (count elements, 128-bit when
+// both sides are 16-byte aligned).
+__global__ void __launch_bounds__(256) prepared_copy(const float *__restrict__ b, float *__restrict__ raw,
+                                                     uint64_t count, int vec) {
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+  const uint64_t first = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (vec) {
+    for (uint64_t i = first; i < count / 4; i += stride)
+      reinterpret_cast<float4 *>(raw)[i] = reinterpret_cast<const float4 *>(b)[i];
+    for (uint64_t i = count / 4 * 4 + first; i < count; i += stride)
+      raw[i] = b[i];
+  } else {
+    for (uint64_t i = first; i < count; i += stride)
+      raw[i] = b[i];
+  }
+}
+
+// B stored [n][k] (ldb = k) transposed into the prepared [k][n] copy: 32 x 32 tiles
+// through shared memory (one padding column keeps the column reads conflict-free).
+__global__ void __launch_bounds__(256) prepared_transpose(const float *__restrict__ b, float *__restrict__ raw,
+                                                          int64_t k, int64_t n) {
+  __shared__ float tile[32][33];
+  const int64_t n0 = int64_t(blockIdx.y) * 32, k0 = int64_t(blockIdx.x) * 32;
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32; // 8 rows of 32
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t row = n0 + r, col = k0 + tx;
+    if (row < n && col < k)
+      tile[r][tx] = b[row * k + col];
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t row = k0 + r, col = n0 + tx; // raw[row][col] = B^T
+    if (row < k && col < n)
+      raw[row * n + col] = tile[tx][r];
+  }
+}
+
 // The kernel forms: N tile width x (which operand, if any, is split in shared
 // memory), plus the transposed form for narrow C (256 columns, raw B, D = C^T).
 enum class Form { n64, n64_raw_a, n128, n128_raw_a, n256, n256_raw_a, transposed };
@@ -1475,10 +1546,15 @@ bool raw_a_layout(const float *a, bool ta, int64_t m, int64_t lda, int64_t sa) {
 //    and A's rows as the 256-wide side, converted in shared memory.
 //  * otherwise: 128 x BN tiles of C; A converted in shared memory when at most two
 //    column tiles re-read it, else split by the split pass.
+//  * prep (one matrix, B stored [k][n] as far as the caller is concerned): B's TF32
+//    pair comes from the prepared operand instead of a split pass over B.
 bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m, int64_t n,
                    int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb, int64_t ldc,
-                   int64_t sc, const float *bias, uint32_t activation, NonFiniteFlag *watch) {
+                   int64_t sc, const float *bias, uint32_t activation, NonFiniteFlag *watch,
+                   const PreparedB *prep = nullptr) {
   if (!encoder() || !L.workspace)
+    return false;
+  if (prep && (batch != 1 || uint64_t(k) != prep->k || uint64_t(n) < 1 || uint64_t(n) > prep->n))
     return false;
   if (batch == 1)
     sa = m * lda;
@@ -1515,7 +1591,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // (or, transposed, n padded to 128: the kernel's M side).
   const int64_t a_rows = a_split ? batch * dm_pad : 0;
   const int64_t b_rows_each = transposed ? dm_pad : dn_pad;
-  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_rows + batch_b * b_rows_each);
+  // A prepared B holds its pair with n_pad (>= b_rows_each) rows of k_pad.
+  const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_rows + (prep ? 0 : batch_b * b_rows_each));
   // After the split operands and the partial tiles: the non-finite flag word (8 bytes;
   // both regions are multiples of 8 bytes).
   const size_t bytes = split_bytes + plan.partial_bytes + (watch ? 8 : 0);
@@ -1534,8 +1611,9 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
     watch->word = flag;
     watch->epoch = epoch;
   }
-  float *ahi = scratch, *alo = ahi + a_rows * k_pad, *bhi = alo + a_rows * k_pad,
-        *blo = bhi + batch_b * b_rows_each * k_pad;
+  float *ahi = scratch, *alo = ahi + a_rows * k_pad;
+  const float *bhi = prep ? prep->hi : alo + a_rows * k_pad;
+  const float *blo = prep ? prep->lo : bhi + batch_b * b_rows_each * k_pad;
   CUtensorMap maps[4];
   if (transposed) { // kernel A = op(B)^T pair, kernel B = raw rows of A
     if (!make_map(&maps[0], bhi, batch_b * dm_pad, k_pad, TM) || !make_map(&maps[1], blo, batch_b * dm_pad, k_pad, TM) ||
@@ -1570,13 +1648,17 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
       split_tf32<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad, flag, epoch);
     ++L.kernels;
   }
-  {
+  if (prep) {
+    prepared_check<<<1, 32, 0, L.stream>>>(prep->header, prep->k, prep->n, L.status, flag, epoch);
+    ++L.kernels;
+  } else {
+    float *bhi_w = const_cast<float *>(bhi), *blo_w = const_cast<float *>(blo);
     const dim3 grid(uint32_t(k_pad / 32), uint32_t(b_rows_each / 32), uint32_t(batch_b));
     if (vec_ok(b, ldb, sb))
-      split_tf32_vec<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each, flag,
-                                                 epoch);
+      split_tf32_vec<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi_w, blo_w, k_pad, sb, b_rows_each,
+                                                 flag, epoch);
     else
-      split_tf32<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi, blo, k_pad, sb, b_rows_each, flag,
+      split_tf32<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, n, k, bhi_w, blo_w, k_pad, sb, b_rows_each, flag,
                                              epoch);
     ++L.kernels;
   }
@@ -1627,7 +1709,7 @@ bool encode_map_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t 
 // shape is outside what this kernel covers or scratch is unavailable.
 bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                         int64_t lda, int64_t ldb, int64_t ldc, bool ta, bool tb, const float *bias,
-                        uint32_t activation, NonFiniteFlag *watch) {
+                        uint32_t activation, NonFiniteFlag *watch, const PreparedB *prep) {
   if (k < 16 || m < 1 || n < 1)
     return false;
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n < 128 * 256))
@@ -1635,7 +1717,7 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   L.kernels = 0;
   const bool gelu_pass = activation == 2u; // tanh GELU: bias in the epilogue, GELU after
   if (!launch_tf32x3(L, a, b, c, 1, m, n, k, lda, ta, 0, ldb, tb, 0, ldc, 0, bias, gelu_pass ? 0u : activation,
-                     watch))
+                     watch, prep))
     return false;
   if (gelu_pass && !L.dry_run) {
     const int64_t blocks = std::min<int64_t>((m * n / 4 + 255) / 256 + 1, int64_t(std::max(1, L.sm_count)) * 8);
@@ -1651,6 +1733,62 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
 // ldc, column stride 1). Same split and GEMM kernels with a batch grid dimension
 // (split) and batch-major tile numbering (GEMM); the split operands of all
 // matrices are stacked row-wise, so no tile crosses a matrix boundary.
+// The header check of a prepared operand before a SIMT product reads its [k][n] copy.
+void launch_prepared_check(Launch &L, const PreparedB &prep) {
+  prepared_check<<<1, 32, 0, L.stream>>>(prep.header, prep.k, prep.n, L.status, nullptr, 0);
+  ++L.kernels;
+}
+
+// (b, prepared, k, n, transpose_b): B ([k][n], or [n][k] when transpose_b) into its
+// prepared form (prepared.hpp): the header, B^T's TF32 pair (the split pass, which
+// marks the header when a high part is infinite) and the [k][n] copy.
+void launch_matmul_prepare(Launch &L) {
+  const auto &A = L.args;
+  const uint64_t k = A[2].u32(), n = A[3].u32();
+  const uint32_t tb = A[4].u32();
+  if (tb > 1)
+    throw Failure(PR_INVALID_ARGUMENT, "Transpose flags must be 0 or 1");
+  const uint64_t bytes = prepared::bytes(k, n);
+  if (!bytes)
+    throw Failure(PR_INVALID_ARGUMENT, "A prepared operand needs 1 <= k, n <= INT32_MAX");
+  if (prepared::n_pad(n) / 32 > 65535)
+    throw Failure(PR_UNSUPPORTED, "A prepared operand holds at most 2097152 columns");
+  need_elements(A[0], k * n, "b");
+  need_elements(A[1], bytes / 4, "prepared");
+  if (reinterpret_cast<uintptr_t>(A[1].ptr) % prepared::kHeaderBytes)
+    throw Failure(PR_INVALID_ARGUMENT, "The prepared tensor must start on a 256-byte boundary");
+  L.variant = "prepare_tf32x3";
+  if (L.dry_run)
+    return;
+  const float *b = static_cast<const float *>(A[0].ptr);
+  char *base = static_cast<char *>(A[1].ptr);
+  auto *header = reinterpret_cast<prepared::Header *>(base);
+  float *raw = reinterpret_cast<float *>(base + prepared::raw_offset());
+  float *hi = reinterpret_cast<float *>(base + prepared::hi_offset(k, n));
+  float *lo = reinterpret_cast<float *>(base + prepared::lo_offset(k, n));
+  const int64_t k_pad = int64_t(prepared::k_pad(k)), n_pad = int64_t(prepared::n_pad(n));
+  const int64_t ldb = tb ? int64_t(k) : int64_t(n);
+  L.kernels = 0;
+  prepared_init<<<1, 32, 0, L.stream>>>(header, k, n, uint64_t(k_pad), uint64_t(n_pad));
+  const dim3 grid(uint32_t(k_pad / 32), uint32_t(n_pad / 32), 1);
+  if ((reinterpret_cast<uintptr_t>(b) & 15u) == 0 && ldb % 4 == 0)
+    split_tf32_vec<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, int64_t(n), int64_t(k), hi, lo, k_pad, 0, n_pad,
+                                               &header->nonfinite, 1);
+  else
+    split_tf32<<<grid, 256, 0, L.stream>>>(b, ldb, tb ? 0 : 1, int64_t(n), int64_t(k), hi, lo, k_pad, 0, n_pad,
+                                           &header->nonfinite, 1);
+  if (tb) {
+    prepared_transpose<<<dim3(uint32_t((k + 31) / 32), uint32_t((n + 31) / 32)), 256, 0, L.stream>>>(
+        b, raw, int64_t(k), int64_t(n));
+  } else {
+    const uint64_t count = k * n;
+    const int64_t blocks = std::min<int64_t>(int64_t((count / 4 + 255) / 256) + 1, int64_t(std::max(1, L.sm_count)) * 8);
+    prepared_copy<<<uint32_t(blocks), 256, 0, L.stream>>>(b, raw, count,
+                                                          (reinterpret_cast<uintptr_t>(b) & 15u) == 0 ? 1 : 0);
+  }
+  L.kernels = 3;
+}
+
 bool launch_tf32x3_batched(Launch &L, const float *a, const float *b, float *c, int64_t batch, int64_t m,
                            int64_t n, int64_t k, int64_t lda, bool ta, int64_t sa, int64_t ldb, bool tb, int64_t sb,
                            int64_t ldc, int64_t sc, NonFiniteFlag *watch) {

@@ -1,5 +1,6 @@
 #include "engine.hpp"
 #include "jit.hpp"
+#include "../kernels/prepared.hpp"
 #include <algorithm>
 #include <atomic>
 #include <chrono>
@@ -876,6 +877,9 @@ void Engine::finish(const std::shared_ptr<Work> &work) {
       if (status == status_out_of_view && failure.empty())
         failure = "Kernel " + work->kernel + " addressed elements outside its bound views; those "
                   "loads read 0 and those stores were skipped";
+      else if (status == prepared::status_mismatch && failure.empty())
+        failure = "Kernel " + work->kernel + " was given a prepared operand that was not prepared for its "
+                  "k and n; its output is undefined";
       else if (status != 0 && failure.empty())
         failure = "Kernel " + work->kernel + " abandoned a bounded wait (status " +
                   std::to_string(status) + ")";

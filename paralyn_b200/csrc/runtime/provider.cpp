@@ -23,6 +23,7 @@
 // The statuses and this order are the reference's contract (runtime/tensor.cpp:
 // 448-1038); tests/test_gpu_provider_validation.py and tests/test_abi.py pin them.
 #include "abi_internal.hpp"
+#include "../kernels/prepared.hpp"
 #include "paralyn/b200.h"
 #include <algorithm>
 #include <cmath>
@@ -862,6 +863,8 @@ namespace pb {
 void launch_layer_norm_gather(Launch &);
 void launch_matmul_bias_activation(Launch &);
 void launch_gather_rows(Launch &);
+void launch_matmul_prepare(Launch &);
+void launch_matmul_prepared(Launch &);
 
 namespace {
 // Binds operands as raw device ranges of one submitted command (for entries that
@@ -938,6 +941,115 @@ PB_EXPORT pr_status pr_b200_matmul_bias_activation_f32(pr_queue queue, pr_module
       d.bits(activation);
       d.bits(bias ? 1u : 0u);
       *out = submit_command(queue, "b200_matmul_bias_activation_f32", launch_matmul_bias_activation,
+                            Dim3{uint32_t((op->n + kTile - 1) / kTile), uint32_t((op->m + kTile - 1) / kTile), 1},
+                            Dim3{kTile, kTile, 1}, std::move(d.args), std::move(d.retained));
+    }));
+  });
+}
+
+// ---- prepared right-hand operands
+PB_EXPORT uint64_t pr_b200_matmul_prepared_bytes(uint64_t k, uint64_t n) { return prepared::bytes(k, n); }
+
+namespace pb {
+namespace {
+// The prepared tensor: rank 1, exactly prepared_bytes(k, n) / 4 elements, starting
+// on a 256-byte boundary of its buffer.
+void expect_prepared(const Operand &o, uint64_t k, uint64_t n) {
+  const uint64_t bytes = prepared::bytes(k, n);
+  if (!bytes)
+    reject(PR_INVALID_ARGUMENT, "A prepared operand needs 1 <= k, n <= INT32_MAX");
+  expect_shape(o, {bytes / 4}, "prepared");
+  if (o.desc->byte_offset % prepared::kHeaderBytes)
+    reject(PR_INVALID_ARGUMENT, "prepared: the view must start on a 256-byte boundary");
+}
+} // namespace
+} // namespace pb
+
+// B (the right-hand operand of pr_matmul_f32: [k, n], or [n, k] with transpose_b)
+// into its prepared form: a command that writes `prepared` (a 1-D FP32 tensor of
+// pr_b200_matmul_prepared_bytes(k, n) / 4 elements on a 256-byte boundary, in its
+// own allocation). Checks, in order: event output, transpose flag, presence, ranks
+// and layouts, the prepared shape, separate allocations, one context and the
+// provider module.
+PB_EXPORT pr_status pr_b200_matmul_prepare_f32(pr_queue queue, pr_module operators, const pr_tensor_desc_v1 *b,
+                                               uint32_t transpose_b, const pr_tensor_desc_v1 *prepared_out,
+                                               pr_event *out) {
+  return guarded("matmul_prepare_f32", [&] {
+    if (!out)
+      reject(PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    if (transpose_b > 1)
+      reject(PR_INVALID_ARGUMENT, "Transpose flags must be 0 or 1");
+    if (!b || !prepared_out)
+      reject(PR_INVALID_ARGUMENT, "Missing matmul tensor");
+    std::vector<Operand> operands{Operand{b, operand_extent(b, {"B", 2}, 2), "B", false},
+                                  Operand{prepared_out, operand_extent(prepared_out, {"prepared", 1}, 1), "prepared",
+                                          true}};
+    const uint64_t k = transpose_b ? b->shape[1] : b->shape[0], n = transpose_b ? b->shape[0] : b->shape[1];
+    bounded_dims({k, n}, "Matmul");
+    expect_prepared(operands[1], k, n);
+    separate(operands[1], operands[0]);
+    one_context(queue, operators, operands);
+    verify_entry(operators, "paralyn_matmul_f32");
+    forward(api("matmul_prepare_f32", [&] {
+      const QueueAccess q = queue_access(queue);
+      DirectArguments d{q, {}, {}};
+      d.tensor(operands[0], false);
+      d.tensor(operands[1], true);
+      for (uint64_t v : {k, n, uint64_t(transpose_b)})
+        d.bits(uint32_t(v));
+      *out = submit_command(queue, "b200_matmul_prepare_f32", launch_matmul_prepare, Dim3{1, 1, 1},
+                            Dim3{kLanes, 1, 1}, std::move(d.args), std::move(d.retained));
+    }));
+  });
+}
+
+// C = op(A) B with B's prepared form in op->b: pr_matmul_f32's record and rules,
+// except that op->b is the prepared tensor (prepared for op->k and op->n) and
+// op->transpose_b must be 0. Results equal pr_matmul_f32 with the B it was prepared
+// from, in every matmul mode (bit for bit in the same mode).
+PB_EXPORT pr_status pr_b200_matmul_prepared_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
+                                                pr_event *out) {
+  static const Rules<pr_matmul_v1> rules = [] {
+    Rules<pr_matmul_v1> r = matmul_rules();
+    r.operation = "matmul_prepared_f32";
+    r.operands[1] = {"prepared", 1};
+    r.scalars = [](const pr_matmul_v1 &m) {
+      matmul_rules().scalars(m);
+      if (m.transpose_b)
+        reject(PR_INVALID_ARGUMENT, "A prepared operand is used as prepared: transpose_b must be 0");
+    };
+    r.shapes = [](const pr_matmul_v1 &m, const std::vector<Operand> &o) {
+      bounded_dims({m.m, m.n, m.k}, "Matmul");
+      if (m.transpose_a)
+        expect_shape(o[0], {m.k, m.m}, "A (stored transposed as [k,m])");
+      else
+        expect_shape(o[0], {m.m, m.k}, "A [m,k]");
+      expect_prepared(o[1], m.k, m.n);
+      expect_shape(o[2], {m.m, m.n}, "C [m,n]");
+    };
+    return r;
+  }();
+  return guarded(rules.operation, [&] {
+    if (!out)
+      reject(PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    check_header(op, rules.record);
+    rules.scalars(*op);
+    std::vector<Operand> operands = operands_of(rules, *op);
+    check_operands(rules, *op, operands, queue, operators);
+    verify_entry(operators, "paralyn_matmul_f32");
+    if (!op->m)
+      return;
+    forward(api("matmul_prepared_f32", [&] {
+      const QueueAccess q = queue_access(queue);
+      DirectArguments d{q, {}, {}};
+      d.tensor(operands[0], false);
+      d.tensor(operands[1], false);
+      d.tensor(operands[2], true);
+      for (uint64_t v : {op->m, op->n, op->k, uint64_t(op->transpose_a), uint64_t(0)})
+        d.bits(uint32_t(v));
+      *out = submit_command(queue, "b200_matmul_prepared_f32", launch_matmul_prepared,
                             Dim3{uint32_t((op->n + kTile - 1) / kTile), uint32_t((op->m + kTile - 1) / kTile), 1},
                             Dim3{kTile, kTile, 1}, std::move(d.args), std::move(d.retained));
     }));

@@ -76,6 +76,22 @@ class ChainShard:
         self.zd = TensorDescriptor(self.z, (m, n))
         self.yd = TensorDescriptor(self.y, (m, n))
         self.seed, self.w_std = seed, w_std
+        self.w_prepared = None  # b200.PreparedMatrix of W once prepare_weights() ran
+
+    def prepare_weights(self):
+        """Prepare W once (its TF32 pair and a copy, pr_b200_matmul_prepare_f32), so
+        that every later step reads the prepared form instead of splitting W again.
+        Results are unchanged bit for bit; a W written after this call is not seen."""
+        if self.w_prepared is not None:
+            self.w_prepared.close()
+        self.w_prepared = b200.PreparedMatrix(self.queue, self.resources.module, self.context, self.wd,
+                                              k=self.k, n=self.n)
+
+    def _matmul(self, xd, zd, rows):
+        if self.w_prepared is None:
+            return matmul_into(self.queue, self.resources.module, xd, self.wd, zd, m=rows, n=self.n, k=self.k)
+        return b200.matmul_prepared_into(self.queue, self.resources.module, xd, self.w_prepared.descriptor, zd,
+                                         m=rows, n=self.n, k=self.k)
 
     def fill_synthetic(self, gamma=1.0, beta=0.0):
         """Device-side generation of this shard's inputs (draw offsets of the full stream)."""
@@ -97,8 +113,7 @@ class ChainShard:
         """Enqueue Z = X W and Y = LayerNorm(Z); with `gathered` (a GatheredOutput)
         the LayerNorm also writes its rows into every rank's gathered Y. Returns the
         two events."""
-        mm = matmul_into(self.queue, self.resources.module, self.xd, self.wd, self.zd,
-                         m=self.local_rows, n=self.n, k=self.k)
+        mm = self._matmul(self.xd, self.zd, self.local_rows)
         if gathered is None:
             ln = layer_norm_into(self.queue, self.resources.module, self.zd, self.gd, self.bd, self.yd,
                                  epsilon=self.epsilon)
@@ -130,8 +145,7 @@ class ChainShard:
             events.append(b200.write_async(self.queue, self.x, x_host + xo, offset=xo, nbytes=4 * rows * k))
             zd = TensorDescriptor(self.z, (rows, n), yo)
             yd = TensorDescriptor(self.y, (rows, n), yo)
-            events.append(matmul_into(self.queue, self.resources.module, TensorDescriptor(self.x, (rows, k), xo),
-                                      self.wd, zd, m=rows, n=n, k=k))
+            events.append(self._matmul(TensorDescriptor(self.x, (rows, k), xo), zd, rows))
             if gathered is None:
                 events.append(layer_norm_into(self.queue, self.resources.module, zd, self.gd, self.bd, yd,
                                               epsilon=self.epsilon))
@@ -146,6 +160,8 @@ class ChainShard:
         return 2 * self.local_rows * self.n * self.k
 
     def close(self):
+        if self.w_prepared is not None:
+            self.w_prepared.close()
         for buf in (self.x, self.w, self.gamma, self.beta, self.z, self.y):
             buf.close()
 

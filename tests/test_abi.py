@@ -24,7 +24,7 @@ ROOT = Path(__file__).resolve().parents[1]
 def declared_symbols():
     names = set()
     for header in (ROOT / "include" / "paralyn").glob("*.h"):
-        names |= set(re.findall(r"^(?:pr_status|uint32_t)\s+(pr_\w+)\(", header.read_text(), re.M))
+        names |= set(re.findall(r"^(?:pr_status|uint32_t|uint64_t)\s+(pr_\w+)\(", header.read_text(), re.M))
     return names
 
 
@@ -191,3 +191,12 @@ def test_module_inspection_maps_operators():
     entries = p.inspect_module(prk.serialize(prk.operators()))
     assert entries == {"array_add": "ir.add.u32", "array_affine": "ir.affine.u32",
                        "array_affine_scalar": "ir.affine_scalar.u32"}
+
+
+def test_prepared_operand_sizes(lib):
+    from paralyn_b200 import b200
+    assert b200.matmul_prepared_bytes(lib, 4096, 4096) == 256 + 4 * 4096 * 4096 + 8 * 4096 * 4096
+    assert b200.matmul_prepared_bytes(lib, 33, 300) == 256 + -(-4 * 33 * 300 // 256) * 256 + 8 * 512 * 64
+    assert b200.matmul_prepared_bytes(lib, 64, 256) == b200.matmul_prepared_bytes(lib, 32, 512)
+    for k, n in ((0, 5), (5, 0), (1 << 31, 5), (5, 1 << 31)):
+        assert b200.matmul_prepared_bytes(lib, k, n) == 0

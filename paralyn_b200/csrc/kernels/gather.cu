@@ -3,7 +3,7 @@
 // and its peers' (CUDA-IPC-mapped device memory of the other GPUs, reached with plain
 // stores). This is the all-gather of a row-sharded result (a GEMM shard's C, for
 // instance) as one kernel that reads the shard once and streams it to every
-// destination at once; no NCCL, no multicast and no TMA touch peer memory.
+// destination at once; only plain stores touch peer memory (no NCCL, no TMA).
 #include "../runtime/builtin.hpp"
 #include <algorithm>
 

@@ -801,7 +801,7 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
 //  warp 0 lane 0 (both CTAs): TMA producer. It waits for its own stage to be free
 //    (`empty`, signalled by CTA 0's MMA commit in both CTAs), CTA 0 arms its `full`
 //    barrier with both CTAs' bytes, and both CTAs' copies complete on CTA 0's
-//    barrier (cta_group::2 TMA, no multicast).
+//    barrier (cta_group::2 TMA; each CTA loads its own half).
 //  warp 1 (both CTAs): allocates 512 TMEM columns as a pair (two 256-column
 //    accumulators); lane 0 of CTA 0 issues the MMAs and commits stages and
 //    accumulators to the barriers of both CTAs.

@@ -543,6 +543,77 @@ def time_steps(w, ctx, group, steps, warmup):
             "clocks": clocks.summary(), "variant": variant, "dominant_seconds": sum(durations) / len(durations)}
 
 
+# Steps whose device work is a few microseconds (the 2^20 add: about 2 us of HBM time)
+# finish faster than the host enqueues them (about 14 us per command through the
+# binding, the checks and the launch), so a host-paced loop times the host. These
+# workloads are timed as the reference times them (the GPU duration of its command
+# buffers): in windows of this many steps, each enqueued behind a queue hold
+# (pr_b200_queue_hold) long enough for the host to enqueue the whole window, so the
+# steps run back to back on the device; `value` is the steps' device time between
+# the markers around each window, summed. The host-paced figure is reported beside
+# it (`host_paced`).
+QUEUE_AHEAD = {"add": 1000}
+HOLD_PER_STEP_S = 40e-6
+
+
+def time_steps_queued(w, ctx, group, steps, warmup, per_window):
+    """time_steps with the device held while each window of steps is enqueued."""
+    import paralyn_b200 as p
+    from paralyn_b200 import b200
+    warm = []
+    for _ in range(warmup):
+        warm += w.step()[0]
+    w.ctx.synchronize()
+    for e in warm:
+        e.close()
+    kernels_before = p.device_kernel_count(ctx)
+    group.barrier()
+    ctx.synchronize()
+    timed, dominant, windows, holds = [], [], [], []
+    hold_s = min(1.0, 2e-3 + HOLD_PER_STEP_S * per_window)
+    with Clocks(group.local_rank) as clocks:
+        done = 0
+        while done < steps:
+            n = min(per_window, steps - done)
+            holds.append(b200.queue_hold(w.queue, hold_s))
+            start = b200.marker(w.queue)
+            for _ in range(n):
+                events, main = w.step()
+                timed += events
+                dominant.append(main)
+            windows.append((start, b200.marker(w.queue)))
+            done += n
+        ctx.synchronize()
+    group.barrier()
+    seconds = sum(b200.elapsed(a, b) for a, b in windows)
+    kernels = p.device_kernel_count(ctx) - kernels_before - len(holds)  # the holds are not steps
+    durations = [e.timing().duration_seconds for e in dominant]
+    variant = last_variant(ctx, w.name)
+    for e in timed + holds + [x for pair in windows for x in pair]:
+        e.close()
+    worst = group.max(seconds)
+    return {"seconds": worst, "steps": steps, "value": w.units_total * steps / worst * w.scale,
+            "ms_per_step": worst / steps * 1e3, "gpu_launches": int(group.max(kernels)),
+            "clocks": clocks.summary(), "variant": variant, "dominant_seconds": sum(durations) / len(durations),
+            "queued": {"steps_per_window": per_window, "windows": len(windows), "hold_s": hold_s,
+                       "busy_fraction": round(sum(durations) / seconds, 4),
+                       "timing": "device time between markers around windows of steps enqueued behind a "
+                                 "queue hold (pr_b200_queue_hold), summed; the holds are outside the windows"}}
+
+
+def timed_region(w, ctx, group, steps, warmup):
+    """The workload's timed region: queued-ahead windows for the microsecond-scale
+    steps (with the host-paced figure beside them), else time_steps."""
+    if w.name not in QUEUE_AHEAD:
+        return time_steps(w, ctx, group, steps, warmup)
+    t = time_steps_queued(w, ctx, group, steps, warmup, QUEUE_AHEAD[w.name])
+    paced = time_steps(w, ctx, group, steps, warmup)
+    t["host_paced"] = {"value": round(paced["value"], 3), "ms_per_step": round(paced["ms_per_step"], 5),
+                       "steps": steps, "timing": "device time between two markers around steps enqueued one by "
+                                                 "one by the host (bound by the host's enqueue rate)"}
+    return t
+
+
 def with_clock_fraction(roofline, clocks):
     mhz = clocks.get("sm_mhz")
     if roofline.get("bound") == "fp32_ffma" and mhz:  # the FFMA peak scales with the clock actually run
@@ -567,14 +638,17 @@ def side_configs(args, ctx, group):
         w = Workload(name, ctx, group)
         if args.matmul_mode != "auto" and name == "gemm":
             w.config["matmul_mode"] = args.matmul_mode
-        t = time_steps(w, ctx, group, DEFAULT_STEPS[name] * (group.world if w.scaling == "strong" else 1),
-                       args.warmup)
+        t = timed_region(w, ctx, group, DEFAULT_STEPS[name] * (group.world if w.scaling == "strong" else 1),
+                         args.warmup)
         roofline = with_clock_fraction(roofline_for(w, t["dominant_seconds"], t["variant"], t["seconds"]),
                                        t["clocks"])
         out[name] = {"metric": w.metric, "value": round(t["value"], 3), "unit": w.unit, "steps": t["steps"],
                      "warmup": args.warmup, "ms_per_step": round(t["ms_per_step"], 5), "scaling": w.scaling,
                      "config": w.config, "roofline": roofline, "clocks": t["clocks"],
                      "gpu_launches": t["gpu_launches"], "dominant_kernel_variant": t["variant"]}
+        for key in ("queued", "host_paced"):
+            if key in t:
+                out[name][key] = t[key]
         del w
         ctx.synchronize()
     return out
@@ -589,7 +663,7 @@ def run_ours(args, group):
     w = Workload(args.workload, ctx, group, gather=args.gather, prepare_w=not args.split_w_per_step)
     if args.matmul_mode != "auto":
         w.config["matmul_mode"] = args.matmul_mode
-    t = time_steps(w, ctx, group, steps_for(args, args.workload, w, world), args.warmup)
+    t = timed_region(w, ctx, group, steps_for(args, args.workload, w, world), args.warmup)
     steps = t["steps"]
 
     e2e = None
@@ -605,6 +679,9 @@ def run_ours(args, group):
             "data": "synthetic (seeded SplitMix64 stream generated on device)", "config": w.config, "e2e": e2e,
             "gpu_launches": t["gpu_launches"], "roofline": roofline, "clocks": t["clocks"],
             "dominant_kernel_variant": t["variant"], "headline_metric": METRIC}
+    for key in ("queued", "host_paced"):
+        if key in t:
+            line[key] = t[key]
     if args.workload == "chain":
         line["w_operand"] = ("split in every step (pr_matmul_f32)" if args.split_w_per_step else
                              "prepared once before the timed steps (pr_b200_matmul_prepare_f32); every step "

@@ -158,6 +158,15 @@ pr_status pr_b200_matmul_prepared_f32(pr_queue queue, pr_module operators, const
  * The GPU itself is left healthy. */
 pr_status pr_b200_selftest_bounded_wait(pr_queue queue, uint64_t cycles, pr_event *event);
 
+/* Enqueues a command that keeps the queue's device work waiting for `nanoseconds`
+ * (at most 1e9; PR_INVALID_ARGUMENT otherwise) by the device's own timer and then
+ * completes (no counterpart in the reference). Commands enqueued behind it start only
+ * after it, so a caller can enqueue a run of short commands while it lasts and have
+ * them run back to back: their device time (pr_b200_marker / pr_b200_event_elapsed
+ * around them) then excludes the host's enqueue gaps, as the reference's GPU
+ * command-buffer timing does. One thread of one block; the rest of the GPU is idle. */
+pr_status pr_b200_queue_hold(pr_queue queue, uint64_t nanoseconds, pr_event *event);
+
 /* Enqueues an empty command whose only effect is a device timestamp on the
  * context queue; it follows every earlier command, copies included.
  * pr_b200_event_elapsed returns the device time between the

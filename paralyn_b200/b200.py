@@ -30,6 +30,7 @@ pr_b200_host_register ptr u64
 pr_b200_host_unregister ptr
 pr_b200_marker h *h
 pr_b200_selftest_bounded_wait h u64 *h
+pr_b200_queue_hold h u64 *h
 pr_b200_matmul_bias_activation_f32 h h ptr ptr u32 *h
 pr_b200_matmul_prepare_f32 h h ptr u32 ptr *h
 pr_b200_matmul_prepared_f32 h h ptr *h
@@ -267,6 +268,15 @@ def selftest_bounded_wait(queue, cycles):
     lib = _b200(queue._lib)
     handle = _c.c_uint64()
     lib.check(lib.api.pr_b200_selftest_bounded_wait(queue.handle, int(cycles), _c.byref(handle)))
+    return Event._adopt(lib, handle.value)
+
+
+def queue_hold(queue, seconds):
+    """A command that keeps the queue's later device work waiting for `seconds` (at
+    most 1) and then completes; returns its Event."""
+    lib = _b200(queue._lib)
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_queue_hold(queue.handle, int(round(seconds * 1e9)), _c.byref(handle)))
     return Event._adopt(lib, handle.value)
 
 

@@ -267,16 +267,6 @@ struct TileArgs {
   // rows, so they share B's tiles in L2); the persistent kernels and split_fixup
   // read it, the one-tile kernel uses 8.
   int group = 8;
-  // CTA-pair kernel, A split ahead (one matrix, A stored [m][k] with 16-byte rows):
-  // the kernel's converter warps split A's rows (a_src, row stride lda_src, k_real
-  // columns) into the pair a_hi_w / a_lo_w ([.][k_pad]) a unit ahead of their use,
-  // in 8-row parts claimed through `parts` (one word per part: 0 free, 1 claimed,
-  // 2 written; zeroed before the launch).
-  const float *a_src = nullptr;
-  int64_t lda_src = 0;
-  int k_real = 0;
-  float *a_hi_w = nullptr, *a_lo_w = nullptr;
-  unsigned *parts = nullptr;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -873,75 +863,16 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
                : "memory");
 }
 
-// ---- A split ahead (AHEAD form of the pair kernel) ----
-// A's split pair is written to global memory by the kernel itself, a work unit ahead
-// of the TMA loads that read it, instead of by a split pass before the kernel. A is
-// cut into bands of 128 rows (what one CTA of a pair loads for a tile) and bands into
-// AHEAD_PARTS parts of 8 rows. The four converter warps of a CTA, before the CTA's
-// next unit, claim every still-free part of that unit's band (atomicCAS 0 -> 1),
-// convert the parts they won with the split pass's own arithmetic, and mark them
-// written (2, release). A producer loads a band only once all its parts read 2. A
-// part is claimed only by a running CTA, whose converters finish it without waiting
-// on anything, so every wait ends without any assumption about which CTAs are
-// resident at the same time.
-constexpr int AHEAD_PART_ROWS = 8, AHEAD_PARTS = PAIR_HALF / AHEAD_PART_ROWS;
-
-// Rows [r0, r0 + AHEAD_PART_ROWS) of op(A) into the split pair, zero padded past m and k (the
-// split pass's layout and arithmetic), by the 128 converter threads (t = 0..127).
-__device__ __forceinline__ void convert_part_ahead(const TileArgs &args, int64_t r0, int t) {
-  const int quads = args.k_blocks * TK / 4; // k_pad / 4
-  const int full_quads = args.k_real / 4;   // quads read with one 128-bit load
-  for (int r = 0; r < AHEAD_PART_ROWS; ++r) {
-    const int64_t row = r0 + r;
-    const bool live = row < args.m;
-    const float *__restrict__ src = args.a_src + (live ? row : 0) * args.lda_src;
-    float4 *__restrict__ hi = reinterpret_cast<float4 *>(args.a_hi_w + row * int64_t(quads) * 4);
-    float4 *__restrict__ lo = reinterpret_cast<float4 *>(args.a_lo_w + row * int64_t(quads) * 4);
-#pragma unroll 4
-    for (int q = t; q < quads; q += 128) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (live) {
-        if (q < full_quads) {
-          v = *reinterpret_cast<const float4 *>(src + 4 * q);
-        } else {
-          for (int e = 0; e < 4; ++e)
-            if (4 * q + e < args.k_real)
-              (&v.x)[e] = src[4 * q + e];
-        }
-      }
-      float4 h, l;
-      split4(v, h, l);
-      if (args.nonfinite && any_inf(h))
-        *args.nonfinite = args.epoch;
-      hi[q] = h;
-      lo[q] = l;
-    }
-  }
-}
-
-__device__ __forceinline__ void converters_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-__device__ __forceinline__ unsigned load_acquire_gpu(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void store_release_gpu(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 // RAW: A is read raw (FP32 boxes of its own rows, from the caller's matrix) and four
 // converter warps per CTA form its TF32 pair in shared memory with the split pass's
 // own conversion, so no split pass runs over A. The raw box of a stage completes on
 // the CTA's own `raw_full` barrier; the converters of both CTAs report to CTA 0's
 // `converted` barrier, which the MMA waits for besides `full` (now B's bytes only).
-// AHEAD: the converter warps split A ahead into global memory (above) and the
-// producer waits for a band's parts before loading it.
-template <bool RAW, bool AHEAD = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW || AHEAD ? THREADS_RAW : THREADS_PLAIN, 1)
+template <bool RAW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
     gemm_tf32x3_pair(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                      const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                      const TileArgs args) {
-  static_assert(!(RAW && AHEAD), "one way of forming A's pair");
   constexpr int S = PAIR_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -956,9 +887,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW || AHEAD ? THREA
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile int *issued = abort_flag + 1;   // k-slices the producer has requested
   volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received (CTA 0)
-  volatile int *producer_unit = abort_flag + 3; // AHEAD: local units the producer has started
-  volatile int *claimed_units = abort_flag + 4; // AHEAD: local units whose band the converters claimed
-  volatile int *claim_won = abort_flag + 5;     // AHEAD: broadcast of one claim's outcome
   float *epi_tiles = reinterpret_cast<float *>(smem + RING_BYTES + BARRIER_BYTES);
 
   const uint32_t rank = cluster_rank();
@@ -1004,8 +932,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW || AHEAD ? THREA
     *abort_flag = 0;
     *issued = 0;
     *consumed = 0;
-    *producer_unit = 0;
-    *claimed_units = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -1025,36 +951,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW || AHEAD ? THREA
 
   if (warp == 0) {
     if (lane == 0) { // TMA producer, both CTAs
-      int g = 0, j = 0, ready_band = -1;
-      for (int u = pair; u < args.units_total && !*abort_flag; u += pairs, ++j) {
+      int g = 0;
+      for (int u = pair; u < args.units_total && !*abort_flag; u += pairs) {
         int tile, kb0, kb1, m0, n0, z;
         unit(u, tile, kb0, kb1);
         locate(tile, m0, n0, z);
         const int a_y = z * args.a_rows + m0 + int(rank) * PAIR_HALF;
         const int b_y = z * args.b_rows + n0 + int(rank) * PAIR_HALF;
-        if (AHEAD) {
-          *producer_unit = j + 1;
-          const int band = a_y / PAIR_HALF;
-          if (band != ready_band) {
-            // Own converters have tried to claim this band's parts, and every part is
-            // written (its claimant is a running CTA).
-            const long long start = clock64();
-            bool ok = true;
-            while (ok && *claimed_units <= j && !*abort_flag)
-              ok = clock64() - start < WAIT_CYCLES;
-            for (int q = 0; ok && q < AHEAD_PARTS && !*abort_flag; ++q)
-              while (load_acquire_gpu(args.parts + band * AHEAD_PARTS + q) != 2u)
-                if (!(ok = clock64() - start < WAIT_CYCLES) || *abort_flag)
-                  break;
-            if (!ok) {
-              atomicExch(args.status, STATUS_TIMEOUT_PRODUCER);
-              *abort_flag = 1;
-              break;
-            }
-            asm volatile("fence.proxy.async.global;" ::: "memory"); // the TMA reads what was written
-            ready_band = band;
-          }
-        }
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % S;
           if (g >= S && !mbar_wait(&empty[s], ((g / S) - 1) & 1)) {
@@ -1131,60 +1034,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW || AHEAD ? THREA
       // Fires once every MMA issued above has finished (both CTAs' TMEM quiet).
       mma_commit_pair(in_cta(drained, 0));
     }
-  } else if (AHEAD && warp >= 2 + EPI_WARPS) { // converter warps 10..13: A's pair ahead of use
-    // The 128 converter threads take every decision together (thread 0 decides and
-    // broadcasts through claim_won between two barrier 1 syncs), so they always
-    // reach the same barriers.
-    const int t = threadIdx.x - THREADS_PLAIN;
-    int j = 0, done_band = -1;
-    for (int u = pair; u < args.units_total; u += pairs, ++j) {
-      if (t == 0) { // at most one unit ahead of this CTA's producer
-        bool go = !*abort_flag;
-        const long long start = clock64();
-        while (go && j >= 1 && *producer_unit < j) {
-          if (*abort_flag) {
-            go = false;
-          } else if (clock64() - start > WAIT_CYCLES) {
-            atomicExch(args.status, STATUS_TIMEOUT_CONVERT);
-            *abort_flag = 1;
-            go = false;
-          }
-        }
-        *claim_won = go ? 2 : 0;
-      }
-      converters_sync();
-      const bool go = *claim_won == 2;
-      converters_sync(); // read by all before thread 0 writes claim_won again
-      if (!go)
-        break;
-      int tile, kb0, kb1, m0, n0, z;
-      unit(u, tile, kb0, kb1);
-      locate(tile, m0, n0, z);
-      const int band = (m0 + int(rank) * PAIR_HALF) / PAIR_HALF;
-      if (band != done_band) {
-        for (int q = 0; q < AHEAD_PARTS; ++q) {
-          unsigned *word = args.parts + band * AHEAD_PARTS + q;
-          if (t == 0)
-            *claim_won = atomicCAS(word, 0u, 1u) == 0u ? 1 : 0;
-          converters_sync();
-          const bool won = *claim_won == 1;
-          if (won)
-            convert_part_ahead(args, int64_t(band) * PAIR_HALF + q * AHEAD_PART_ROWS, t);
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          converters_sync(); // every converter thread's stores of the part are done
-          if (won && t == 0) {
-            __threadfence();
-            store_release_gpu(word, 2u);
-          }
-        }
-        done_band = band;
-      }
-      if (t == 0)
-        *claimed_units = j + 1;
-    }
-    if (t == 0)
-      *claimed_units = 1 << 30; // nothing more to claim
-  } else if (RAW && warp >= 2 + EPI_WARPS) { // RAW converter warps 10..13 of both CTAs
+  } else if (warp >= 2 + EPI_WARPS) { // RAW converter warps 10..13 of both CTAs
     const int t = threadIdx.x - THREADS_PLAIN;
     const uint32_t converted0 = in_cta(converted, 0);
     int g = 0;
@@ -1500,24 +1350,24 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
 
 // CTA pairs the device can hold at once with the pair kernel's shared memory (the
 // persistent grid), set up once per device; 0 when the pair kernel cannot run.
-template <bool RAW, bool AHEAD = false> int pair_capacity(int device) {
+template <bool RAW> int pair_capacity(int device) {
   static int capacity[64] = {};
   static bool known[64] = {};
   if (device < 0 || device >= 64)
     return 0;
   if (!known[device]) {
     known[device] = true;
-    if (cudaFuncSetAttribute(gemm_tf32x3_pair<RAW, AHEAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_tf32x3_pair<RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES_PERSISTENT) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(2, 1, 1);
-    config.blockDim = dim3(RAW || AHEAD ? THREADS_RAW : THREADS_PLAIN, 1, 1);
+    config.blockDim = dim3(RAW ? THREADS_RAW : THREADS_PLAIN, 1, 1);
     config.dynamicSmemBytes = SMEM_BYTES_PERSISTENT;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tf32x3_pair<RAW, AHEAD>, &config) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tf32x3_pair<RAW>, &config) != cudaSuccess) {
       cudaGetLastError();
       clusters = 0;
     }
@@ -1526,8 +1376,8 @@ template <bool RAW, bool AHEAD = false> int pair_capacity(int device) {
   return capacity[device];
 }
 
-void launch_pair(Launch &L, bool raw, bool ahead, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles,
-                 const UnitPlan &plan, float *partials) {
+void launch_pair(Launch &L, bool raw, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
+                 float *partials) {
   t.tiles_total = int(tiles);
   t.units_total = plan.units;
   t.full_units = plan.full_units;
@@ -1535,9 +1385,6 @@ void launch_pair(Launch &L, bool raw, bool ahead, const CUtensorMap (&maps)[4], 
   t.partials = partials;
   if (raw)
     gemm_tf32x3_pair<true><<<uint32_t(2 * plan.ctas), THREADS_RAW, SMEM_BYTES_PERSISTENT, L.stream>>>(
-        maps[0], maps[1], maps[2], maps[3], t);
-  else if (ahead)
-    gemm_tf32x3_pair<false, true><<<uint32_t(2 * plan.ctas), THREADS_RAW, SMEM_BYTES_PERSISTENT, L.stream>>>(
         maps[0], maps[1], maps[2], maps[3], t);
   else
     gemm_tf32x3_pair<false><<<uint32_t(2 * plan.ctas), THREADS_PLAIN, SMEM_BYTES_PERSISTENT, L.stream>>>(
@@ -1562,15 +1409,6 @@ bool pair_enabled() {
 }
 bool pair_raw_enabled() {
   static const bool enabled = env_flag("PARALYN_GEMM_PAIR_RAW");
-  return enabled;
-}
-// PARALYN_GEMM_SPLIT_AHEAD=1: the pair kernel splits A itself ahead of use instead of
-// reading an A split by the split pass.
-bool split_ahead_enabled() {
-  static const bool enabled = [] {
-    const char *v = std::getenv("PARALYN_GEMM_SPLIT_AHEAD");
-    return v && v[0] == '1';
-  }();
   return enabled;
 }
 // Tile rows per raster group of the pair kernel: the A rows of one group (256 rows
@@ -1733,14 +1571,7 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // Converting A in shared memory repeats its TF32 conversions once per column tile,
   // so (as for the one-SM kernel) it pays only while few column tiles re-read A.
   const bool pair_raw = wide && form == Form::n256_raw_a && pair_raw_enabled();
-  // Otherwise, when A's rows can be read as they are (one matrix), the pair kernel
-  // splits A itself a unit ahead of use and no split pass runs over A.
-  const bool ahead_form = wide && !pair_raw && batch == 1 && raw_a && split_ahead_enabled();
-  const int pairs = !wide ? 0
-                          : (pair_raw ? pair_capacity<true>(L.device)
-                                      : (ahead_form ? pair_capacity<false, true>(L.device)
-                                                    : pair_capacity<false>(L.device)));
-  const bool ahead = ahead_form && pairs > 0;
+  const int pairs = !wide ? 0 : (pair_raw ? pair_capacity<true>(L.device) : pair_capacity<false>(L.device));
   if (pairs)
     form = pair_raw ? Form::n256_raw_a : Form::n256;
   const bool a_split = !transposed && (form == Form::n64 || form == Form::n128 || form == Form::n256);
@@ -1763,10 +1594,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // A prepared B holds its pair with n_pad (>= b_rows_each) rows of k_pad.
   const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_rows + (prep ? 0 : batch_b * b_rows_each));
   // After the split operands and the partial tiles: the non-finite flag word (8 bytes;
-  // both regions are multiples of 8 bytes), then the claim words of A's parts when the
-  // pair kernel splits A ahead.
-  const size_t part_words = ahead ? size_t(dm_pad / PAIR_HALF) * AHEAD_PARTS : 0;
-  const size_t bytes = split_bytes + plan.partial_bytes + 8 + 4 * part_words;
+  // both regions are multiples of 8 bytes).
+  const size_t bytes = split_bytes + plan.partial_bytes + (watch ? 8 : 0);
   if (L.dry_run)
     return true;
   auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
@@ -1782,9 +1611,6 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
     watch->word = flag;
     watch->epoch = epoch;
   }
-  unsigned *part_flags = ahead ? reinterpret_cast<unsigned *>(reinterpret_cast<char *>(scratch) + split_bytes +
-                                                               plan.partial_bytes + 8)
-                               : nullptr;
   float *ahi = scratch, *alo = ahi + a_rows * k_pad;
   const float *bhi = prep ? prep->hi : alo + a_rows * k_pad;
   const float *blo = prep ? prep->lo : bhi + batch_b * b_rows_each * k_pad;
@@ -1814,10 +1640,7 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   auto vec_ok = [](const float *x, int64_t ld, int64_t stride) {
     return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && ld % 4 == 0 && stride % 4 == 0;
   };
-  if (ahead) { // no split pass over A: its parts start unclaimed
-    if (cudaMemsetAsync(part_flags, 0, 4 * part_words, L.stream) != cudaSuccess)
-      throw Failure(PR_EXECUTION_FAILED, "Could not clear the GEMM's claim words");
-  } else if (a_split) {
+  if (a_split) {
     const dim3 grid(uint32_t(k_pad / 32), uint32_t(dm_pad / 32), uint32_t(batch));
     if (vec_ok(a, lda, batch > 1 ? sa : 0))
       split_tf32_vec<<<grid, 256, 0, L.stream>>>(a, lda, ta ? 1 : 0, m, k, ahi, alo, k_pad, sa, dm_pad, flag, epoch);
@@ -1857,17 +1680,9 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   t.epoch = epoch;
   if (pairs)
     t.group = pair_group(pair_raw);
-  if (ahead) {
-    t.a_src = a;
-    t.lda_src = lda;
-    t.k_real = int(k);
-    t.a_hi_w = ahi;
-    t.a_lo_w = alo;
-    t.parts = part_flags;
-  }
   ++L.kernels;
   if (pairs)
-    launch_pair(L, pair_raw, ahead, maps, t, tiles_m * tiles_n * batch, plan, partials);
+    launch_pair(L, pair_raw, maps, t, tiles_m * tiles_n * batch, plan, partials);
   else
     launch_form(form, L, maps, t, tiles_m * tiles_n * batch, plan, partials);
   return true;

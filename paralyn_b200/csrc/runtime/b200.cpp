@@ -146,6 +146,22 @@ PB_EXPORT pr_status pr_b200_selftest_bounded_wait(pr_queue queue, uint64_t cycle
   });
 }
 
+namespace pb {
+void launch_queue_hold(Launch &);
+}
+
+PB_EXPORT pr_status pr_b200_queue_hold(pr_queue queue, uint64_t nanoseconds, pr_event *out) {
+  return api("b200_queue_hold", [&] {
+    require(out, PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    require(nanoseconds <= 1000000000ull, PR_INVALID_ARGUMENT, "A hold lasts at most 1e9 ns");
+    std::vector<BoundArg> args(2);
+    args[0].bits = uint32_t(nanoseconds);
+    args[1].bits = uint32_t(nanoseconds >> 32);
+    *out = submit_command(queue, "b200_queue_hold", launch_queue_hold, Dim3{}, Dim3{}, std::move(args), {});
+  });
+}
+
 PB_EXPORT pr_status pr_b200_marker(pr_queue queue, pr_event *out) {
   return api("b200_marker", [&] {
     require(out, PR_INVALID_ARGUMENT, "Missing event output");

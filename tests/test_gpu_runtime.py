@@ -128,3 +128,18 @@ def test_bounded_wait_failure_path():
                 pass
     with p.Context("cuda:0") as ctx, p.asarray(np.ones(1000, np.float32), context=ctx) as a, p.add(a, a) as b:
         assert np.all(np.asarray(b.to_host(), np.float32) == 2.0)
+
+
+def test_queue_hold_delays_later_commands(context):
+    # The hold keeps later commands waiting for its duration (device timer), then the
+    # queue runs on; lengths above one second are refused before anything is enqueued.
+    queue = context.queue()
+    before = p.b200.marker(queue)
+    hold = p.b200.queue_hold(queue, 0.005)
+    after = p.b200.marker(queue)
+    assert p.b200.elapsed(before, after) >= 0.0045
+    with pytest.raises(p.Error) as error:
+        p.b200.queue_hold(queue, 1.5)
+    assert error.value.code == p.Status.INVALID_ARGUMENT
+    for e in (before, hold, after, queue):
+        e.close()

@@ -828,6 +828,14 @@ def roofline_for(w, seconds, variant, region_seconds):
                               "FP32 product)"}
     sms = 148
     peak = sms * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    if variant and "reference_order" in variant:
+        # A rounded multiply and a rounded add per product: two FP32 pipe operations
+        # for the two flops an FFMA does in one.
+        return {"bound": "fp32_mul_add", "achieved": round(achieved, 2), "peak": round(peak / 2, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / (peak / 2), 4), "traffic": traffic,
+                "frac_of_ffma_peak": round(achieved / peak, 4),
+                "peak_basis": f"148 SMs x 128 FP32 lanes x 1 flop (FMUL then FADD per product) x {basis} max "
+                              "SM clock"}
     return {"bound": "fp32_ffma", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "peak_basis": f"148 SMs x 128 FP32 lanes x 2 flop x {basis} max SM clock"}

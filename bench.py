@@ -668,8 +668,10 @@ def run_ours(args, group):
 
     e2e = None
     if not args.no_e2e:
-        # About 8 GB of host<->device traffic per e2e measurement (PCIe-bound).
-        e2e_steps = max(2, min(steps, int(8e9 // (w.h2d + w.d2h))))
+        # About 24 GB of host<->device traffic per e2e measurement (PCIe-bound): the
+        # pipeline's fill and drain, one slice each, weigh less over more steps (chain:
+        # 11 steps, 92-94 TFLOP/s against 90 with 3).
+        e2e_steps = max(2, min(steps, int(24e9 // (w.h2d + w.d2h))))
         e2e = end_to_end(w, ctx, group, steps=e2e_steps)
 
     roofline = with_clock_fraction(roofline_for(w, t["dominant_seconds"], t["variant"], t["seconds"]), t["clocks"])

@@ -614,10 +614,19 @@ def timed_region(w, ctx, group, steps, warmup):
     return t
 
 
+def sm_count():
+    """Streaming multiprocessors of the GPU in use, queried at run time."""
+    import torch
+    if torch.cuda.is_available():
+        return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return 148  # a B200, for device-free calls
+
+
 def with_clock_fraction(roofline, clocks):
     mhz = clocks.get("sm_mhz")
     if roofline.get("bound") == "fp32_ffma" and mhz:  # the FFMA peak scales with the clock actually run
-        roofline["frac_at_median_sm_clock"] = round(roofline["achieved"] / (148 * 128 * 2 * mhz * 1e6 / 1e12), 4)
+        roofline["frac_at_median_sm_clock"] = round(
+            roofline["achieved"] / (sm_count() * 128 * 2 * mhz * 1e6 / 1e12), 4)
     return roofline
 
 
@@ -828,7 +837,7 @@ def roofline_for(w, seconds, variant, region_seconds):
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_basis": f"{basis} bf16 cuBLAS {which} / 2 (TF32 rate) / 3 (three TF32 products per "
                               "FP32 product)"}
-    sms = 148
+    sms = sm_count()
     peak = sms * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
     if variant and "reference_order" in variant:
         # A rounded multiply and a rounded add per product: two FP32 pipe operations
@@ -836,11 +845,11 @@ def roofline_for(w, seconds, variant, region_seconds):
         return {"bound": "fp32_mul_add", "achieved": round(achieved, 2), "peak": round(peak / 2, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / (peak / 2), 4), "traffic": traffic,
                 "frac_of_ffma_peak": round(achieved / peak, 4),
-                "peak_basis": f"148 SMs x 128 FP32 lanes x 1 flop (FMUL then FADD per product) x {basis} max "
+                "peak_basis": f"{sms} SMs x 128 FP32 lanes x 1 flop (FMUL then FADD per product) x {basis} max "
                               "SM clock"}
     return {"bound": "fp32_ffma", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
-            "peak_basis": f"148 SMs x 128 FP32 lanes x 2 flop x {basis} max SM clock"}
+            "peak_basis": f"{sms} SMs x 128 FP32 lanes x 2 flop x {basis} max SM clock"}
 
 
 def load_traffic():

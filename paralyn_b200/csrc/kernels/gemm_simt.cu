@@ -509,7 +509,11 @@ void recompute_if_infinite(Launch &L, const GemmArgs &g, bool ta, bool tb, uint3
   GemmArgs guarded = g;
   guarded.only_if = watch.word;
   guarded.epoch = watch.epoch;
-  dispatch<matmul_ffma>(guarded, ta, tb, L.stream, batch, int64_t(2) * std::max(1, L.sm_count));
+  // About two blocks per SM over the whole batch: the blocks of a launch whose flag
+  // is clear return at once, and for a batch of many matrices a grid of two blocks per
+  // SM for every matrix would take many rounds of block launches to do nothing.
+  const int64_t per_matrix = std::max<int64_t>(1, (int64_t(2) * std::max(1, L.sm_count) + batch - 1) / batch);
+  dispatch<matmul_ffma>(guarded, ta, tb, L.stream, batch, per_matrix);
   ++L.kernels;
 }
 

@@ -452,8 +452,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Eight epilogue warps: warps 2..5 and 6..9 each cover the four TMEM lane quarters,
 // the first group the left half of the tile's columns, the second the right half,
 // staged 32 rows x 16 columns at a time.
-constexpr int EPI_WARPS = 8, EPI_PITCH16 = 20;
+constexpr int EPI_WARPS = 8, EPI_PITCH16 = 16;
 constexpr int EPI_STAGE_FLOATS = 32 * EPI_PITCH16;
+// An epilogue warp's staging tile, 32 rows x 16 columns, row pitch 16 floats, with the
+// 4-float groups of row r stored in the order q ^ ((r / 2) % 4). Both accesses are
+// free of bank conflicts: the rows written from tensor memory (lane = row, 8 lanes
+// per phase) and the reads for the global stores, where each 8-lane phase takes two
+// rows x 64 bytes, so that one store instruction writes 8 rows in four phases of two
+// cache lines each (the unswizzled pitch-20 tile needed 8 rows per phase: 8 lines,
+// and the stores kept the L1 load/store pipe 87 % busy on the batched Q K^T product).
+__device__ __forceinline__ int stage_index(int r, int c) {
+  return r * EPI_PITCH16 + ((((c >> 2) ^ (r >> 1)) & 3) << 2) + (c & 3);
+}
 constexpr int RING_BYTES = 192 * 1024, BARRIER_BYTES = 512;
 constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + EPI_WARPS * EPI_STAGE_FLOATS * 4;
 constexpr int THREADS_PLAIN = 64 + 32 * EPI_WARPS, THREADS_RAW = THREADS_PLAIN + 128; // + 4 converter warps
@@ -742,17 +752,17 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
         }
 #pragma unroll
         for (int q = 0; q < 16; q += 4)
-          *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH16 + q]) =
+          *reinterpret_cast<float4 *>(&tile_s[stage_index(lane, q)]) =
               make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         __syncwarp();
         if (vec_c && rows_here == 32 && first + 15 < n_lim) {
-          // 8 rows x 4 float4 per instruction; each group of 8 lanes reads one column
-          // chunk of 8 rows (row pitch 20 floats): eight distinct 4-bank groups
-          const int r_in = lane % 8, c4 = 4 * (lane / 8);
+          // 8 rows x 64 bytes per instruction: lane = (phase, p), phase = lane / 8 takes
+          // rows 2 phase and 2 phase + 1, p % 4 the 4-float group
+          const int r_in = 2 * (lane >> 3) + ((lane & 7) >> 2), c4 = 4 * (lane & 3);
           float4 w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            w[i] = *reinterpret_cast<const float4 *>(&tile_s[(8 * i + r_in) * EPI_PITCH16 + c4]);
+            w[i] = *reinterpret_cast<const float4 *>(&tile_s[stage_index(8 * i + r_in, c4)]);
           float *cptr = c_base + (row0 + r_in) * ldc + first + c4;
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -762,7 +772,7 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
           if (column < n_lim) {
             float *cptr = c_base + row0 * ldc + column;
             for (int r = lane >> 4; r < rows_here; r += 2)
-              cptr[r * ldc] = tile_s[r * EPI_PITCH16 + (lane & 15)];
+              cptr[r * ldc] = tile_s[stage_index(r, lane & 15)];
           }
         }
         __syncwarp();
@@ -1115,15 +1125,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : 
         }
 #pragma unroll
         for (int q = 0; q < 16; q += 4)
-          *reinterpret_cast<float4 *>(&tile_s[lane * EPI_PITCH16 + q]) =
+          *reinterpret_cast<float4 *>(&tile_s[stage_index(lane, q)]) =
               make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         __syncwarp();
         if (vec_c && rows_here == 32 && first + 15 < n_lim) {
-          const int r_in = lane % 8, c4 = 4 * (lane / 8);
+          const int r_in = 2 * (lane >> 3) + ((lane & 7) >> 2), c4 = 4 * (lane & 3);
           float4 w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            w[i] = *reinterpret_cast<const float4 *>(&tile_s[(8 * i + r_in) * EPI_PITCH16 + c4]);
+            w[i] = *reinterpret_cast<const float4 *>(&tile_s[stage_index(8 * i + r_in, c4)]);
           float *cptr = c_base + (row0 + r_in) * ldc + first + c4;
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -1133,7 +1143,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : 
           if (column < n_lim) {
             float *cptr = c_base + row0 * ldc + column;
             for (int r = lane >> 4; r < rows_here; r += 2)
-              cptr[r * ldc] = tile_s[r * EPI_PITCH16 + (lane & 15)];
+              cptr[r * ldc] = tile_s[stage_index(r, lane & 15)];
           }
         }
         __syncwarp();

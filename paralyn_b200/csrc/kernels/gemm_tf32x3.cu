@@ -1237,29 +1237,6 @@ template <int BN, int TMR = TM> __global__ void __launch_bounds__(256) split_fix
   }
 }
 
-// C = activate(C) in place over [m, n] with row stride ldc: the tanh GELU of a fused
-// GEMM + bias + GELU runs here rather than in the GEMM epilogue, whose four warps
-// share the SM's schedulers with the single-thread TMA and MMA issuers (there the
-// GELU arithmetic slowed the main loop more than this extra pass over C costs).
-__global__ void __launch_bounds__(256) activate_in_place(float *c, int64_t m, int64_t n, int64_t ldc,
-                                                         uint32_t activation) {
-  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  if (ldc == n && (reinterpret_cast<uintptr_t>(c) & 15u) == 0 && (m * n) % 4 == 0) {
-    float4 *c4 = reinterpret_cast<float4 *>(c);
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < m * n / 4; i += stride) {
-      float4 v = c4[i];
-      v.x = activate(v.x, activation);
-      v.y = activate(v.y, activation);
-      v.z = activate(v.z, activation);
-      v.w = activate(v.w, activation);
-      c4[i] = v;
-    }
-    return;
-  }
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < m * n; i += stride) {
-    float *p = c + (i / n) * ldc + i % n;
-    *p = activate(*p, activation);
-  }
 }
 
 // ---- host side ----
@@ -1738,15 +1715,9 @@ bool launch_tf32x3_gemm(Launch &L, const float *a, const float *b, float *c, int
   if (L.matmul_mode == matmul_auto && (k < 64 || m * n < 128 * 256))
     return false;
   L.kernels = 0;
-  const bool gelu_pass = activation == 2u; // tanh GELU: bias in the epilogue, GELU after
-  if (!launch_tf32x3(L, a, b, c, 1, m, n, k, lda, ta, 0, ldb, tb, 0, ldc, 0, bias, gelu_pass ? 0u : activation,
-                     watch, prep))
+  // Bias and activation (ReLU or the tanh GELU) run in the GEMM epilogue.
+  if (!launch_tf32x3(L, a, b, c, 1, m, n, k, lda, ta, 0, ldb, tb, 0, ldc, 0, bias, activation, watch, prep))
     return false;
-  if (gelu_pass && !L.dry_run) {
-    const int64_t blocks = std::min<int64_t>((m * n / 4 + 255) / 256 + 1, int64_t(std::max(1, L.sm_count)) * 8);
-    activate_in_place<<<uint32_t(blocks), 256, 0, L.stream>>>(c, m, n, ldc, activation);
-    ++L.kernels;
-  }
   L.variant = "tcgen05_tf32x3";
   return true;
 }

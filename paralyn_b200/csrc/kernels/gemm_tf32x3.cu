@@ -1237,8 +1237,6 @@ template <int BN, int TMR = TM> __global__ void __launch_bounds__(256) split_fix
   }
 }
 
-}
-
 // ---- host side ----
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,

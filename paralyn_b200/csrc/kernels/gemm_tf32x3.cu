@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // short last round). The N tile width BN is 64, 128 or 256 (the narrow tiles keep
 // the tensor cores off padding when n is small); every form uses a 192 KB ring of
 // 16-deep k-slices. With RAW = RAW_A (RAW_B) the producer loads raw FP32 boxes of
-// the A (B) operand and four converter warps split them into the hi/lo pair in
+// the A (B) operand and sixteen converter warps split them into the hi/lo pair in
 // shared memory with the same conversion as split_tf32 (so the operands, and the
 // result, are bit-identical), which saves the split pass over that operand when
 // few tiles re-read it. TOUT computes C^T: the kernel's M side is C's columns and
@@ -480,6 +480,12 @@ __device__ __forceinline__ int stage_index(int r, int c) {
 constexpr int RING_BYTES = 192 * 1024, BARRIER_BYTES = 512;
 constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + EPI_WARPS * EPI_STAGE_FLOATS * 4;
 constexpr int THREADS_PLAIN = 64 + 32 * EPI_WARPS, THREADS_RAW = THREADS_PLAIN + 128; // + 4 converter warps
+// The one-SM kernel's converter warps, which share each k-slice (the CTA pair keeps
+// four per CTA). A slice's conversion sits on the ring's critical loop (load ->
+// convert -> MMA -> release), so it is spread thin: with four warps the transposed
+// P V product of the encoder block took 158 us, with eight 125, with sixteen 123.
+constexpr int CONVERT_WARPS = 16, CONVERT_THREADS = 32 * CONVERT_WARPS,
+              THREADS_RAW_ONE = THREADS_PLAIN + CONVERT_THREADS;
 constexpr int STATUS_TIMEOUT_CONVERT = 0x7f3204;
 constexpr int RAW_NONE = 0, RAW_A = 1, RAW_B = 2;
 
@@ -515,7 +521,7 @@ __device__ __forceinline__ float4 tf32_hi(float4 v) {
 }
 
 template <int BN, int RAW, bool TOUT>
-__global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
+__global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
     gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                            const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                            const TileArgs args) {
@@ -565,7 +571,7 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&converted[s], 4);
+      mbar_init(&converted[s], CONVERT_WARPS);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
@@ -671,9 +677,10 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
       // Fires once every MMA issued above has finished (TMEM quiet before it is freed).
       mma_commit(drained);
     }
-  } else if (warp >= 2 + EPI_WARPS) { // RAW converter warps 10..13: raw box -> hi in place, lo beside it
+  } else if (warp >= 2 + EPI_WARPS) { // RAW converter warps 10..25: raw box -> hi in place, lo beside it
     const int t = threadIdx.x - THREADS_PLAIN;
     constexpr int RAW_OFFSET = RAW == RAW_B ? 2 * A_BYTES : 0, RAW_BYTES = RAW == RAW_B ? C::B_BYTES : A_BYTES;
+    static_assert(RAW_BYTES % (16 * CONVERT_THREADS) == 0, "converter share");
     int g = 0;
     for (int u = blockIdx.x; u < args.units_total && !*abort_flag; u += gridDim.x) {
       int tile, kb0, kb1;
@@ -690,11 +697,11 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
         float4 *lo = reinterpret_cast<float4 *>(smem + s * C::STAGE + RAW_OFFSET + RAW_BYTES);
         // The swizzle is the same for both boxes, so the pair is formed position by position.
 #pragma unroll
-        for (int i = 0; i < RAW_BYTES / 16 / 128; ++i) {
-          const float4 v = hi[t + 128 * i];
+        for (int i = 0; i < RAW_BYTES / 16 / CONVERT_THREADS; ++i) {
+          const float4 v = hi[t + CONVERT_THREADS * i];
           const float4 h = tf32_hi(v);
-          lo[t + 128 * i] = tf32_hi(make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
-          hi[t + 128 * i] = h;
+          lo[t + CONVERT_THREADS * i] = tf32_hi(make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
+          hi[t + CONVERT_THREADS * i] = h;
           if (args.nonfinite && any_inf(h))
             *args.nonfinite = args.epoch;
         }
@@ -1338,7 +1345,7 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
   t.full_units = plan.full_units;
   t.split = plan.split;
   t.partials = partials;
-  gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? THREADS_RAW : THREADS_PLAIN, SMEM_BYTES_PERSISTENT,
+  gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? THREADS_RAW_ONE : THREADS_PLAIN, SMEM_BYTES_PERSISTENT,
                                           L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
     split_fixup<BN><<<dim3(TM / (1024 / BN), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);

@@ -58,7 +58,8 @@ def parse():
     ap.add_argument("--matmul-mode", default="auto", choices=("auto", "reference", "ffma", "tf32x3"),
                     help="summation mode of the GEMM workloads (default auto: the 3xTF32 tensor-core kernel)")
     ap.add_argument("--split-w-per-step", action="store_true",
-                    help="chain: split W in every step (pr_matmul_f32) instead of preparing it once "
+                    help="chain and block: split the weights in every step (pr_matmul_f32, "
+                         "pr_b200_matmul_bias_activation_f32) instead of preparing them once "
                          "(pr_b200_matmul_prepare_f32) before the timed steps")
     ap.add_argument("--gather", action="store_true",
                     help="chain: also gather Y on every GPU (LayerNorm writes its rows to all ranks over NVLink); "
@@ -356,6 +357,8 @@ class Workload:
         elif name == "block":
             from paralyn_b200.block import EncoderBlock
             self.block = EncoderBlock(ctx, 2048, 1024, 16, 4096, causal=True, seed=2026)
+            if prepare_w:  # the weights are the same in every block: their TF32 pairs are made once
+                self.block.prepare_weights()
             self.units_local = self.block.flops()
             self.units_total = self.units_local * world
             self.h2d = self.d2h = 4 * 2048 * 1024
@@ -697,6 +700,11 @@ def run_ours(args, group):
         line["w_operand"] = ("split in every step (pr_matmul_f32)" if args.split_w_per_step else
                              "prepared once before the timed steps (pr_b200_matmul_prepare_f32); every step "
                              "splits X, multiplies (pr_b200_matmul_prepared_f32) and normalizes")
+    if args.workload == "block":
+        line["w_operand"] = ("split in every block (pr_b200_matmul_bias_activation_f32)" if args.split_w_per_step
+                             else "the four projection weights prepared once before the timed steps "
+                             "(pr_b200_matmul_prepare_f32); every block runs its 11 commands with the projections "
+                             "reading them (pr_b200_matmul_prepared_bias_activation_f32)")
     if args.workload == "chain" and not args.no_configs:
         line["configs"] = side_configs(args, ctx, group)
     if group.rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -148,6 +148,15 @@ pr_status pr_b200_matmul_prepare_f32(pr_queue queue, pr_module operators, const 
                                      uint32_t transpose_b, const pr_tensor_desc_v1 *prepared, pr_event *event);
 pr_status pr_b200_matmul_prepared_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
                                       pr_event *event);
+/* pr_b200_matmul_prepared_f32 with pr_b200_matmul_bias_activation_f32's epilogue: C =
+ * activation(op(A) B + bias[column]) with B's prepared form in op->b. Validation is
+ * the prepared product's, then bias (may be NULL: a contiguous [n] tensor not
+ * aliasing C) with the operands and activation with the record's scalars; the result
+ * equals pr_b200_matmul_bias_activation_f32 with the B the tensor was prepared from,
+ * bit for bit, in every matmul mode. */
+pr_status pr_b200_matmul_prepared_bias_activation_f32(pr_queue queue, pr_module operators, const pr_matmul_v1 *op,
+                                                      const pr_tensor_desc_v1 *bias, uint32_t activation,
+                                                      pr_event *event);
 
 /* Failure-path probe (no counterpart in the reference). Enqueues a one-thread
  * kernel that waits on a shared-memory barrier nothing completes and gives up after

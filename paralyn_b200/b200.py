@@ -34,6 +34,7 @@ pr_b200_queue_hold h u64 *h
 pr_b200_matmul_bias_activation_f32 h h ptr ptr u32 *h
 pr_b200_matmul_prepare_f32 h h ptr u32 ptr *h
 pr_b200_matmul_prepared_f32 h h ptr *h
+pr_b200_matmul_prepared_bias_activation_f32 h h ptr ptr u32 *h
 pr_b200_event_elapsed h h *f64
 pr_b200_fill_synthetic_f32 h *TensorDescRecord u64 u64 u32 f32 f32 *h
 """
@@ -234,6 +235,23 @@ def matmul_prepared_into(queue, operators, a, prepared, c, *, m, n, k, transpose
     handle = _c.c_uint64()
     lib.check(lib.api.pr_b200_matmul_prepared_f32(queue.handle, operators.handle, _c.byref(record),
                                                   _c.byref(handle)))
+    return Event._adopt(lib, handle.value) if handle.value else None
+
+
+def matmul_prepared_bias_activation_into(queue, operators, a, prepared, c, bias, *, m, n, k, transpose_a=False,
+                                         activation=0):
+    """C = activation(op(A) B + bias[column]) from B's prepared form (bias may be
+    None); equal to matmul_bias_activation_into with that B, bit for bit."""
+    from .tensor import MatmulRecord, TENSOR_VERSION_1, Activation
+    lib = _b200(queue._lib)
+    descs = [x._native() for x in (a, prepared, c)]
+    record = MatmulRecord(_c.sizeof(MatmulRecord), TENSOR_VERSION_1, m, n, k, int(bool(transpose_a)), 0,
+                          *(_pointer(d) for d in descs))
+    bias_native = bias._native() if bias is not None else None
+    handle = _c.c_uint64()
+    lib.check(lib.api.pr_b200_matmul_prepared_bias_activation_f32(
+        queue.handle, operators.handle, _c.byref(record),
+        _c.byref(bias_native) if bias_native is not None else None, int(Activation(activation)), _c.byref(handle)))
     return Event._adopt(lib, handle.value) if handle.value else None
 
 

@@ -9,7 +9,10 @@ projection + bias + tanh-GELU -> down projection + bias -> residual add.
 
 `run()` enqueues the reference's 15 launches; `run(fused=True)` runs the same block in
 11, with every bias (and the GELU) in the epilogue of its GEMM
-(pr_b200_matmul_bias_activation_f32), bit-identical to the 15-launch form.
+(pr_b200_matmul_bias_activation_f32), bit-identical to the 15-launch form. After
+`prepare_weights()` the four projections read their weights' prepared forms
+(pr_b200_matmul_prepare_f32, made once), so no block splits a weight again; the results
+stay bit-identical.
 Weights come from the seeded device stream (scales 0.125 / 0.0625, gamma 1 +- 0.25,
 biases +- 0.25, as the reference example uses); all buffers stay on the device.
 """
@@ -43,6 +46,7 @@ class EncoderBlock:
             "ff1_g": (T, F), "ff2": (T, D), "ff2_b": (T, D), "out": (T, D)}
         self.buf = {name: context.buffer(4 * int(np.prod(shape))) for name, shape in self.shapes.items()}
         self._descriptors = {}
+        self.prepared = {}  # weight name -> b200.PreparedMatrix
         fills = {"x": (1.0, 0.0), "w_qkv": (0.125, 0.0), "w_o": (0.125, 0.0), "w_1": (0.125, 0.0),
                  "w_2": (0.0625, 0.0), "b_qkv": (0.25, 0.0), "b_o": (0.25, 0.0), "b_1": (0.25, 0.0),
                  "b_2": (0.25, 0.0), "beta1": (0.25, 0.0), "beta2": (0.25, 0.0)}
@@ -65,6 +69,19 @@ class EncoderBlock:
                                                              strides)
         return desc
 
+    def prepare_weights(self):
+        """Prepare the projection weights once; later runs skip their split passes.
+        A weight written after this is not seen by the projections (prepare again)."""
+        self.release_prepared()
+        for name in ("w_qkv", "w_o", "w_1", "w_2"):
+            k, n = self.shapes[name]
+            self.prepared[name] = b200.PreparedMatrix(self.ops.queue, self.ops.module, self.context, self.d(name),
+                                                      k=k, n=n)
+
+    def release_prepared(self):
+        while self.prepared:
+            self.prepared.popitem()[1].close()
+
     def flops(self):
         """GEMM flops of one block (projections, scores, P V, MLP)."""
         T, D, H, F, DH = self.T, self.D, self.H, self.F, self.DH
@@ -76,11 +93,16 @@ class EncoderBlock:
         T, D, H, F, DH = self.T, self.D, self.H, self.F, self.DH
 
         def dense(a, w, bias, out, pre, n, k, activation=Activation.NONE):
+            prepared = self.prepared.get(w)
+            if fused and prepared:
+                return [b200.matmul_prepared_bias_activation_into(q, m, d(a), prepared.descriptor, d(out), d(bias),
+                                                                  m=T, n=n, k=k, activation=activation)]
             if fused:
                 return [b200.matmul_bias_activation_into(q, m, d(a), d(w), d(out), d(bias), m=T, n=n, k=k,
                                                          activation=activation)]
-            return [matmul_into(q, m, d(a), d(w), d(pre), m=T, n=n, k=k),
-                    bias_activation_into(q, m, d(pre), d(bias), d(out), activation=activation)]
+            product = (b200.matmul_prepared_into(q, m, d(a), prepared.descriptor, d(pre), m=T, n=n, k=k)
+                       if prepared else matmul_into(q, m, d(a), d(w), d(pre), m=T, n=n, k=k))
+            return [product, bias_activation_into(q, m, d(pre), d(bias), d(out), activation=activation)]
 
         events = [layer_norm_into(q, m, d("x"), d("gamma1"), d("beta1"), d("ln1"), epsilon=self.epsilon)]
         events += dense("ln1", "w_qkv", "b_qkv", "qkv_b", "qkv", 3 * D, D)
@@ -104,5 +126,6 @@ class EncoderBlock:
         return np.frombuffer(self.buf[name].read(), np.float32).reshape(self.shapes[name]).copy()
 
     def close(self):
+        self.release_prepared()
         for b in self.buf.values():
             b.close()

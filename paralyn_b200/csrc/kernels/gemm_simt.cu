@@ -661,6 +661,13 @@ void launch_matmul_bias_activation(Launch &L) {
   run_matmul(L, has_bias ? &L.args[8] : nullptr, L.args[9].u32());
 }
 
+// pr_b200_matmul_prepared_bias_activation_f32: the fused launch's arguments with B's
+// prepared form in place of B (transpose_b = 0).
+void launch_matmul_prepared_bias_activation(Launch &L) {
+  const bool has_bias = L.args[10].u32() != 0;
+  run_matmul(L, has_bias ? &L.args[8] : nullptr, L.args[9].u32(), true);
+}
+
 namespace {
 // Highest element index + 1 of a strided [d0, d1, d2] operand (all extents > 0).
 uint64_t extent(uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s0, uint64_t s1, uint64_t s2) {

@@ -865,6 +865,7 @@ void launch_matmul_bias_activation(Launch &);
 void launch_gather_rows(Launch &);
 void launch_matmul_prepare(Launch &);
 void launch_matmul_prepared(Launch &);
+void launch_matmul_prepared_bias_activation(Launch &);
 
 namespace {
 // Binds operands as raw device ranges of one submitted command (for entries that
@@ -1050,6 +1051,73 @@ PB_EXPORT pr_status pr_b200_matmul_prepared_f32(pr_queue queue, pr_module operat
       for (uint64_t v : {op->m, op->n, op->k, uint64_t(op->transpose_a), uint64_t(0)})
         d.bits(uint32_t(v));
       *out = submit_command(queue, "b200_matmul_prepared_f32", launch_matmul_prepared,
+                            Dim3{uint32_t((op->n + kTile - 1) / kTile), uint32_t((op->m + kTile - 1) / kTile), 1},
+                            Dim3{kTile, kTile, 1}, std::move(d.args), std::move(d.retained));
+    }));
+  });
+}
+
+// C = activation(op(A) B + bias[column]) with B's prepared form in op->b: the
+// prepared product's record and rules plus the optional bias [n] (checked with the
+// operands) and the activation (checked with the record's scalars), as
+// pr_b200_matmul_bias_activation_f32 adds them to pr_matmul_f32's. Results equal
+// pr_b200_matmul_bias_activation_f32 with the B the tensor was prepared from.
+PB_EXPORT pr_status pr_b200_matmul_prepared_bias_activation_f32(pr_queue queue, pr_module operators,
+                                                                const pr_matmul_v1 *op,
+                                                                const pr_tensor_desc_v1 *bias, uint32_t activation,
+                                                                pr_event *out) {
+  static const Rules<pr_matmul_v1> rules = [] {
+    Rules<pr_matmul_v1> r = matmul_rules();
+    r.operation = "matmul_prepared_bias_activation_f32";
+    r.operands[1] = {"prepared", 1};
+    r.operands.push_back({"bias", 1, Layout::row_major, false, true});
+    r.scalars = [](const pr_matmul_v1 &m) {
+      matmul_rules().scalars(m);
+      if (m.transpose_b)
+        reject(PR_INVALID_ARGUMENT, "A prepared operand is used as prepared: transpose_b must be 0");
+    };
+    r.shapes = [](const pr_matmul_v1 &m, const std::vector<Operand> &o) {
+      bounded_dims({m.m, m.n, m.k}, "Matmul");
+      if (m.transpose_a)
+        expect_shape(o[0], {m.k, m.m}, "A (stored transposed as [k,m])");
+      else
+        expect_shape(o[0], {m.m, m.k}, "A [m,k]");
+      expect_prepared(o[1], m.k, m.n);
+      expect_shape(o[2], {m.m, m.n}, "C [m,n]");
+      if (o[3].desc)
+        expect_shape(o[3], {m.n}, "bias");
+    };
+    return r;
+  }();
+  return guarded(rules.operation, [&] {
+    if (!out)
+      reject(PR_INVALID_ARGUMENT, "Missing event output");
+    *out = 0;
+    check_header(op, rules.record);
+    rules.scalars(*op);
+    if (!known_activation(activation))
+      reject(PR_INVALID_ARGUMENT, "Unknown activation");
+    std::vector<Operand> operands(4);
+    const pr_tensor_desc_v1 *descs[4] = {op->a, op->b, op->c, bias};
+    for (int i = 0; i < 4; ++i)
+      operands[i] = Operand{descs[i], {}, rules.operands[i].label, rules.operands[i].output};
+    check_operands(rules, *op, operands, queue, operators);
+    verify_entry(operators, "paralyn_matmul_f32");
+    if (!op->m)
+      return;
+    forward(api("matmul_prepared_bias_activation_f32", [&] {
+      const QueueAccess q = queue_access(queue);
+      DirectArguments d{q, {}, {}};
+      d.tensor(operands[0], false);
+      d.tensor(operands[1], false);
+      d.tensor(operands[2], true);
+      for (uint64_t v : {op->m, op->n, op->k, uint64_t(op->transpose_a), uint64_t(0)})
+        d.bits(uint32_t(v));
+      d.tensor(operands[3], false);
+      d.bits(activation);
+      d.bits(bias ? 1u : 0u);
+      *out = submit_command(queue, "b200_matmul_prepared_bias_activation_f32",
+                            launch_matmul_prepared_bias_activation,
                             Dim3{uint32_t((op->n + kTile - 1) / kTile), uint32_t((op->m + kTile - 1) / kTile), 1},
                             Dim3{kTile, kTile, 1}, std::move(d.args), std::move(d.retained));
     }));

@@ -207,7 +207,7 @@ B200_SYMBOLS = ("pr_b200_matmul_mode_set", "pr_b200_matmul_mode_get", "pr_b200_f
                 "pr_b200_buffer_read_async", "pr_b200_host_register", "pr_b200_host_unregister",
                 "pr_b200_selftest_bounded_wait", "pr_b200_matmul_bias_activation_f32", "pr_b200_gather_rows_f32",
                 "pr_b200_matmul_prepared_bytes", "pr_b200_matmul_prepare_f32", "pr_b200_matmul_prepared_f32",
-                "pr_b200_queue_hold")
+                "pr_b200_matmul_prepared_bias_activation_f32", "pr_b200_queue_hold")
 
 
 def _ctype(kind, records):

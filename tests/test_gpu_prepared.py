@@ -1,11 +1,14 @@
-"""Prepared right-hand operands (pr_b200_matmul_prepare_f32 / _prepared_f32) on a device.
+"""Prepared right-hand operands (pr_b200_matmul_prepare_f32 / _prepared_f32 /
+_prepared_bias_activation_f32) on a device.
 
 A product from B's prepared form must equal pr_matmul_f32 with that B bit for bit in
 every matmul mode (the reference order against the oracle as well), through each
 kernel form the shape selects: the SIMT kernels (small shapes, FFMA, REFERENCE), the
 one-SM tensor-core kernel with the split pass over A or A converted in shared memory,
 the transposed form (n <= 128), and the CTA-pair kernel (m >= 256, n > 128). Infinities
-of B propagate in AUTO as through pr_matmul_f32. A tensor prepared for another (k, n),
+of B propagate in AUTO as through pr_matmul_f32. The fused form (bias and activation in
+the GEMM epilogue) equals pr_b200_matmul_bias_activation_f32 with that B bit for bit the
+same way. A tensor prepared for another (k, n),
 or never prepared, fails the command when it runs; the host-side checks reject wrong
 sizes, alignments and flags before anything is enqueued.
 """
@@ -115,6 +118,67 @@ def test_chain_with_prepared_weights_equals_the_plain_chain(context):
     assert results[0] == results[1]
 
 
+def fused_products(context, a, b, bias, m, n, k, ta, mode, activation):
+    """(pr_b200_matmul_bias_activation_f32 result, prepared-form result, variant) for
+    the same operands, bias (or None), activation and mode."""
+    res = T.operators_of(context)
+    p.set_matmul_mode(context, mode)
+    bufs = [context.buffer(4 * a.size), context.buffer(4 * b.size), context.buffer(4 * n),
+            context.buffer(4 * m * n), context.buffer(4 * m * n)]
+    try:
+        bufs[0].write(a.ravel())
+        bufs[1].write(b.ravel())
+        ad = T.TensorDescriptor(bufs[0], (k, m) if ta else (m, k))
+        bd = T.TensorDescriptor(bufs[1], (k, n))
+        bias_d = None
+        if bias is not None:
+            bufs[2].write(bias)
+            bias_d = T.TensorDescriptor(bufs[2], (n,))
+        plain = b200.matmul_bias_activation_into(res.queue, res.module, ad, bd, T.TensorDescriptor(bufs[3], (m, n)),
+                                                 bias_d, m=m, n=n, k=k, transpose_a=ta, activation=activation)
+        prepared = b200.PreparedMatrix(res.queue, res.module, context, bd, k=k, n=n)
+        try:
+            event = b200.matmul_prepared_bias_activation_into(
+                res.queue, res.module, ad, prepared.descriptor, T.TensorDescriptor(bufs[4], (m, n)), bias_d,
+                m=m, n=n, k=k, transpose_a=ta, activation=activation)
+            event.wait()
+            event.close()
+            variant = b200.last_variant(context, "b200_matmul_prepared_bias_activation_f32")
+        finally:
+            prepared.close()
+        plain.wait()
+        plain.close()
+        want = np.frombuffer(bufs[3].read(), np.float32).reshape(m, n).copy()
+        got = np.frombuffer(bufs[4].read(), np.float32).reshape(m, n).copy()
+        return want, got, variant
+    finally:
+        p.set_matmul_mode(context, p.MatmulMode.AUTO)
+        for buf in bufs:
+            buf.close()
+
+
+# (m, n, k, transpose_a): SIMT, A converted in shared memory, split A stored [k, m],
+# the transposed form, CTA pairs
+FUSED_SHAPES = ((5, 7, 3, False), (300, 129, 64, False), (257, 300, 1000, True), (130, 64, 96, False),
+                (1000, 4096, 512, False))
+
+
+@pytest.mark.parametrize("m,n,k,ta", FUSED_SHAPES)
+def test_prepared_bias_activation_equals_the_fused_product(context, m, n, k, ta):
+    a = synthetic.uniform(7500 + m, 0, m * k).reshape((k, m) if ta else (m, k))
+    b = synthetic.uniform(7600 + n, 0, k * n).reshape(k, n)
+    bias = synthetic.uniform(7700 + n, 0, n)
+    cases = [(mode, T.Activation.GELU_TANH, bias) for mode in MODES] + \
+        [(p.MatmulMode.AUTO, T.Activation.RELU, bias), (p.MatmulMode.AUTO, T.Activation.NONE, None),
+         (p.MatmulMode.TF32X3, T.Activation.GELU_TANH, None)]
+    for mode, activation, bias_values in cases:
+        want, got, variant = fused_products(context, a, b, bias_values, m, n, k, ta, mode, activation)
+        assert got.tobytes() == want.tobytes(), (m, n, k, ta, mode, activation, variant)
+        tensor_cores = (mode == p.MatmulMode.TF32X3 and k >= 16) or \
+            (mode == p.MatmulMode.AUTO and k >= 64 and m * n >= 128 * 256)
+        assert (variant == "tcgen05_tf32x3") == tensor_cores, (m, n, k, mode, variant)
+
+
 # ---- validation ----
 class Calls:
     def __init__(self, context):
@@ -141,6 +205,13 @@ class Calls:
     def product(self, record):
         out = c.c_uint64(99)
         status = self.lib.api.pr_b200_matmul_prepared_f32(self.queue, self.module, c.byref(record), c.byref(out))
+        return status, out.value, self.operation()
+
+    def fused(self, record, bias, activation):
+        out = c.c_uint64(99)
+        status = self.lib.api.pr_b200_matmul_prepared_bias_activation_f32(
+            self.queue, self.module, c.byref(record), c.byref(bias) if bias is not None else None, activation,
+            c.byref(out))
         return status, out.value, self.operation()
 
     def operation(self):
@@ -200,6 +271,21 @@ def test_prepare_and_product_validation(context):
         # no rows: no command and no event
         assert calls.product(record(0, n, k, calls.desc(calls.buf(4), (0, k)), good,
                                     calls.desc(calls.buf(4), (0, n))))[:2] == (S.SUCCESS, 0)
+        # the fused form: the product's rules, then the activation and the bias shape
+        op = "matmul_prepared_bias_activation_f32"
+        bias = calls.desc(calls.buf(4 * n), (n,))
+        assert calls.fused(record(m, n, k, a, good, cc, tb=1), bias, 2) == (S.INVALID_ARGUMENT, 0, op)
+        assert calls.fused(record(m, n, k, a, good, cc), bias, 3) == (S.INVALID_ARGUMENT, 0, op)
+        assert calls.fused(record(m, n, k, a, good, cc), calls.desc(calls.buf(4 * n + 4), (n + 1,)), 2) == \
+            (S.INVALID_ARGUMENT, 0, op)
+        assert calls.fused(record(m, n, k, a, calls.desc(room, (size // 4,), 16), cc), bias, 2)[:2] == \
+            (S.INVALID_ARGUMENT, 0)
+        for with_bias in (bias, None):
+            status, event, _ = calls.fused(record(m, n, k, a, good, cc), with_bias, 2)
+            assert status == S.SUCCESS and event != 0
+            ev = Event._adopt(calls.lib, event)
+            ev.wait()
+            ev.close()
     finally:
         calls.close()
 

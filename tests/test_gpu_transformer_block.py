@@ -224,7 +224,8 @@ def _evidence(context, directory):
 def test_library_block_fused_equals_fifteen_launches(context, causal):
     # paralyn_b200.block.EncoderBlock: the 11-launch form (bias and GELU in the GEMM
     # epilogues) writes exactly the bits of the reference's 15-launch sequence, at a
-    # size where the GEMMs run on the tensor-core kernel (AUTO mode).
+    # size where the GEMMs run on the tensor-core kernel (AUTO mode), and so do both
+    # forms with the projection weights prepared once.
     from paralyn_b200.block import EncoderBlock
     block = EncoderBlock(context, 384, 256, 4, 1024, causal=causal, seed=77)
     try:
@@ -244,6 +245,18 @@ def test_library_block_fused_equals_fifteen_launches(context, causal):
             e.close()
         for name in names:
             assert block.read(name).tobytes() == want[name].tobytes(), name
+        # with the weights prepared once: the same bits in both forms
+        block.prepare_weights()
+        for fused, count in ((True, 11), (False, 15)):
+            for name in names:
+                block.buf[name].write(np.full(int(np.prod(block.shapes[name])), np.nan, np.float32))
+            events = block.run(fused=fused)
+            assert len(events) == count
+            events[-1].wait()
+            for e in events:
+                e.close()
+            for name in names:
+                assert block.read(name).tobytes() == want[name].tobytes(), (name, fused)
         # stage-local check of the fused MLP up-projection against the oracle
         ln2, w1, b1 = block.read("ln2"), block.read("w_1"), block.read("b_1")
         value, _, magnitude = oracle.batched_dot_bound(ln2.ravel(), (0, (0, 256, 1)), w1.ravel(), (0, (0, 1024, 1)),

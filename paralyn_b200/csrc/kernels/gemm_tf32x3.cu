@@ -489,16 +489,26 @@ constexpr int CONVERT_WARPS = 16, CONVERT_THREADS = 32 * CONVERT_WARPS,
 constexpr int STATUS_TIMEOUT_CONVERT = 0x7f3204;
 constexpr int RAW_NONE = 0, RAW_A = 1, RAW_B = 2;
 
-template <int BN> struct Tile {
+// MR: rows of a tile (the MMA's M), 128, or 64 for the transposed form of a C with at
+// most 64 columns: an M = 64 MMA writes D's row r to TMEM lane (r % 16) + 32 (r / 16),
+// the first 16 lanes of each warp's quarter, so no MMA or TMA copy is spent on the 64
+// rows of zero padding an M = 128 tile would carry, and a stage is 40 KB instead of 48.
+template <int BN, int MR = TM> struct Tile {
   static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
+  static_assert(MR == 128 || MR == 64, "M tile");
+  static constexpr int A_BYTES = MR * TK * 4;
   static constexpr int B_BYTES = BN * TK * 4;
   static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
-  static constexpr int STAGES = RING_BYTES / STAGE; // 4, 6 or 8
-  static constexpr uint32_t COLUMNS = BN;            // TMEM columns of one accumulator
-  // D f32, A and B tf32, both K-major, N = BN, M = 128.
+  static constexpr int RING = MR == 64 ? 200 * 1024 : RING_BYTES;
+  static constexpr int STAGES = RING / STAGE; // 4, 6 or 8; 5 for the M = 64 form
+  static constexpr int SMEM = 1024 + RING + BARRIER_BYTES + EPI_WARPS * EPI_STAGE_FLOATS * 4;
+  static constexpr int LANES = MR / 4;        // D rows in each warp's TMEM lane quarter
+  static constexpr uint32_t COLUMNS = BN;     // TMEM columns of one accumulator
+  // D f32, A and B tf32, both K-major, N = BN, M = MR.
   static constexpr uint32_t IDESC =
-      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(TM >> 4) << 24);
+      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(MR >> 4) << 24);
 };
+static_assert(Tile<256, 64>::SMEM <= 227 * 1024, "shared memory of the M = 64 form");
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
   asm volatile(
@@ -507,12 +517,12 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-template <int BN>
+template <int BN, int MR>
 __device__ __forceinline__ void mma_tf32_n(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-      "l"(a), "l"(b), "r"(Tile<BN>::IDESC), "r"(accumulate)
+      "l"(a), "l"(b), "r"(Tile<BN, MR>::IDESC), "r"(accumulate)
       : "memory");
 }
 
@@ -520,16 +530,16 @@ __device__ __forceinline__ float4 tf32_hi(float4 v) {
   return make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
 }
 
-template <int BN, int RAW, bool TOUT>
+template <int BN, int RAW, bool TOUT, int MR = TM>
 __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
     gemm_tf32x3_persistent(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                            const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                            const TileArgs args) {
-  using C = Tile<BN>;
-  constexpr int S = C::STAGES;
+  using C = Tile<BN, MR>;
+  constexpr int S = C::STAGES, A_BYTES = C::A_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + RING_BYTES);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::RING);
   uint64_t *empty = full + S;
   uint64_t *converted = empty + S; // RAW: the stage's raw operand is split in shared memory
   uint64_t *tmem_full = converted + S;
@@ -539,7 +549,7 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile int *issued = abort_flag + 1;   // k-slices the producer has requested
   volatile int *consumed = abort_flag + 2; // k-slices whose data the MMA thread received
-  float *epi_tiles = reinterpret_cast<float *>(smem + RING_BYTES + BARRIER_BYTES);
+  float *epi_tiles = reinterpret_cast<float *>(smem + C::RING + BARRIER_BYTES);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
@@ -548,7 +558,7 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
     const int id = tile % per_batch, group = args.group, per_group = group * args.tiles_n;
     const int first_m = (id / per_group) * group;
     const int rows_in_group = min(group, args.tiles_m - first_m);
-    m0 = (first_m + (id % per_group) % rows_in_group) * TM;
+    m0 = (first_m + (id % per_group) % rows_in_group) * MR;
     n0 = ((id % per_group) / rows_in_group) * BN;
     a_y = z * args.a_rows + m0;
     b_y = z * args.b_rows + n0;
@@ -664,9 +674,9 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
             const uint64_t bl = desc_k_sw64(stage + 2 * A_BYTES + C::B_BYTES + step);
             // Products in the order a_hi b_hi, a_hi b_lo, a_lo b_hi of C's own operands
             // (the transposed form's A is C's B), so both forms give the same bits.
-            mma_tf32_n<BN>(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
-            mma_tf32_n<BN>(acc, TOUT ? al : ah, TOUT ? bh : bl, 1u);
-            mma_tf32_n<BN>(acc, TOUT ? ah : al, TOUT ? bl : bh, 1u);
+            mma_tf32_n<BN, MR>(acc, ah, bh, (kb > kb0 || kk > 0) ? 1u : 0u);
+            mma_tf32_n<BN, MR>(acc, TOUT ? al : ah, TOUT ? bh : bl, 1u);
+            mma_tf32_n<BN, MR>(acc, TOUT ? ah : al, TOUT ? bl : bh, 1u);
           }
           mma_commit(&empty[s]);
         }
@@ -735,25 +745,26 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
       // 128 x BN partial tile (row stride BN), all of it written.
       const bool whole = u < args.full_units;
       float *const c_base = whole ? args.c + int64_t(z) * args.c_batch
-                                  : args.partials + int64_t(u - args.full_units) * (TM * BN);
-      const int64_t ldc = whole ? args.ldc : BN, m_lim = whole ? args.m : TM, n_lim = whole ? args.n : BN;
-      const int64_t row0 = (whole ? int64_t(m0) : 0) + 32 * sub; // this warp's 32 rows
+                                  : args.partials + int64_t(u - args.full_units) * (MR * BN);
+      const int64_t ldc = whole ? args.ldc : BN, m_lim = whole ? args.m : MR, n_lim = whole ? args.n : BN;
+      // This warp's rows: C::LANES (32, or 16 in the M = 64 form) held by its first lanes.
+      const int64_t row0 = (whole ? int64_t(m0) : 0) + C::LANES * sub;
       const int64_t col0 = whole ? int64_t(n0) : 0;
       const int64_t left = m_lim - row0;
-      const int rows_here = left >= 32 ? 32 : (left > 0 ? int(left) : 0);
+      const int rows_here = left >= C::LANES ? C::LANES : (left > 0 ? int(left) : 0);
       float *tile_s = epi_tiles + (warp - 2) * EPI_STAGE_FLOATS;
       const uint32_t acc = tmem + uint32_t(b) * C::COLUMNS + (uint32_t(32 * sub) << 16);
       const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
       for (int col = half * (BN / 2); col < (half + 1) * (BN / 2); col += 16) {
         float v[16];
-        tmem_load_16(acc + uint32_t(col), v); // thread = row 32*sub + lane, 16 columns
+        tmem_load_16(acc + uint32_t(col), v); // lane < C::LANES: row C::LANES*sub + lane, 16 columns
         const int64_t first = col0 + col;
         if (first >= n_lim)
           break; // the remaining columns of the tile are past n
-        if (TOUT && whole) { // D row = C column (the lanes store 32 consecutive C columns)
+        if (TOUT && whole) { // D row = C column (the lanes store consecutive C columns)
           const int64_t c_col = row0 + lane;
-          if (c_col < m_lim) {
+          if (lane < C::LANES && c_col < m_lim) {
             float *cptr = c_base + first * ldc + c_col;
 #pragma unroll
             for (int q = 0; q < 16; ++q)
@@ -1298,13 +1309,13 @@ int64_t round_up(int64_t v, int64_t to) { return (v + to - 1) / to * to; }
 
 // Shared-memory limit of one persistent-kernel form, set once per device (the
 // attribute belongs to the device's context).
-template <int BN, int RAW, bool TOUT> bool configure_persistent(int device) {
+template <int BN, int RAW, bool TOUT, int MR = TM> bool configure_persistent(int device) {
   static bool configured[64] = {};
   if (device < 0 || device >= 64)
     return false;
   if (!configured[device]) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_persistent<BN, RAW, TOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES_PERSISTENT) != cudaSuccess) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_persistent<BN, RAW, TOUT, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Tile<BN, MR>::SMEM) != cudaSuccess) {
       cudaGetLastError();
       return false;
     }
@@ -1337,7 +1348,7 @@ UnitPlan plan_units(int64_t tiles, int sm_count, int k_blocks, int bn, int tile_
   return p;
 }
 
-template <int BN, int RAW, bool TOUT>
+template <int BN, int RAW, bool TOUT, int MR = TM>
 void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
                        float *partials) {
   t.tiles_total = int(tiles);
@@ -1345,10 +1356,10 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
   t.full_units = plan.full_units;
   t.split = plan.split;
   t.partials = partials;
-  gemm_tf32x3_persistent<BN, RAW, TOUT><<<uint32_t(plan.ctas), RAW ? THREADS_RAW_ONE : THREADS_PLAIN, SMEM_BYTES_PERSISTENT,
-                                          L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+  gemm_tf32x3_persistent<BN, RAW, TOUT, MR><<<uint32_t(plan.ctas), RAW ? THREADS_RAW_ONE : THREADS_PLAIN,
+                                              Tile<BN, MR>::SMEM, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
-    split_fixup<BN><<<dim3(TM / (1024 / BN), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);
+    split_fixup<BN, MR><<<dim3(MR / (1024 / BN), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);
     ++L.kernels;
   }
 }
@@ -1414,6 +1425,12 @@ bool pair_enabled() {
 }
 bool pair_raw_enabled() {
   static const bool enabled = env_flag("PARALYN_GEMM_PAIR_RAW");
+  return enabled;
+}
+// The transposed form of a C with at most 64 columns runs 64-row tiles (M = 64 MMAs);
+// PARALYN_GEMM_NARROW=0 keeps it on 128-row tiles, half of them zero padding.
+bool narrow_enabled() {
+  static const bool enabled = env_flag("PARALYN_GEMM_NARROW");
   return enabled;
 }
 // Tile rows per raster group of the pair kernel: the A rows of one group (256 rows
@@ -1501,8 +1518,9 @@ __global__ void __launch_bounds__(256) prepared_transpose(const float *__restric
 }
 
 // The kernel forms: N tile width x (which operand, if any, is split in shared
-// memory), plus the transposed form for narrow C (256 columns, raw B, D = C^T).
-enum class Form { n64, n64_raw_a, n128, n128_raw_a, n256, n256_raw_a, transposed };
+// memory), plus the transposed form for narrow C (256 columns, raw B, D = C^T), with
+// 64-row tiles (M = 64 MMAs) when C has at most 64 columns.
+enum class Form { n64, n64_raw_a, n128, n128_raw_a, n256, n256_raw_a, transposed, transposed64 };
 Form form_of(int bn, bool raw_a) {
   if (bn == 64)
     return raw_a ? Form::n64_raw_a : Form::n64;
@@ -1519,6 +1537,7 @@ bool configure_form(Form f, int device) {
   case Form::n256: return configure_persistent<256, RAW_NONE, false>(device);
   case Form::n256_raw_a: return configure_persistent<256, RAW_A, false>(device);
   case Form::transposed: return configure_persistent<256, RAW_B, true>(device);
+  case Form::transposed64: return configure_persistent<256, RAW_B, true, 64>(device);
   }
   return false;
 }
@@ -1532,6 +1551,7 @@ void launch_form(Form f, Launch &L, const CUtensorMap (&maps)[4], const TileArgs
   case Form::n256: return launch_persistent<256, RAW_NONE, false>(L, maps, t, tiles, plan, partials);
   case Form::n256_raw_a: return launch_persistent<256, RAW_A, false>(L, maps, t, tiles, plan, partials);
   case Form::transposed: return launch_persistent<256, RAW_B, true>(L, maps, t, tiles, plan, partials);
+  case Form::transposed64: return launch_persistent<256, RAW_B, true, 64>(L, maps, t, tiles, plan, partials);
   }
 }
 
@@ -1567,9 +1587,10 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   const bool transposed = raw_a && n <= 128;
   // The kernel's D [dm, dn]: C itself, or C^T in the transposed form.
   const int64_t dm = transposed ? n : m, dn = transposed ? m : n;
+  const bool narrow = transposed && dm <= 64 && narrow_enabled(); // M = 64 tiles
   const int bn = transposed ? 256 : tile_width(n);
   const int64_t k_pad = round_up(k, 32), dn_pad = round_up(dn, bn), tiles_n = dn_pad / bn;
-  Form form = transposed ? Form::transposed : form_of(bn, raw_a && tiles_n <= 2);
+  Form form = transposed ? (narrow ? Form::transposed64 : Form::transposed) : form_of(bn, raw_a && tiles_n <= 2);
   // Wide products run on CTA pairs (256 x 256 tiles), reading A raw when its layout
   // allows (then no split pass runs over A).
   const bool wide = (form == Form::n256 || form == Form::n256_raw_a) && dm >= PAIR_M && pair_enabled();
@@ -1580,7 +1601,7 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   if (pairs)
     form = pair_raw ? Form::n256_raw_a : Form::n256;
   const bool a_split = !transposed && (form == Form::n64 || form == Form::n128 || form == Form::n256);
-  const int64_t m_tile = pairs ? PAIR_M : TM;
+  const int64_t m_tile = pairs ? PAIR_M : (narrow ? 64 : TM);
   const int64_t dm_pad = round_up(dm, m_tile), tiles_m = dm_pad / m_tile, batch_b = sb ? batch : 1;
   // Grid limits of the split passes (rows / 32 in grid.y) and 32-bit TMA row
   // coordinates of the split operands; a raw operand is addressed by its own map.
@@ -1590,10 +1611,10 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
       dm > INT32_MAX || dn > INT32_MAX)
     return false;
   const UnitPlan plan = pairs ? plan_units(tiles_m * tiles_n * batch, pairs, int(k_pad / TK), bn, PAIR_M)
-                              : plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn);
+                              : plan_units(tiles_m * tiles_n * batch, L.sm_count, int(k_pad / TK), bn, int(m_tile));
   // Split operands in the workspace: A's pair [batch * m_pad][k_pad] unless A is
   // converted in shared memory; B's pair [batch_b * rows][k_pad], rows = n_pad
-  // (or, transposed, n padded to 128: the kernel's M side).
+  // (or, transposed, n padded to the tile's 128 or 64 rows: the kernel's M side).
   const int64_t a_rows = a_split ? batch * dm_pad : 0;
   const int64_t b_rows_each = transposed ? dm_pad : dn_pad;
   // A prepared B holds its pair with n_pad (>= b_rows_each) rows of k_pad.
@@ -1621,7 +1642,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   const float *blo = prep ? prep->lo : bhi + batch_b * b_rows_each * k_pad;
   CUtensorMap maps[4];
   if (transposed) { // kernel A = op(B)^T pair, kernel B = raw rows of A
-    if (!make_map(&maps[0], bhi, batch_b * dm_pad, k_pad, TM) || !make_map(&maps[1], blo, batch_b * dm_pad, k_pad, TM) ||
+    if (!make_map(&maps[0], bhi, batch_b * dm_pad, k_pad, uint32_t(m_tile)) ||
+        !make_map(&maps[1], blo, batch_b * dm_pad, k_pad, uint32_t(m_tile)) ||
         !make_raw_map(&maps[2], a, batch, m, k, lda, sa, uint32_t(bn)))
       return false;
     maps[3] = maps[2]; // unused

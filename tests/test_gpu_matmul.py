@@ -133,7 +133,8 @@ def test_matmul_validation(context):
 
 
 @pytest.mark.parametrize("m,n,k", [(2432, 2048, 1024), (4096, 4096, 256), (4096, 4096, 40), (128 * 150, 256, 96),
-                                   (2048, 1024, 1024), (512, 512, 512), (1000, 60, 4000), (5000, 128, 512)])
+                                   (2048, 1024, 1024), (512, 512, 512), (1000, 60, 4000), (5000, 128, 512),
+                                   (300, 64, 4096), (256 * 150, 33, 128)])
 def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
     # Tile counts just above a multiple of the 148 persistent CTAs, or below it: the
     # tiles of the last (or only), mostly idle round are cut into k-ranges whose
@@ -243,11 +244,13 @@ def aligned_matmul(context, a, b, m, n, k, ta):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 1, 16), (16, 16, 16), (129, 65, 260), (257, 100, 96), (300, 129, 64),
-                                   (2048, 64, 2048), (1000, 512, 100), (4096, 200, 1024)])
+                                   (2048, 64, 2048), (1000, 512, 100), (4096, 200, 1024), (777, 48, 520),
+                                   (37888, 64, 64)])
 def test_a_split_in_shared_memory_equals_the_split_pass(context, m, n, k):
     # A stored [m, k] with 16-byte aligned rows is loaded raw and split into its TF32
     # pair inside the GEMM kernel: as the A operand when at most two column tiles
-    # re-read it, as the 256-wide B operand of C^T when n <= 128. Stored [k, m] it goes
+    # re-read it, as the 256-wide B operand of C^T when n <= 128 (on 64-row tiles of
+    # C^T, M = 64 MMAs, when n <= 64). Stored [k, m] it goes
     # through the separate split pass into 128 x BN tiles of C. Same conversion, same
     # products in the same order and, at these sizes, the same k-ranges for the
     # split tail: equal bits. (Where the two tilings cut k differently the partial
@@ -335,7 +338,8 @@ def same_specials_and_contract(c, a, b, m, n, k):
 #   (300, 260, 96): A converted in shared memory (two column tiles), B split
 #   (300, 1000, 96): both operands split
 #   (4096, 100, 96): the transposed form (n <= 128: A's rows converted as the wide side)
-@pytest.mark.parametrize("m,n,k", [(300, 260, 96), (300, 1000, 96), (4096, 100, 96)])
+#   (4096, 64, 96): the same on 64-row tiles (n <= 64: M = 64 MMAs)
+@pytest.mark.parametrize("m,n,k", [(300, 260, 96), (300, 1000, 96), (4096, 100, 96), (4096, 64, 96)])
 @pytest.mark.parametrize("where", ("a", "b", "huge"))
 def test_auto_mode_propagates_infinities_like_the_reference(context, m, n, k, where):
     a = synthetic.uniform(9500, 0, m * k).reshape(m, k)

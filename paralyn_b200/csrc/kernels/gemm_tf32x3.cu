@@ -28,8 +28,10 @@
 //     warps 2-9: epilogue, two warps per TMEM lane quarter (one per column half):
 //       tcgen05.ld 32 lanes x 16 columns, fused bias/ReLU, 128-bit stores staged
 //       through shared memory; then the accumulator is handed back.
-//     warps 10-13 (raw forms only): split the raw box of each stage into its TF32
+//     warps 10-25 (raw forms only): split the raw box of each stage into its TF32
 //       pair in shared memory.
+//     The transposed form of a C with at most 64 columns runs 64-row tiles (M = 64
+//     MMAs, D's row r in TMEM lane (r % 16) + 32 (r / 16)).
 //     A separate kernel adds the partial tiles of split tiles (split_fixup).
 //  3. one-tile GEMM kernel (gemm_tf32x3, 6 warps, one 128x256 tile per CTA) for the
 //     allocation-free entry point at the end of this file.
@@ -478,8 +480,7 @@ __device__ __forceinline__ int stage_index(int r, int c) {
   return r * EPI_PITCH16 + ((((c >> 2) ^ (r >> 1)) & 3) << 2) + (c & 3);
 }
 constexpr int RING_BYTES = 192 * 1024, BARRIER_BYTES = 512;
-constexpr int SMEM_BYTES_PERSISTENT = 1024 + RING_BYTES + BARRIER_BYTES + EPI_WARPS * EPI_STAGE_FLOATS * 4;
-constexpr int THREADS_PLAIN = 64 + 32 * EPI_WARPS, THREADS_RAW = THREADS_PLAIN + 128; // + 4 converter warps
+constexpr int THREADS_PLAIN = 64 + 32 * EPI_WARPS;
 // The one-SM kernel's converter warps, which share each k-slice (the CTA pair keeps
 // four per CTA). A slice's conversion sits on the ring's critical loop (load ->
 // convert -> MMA -> release), so it is spread thin: with four warps the transposed
@@ -909,8 +910,18 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
 // own conversion, so no split pass runs over A. The raw box of a stage completes on
 // the CTA's own `raw_full` barrier; the converters of both CTAs report to CTA 0's
 // `converted` barrier, which the MMA waits for besides `full` (now B's bytes only).
+// The CTA pair's epilogue warps: PAIR_EPI_WARPS / 4 per TMEM lane quarter, each taking
+// that share of the tile's columns (plus four converter warps per CTA in the RAW form).
+// Sixteen sped up the GELU epilogue of the encoder block's MLP up-projection (103 ->
+// 97 us) but slowed the store-bound score products (32 x 2048 x 2048 x 128: 141 -> 131
+// TFLOP/s), so eight stay.
+constexpr int PAIR_EPI_WARPS = 8, PAIR_PARTS = PAIR_EPI_WARPS / 4;
+constexpr int PAIR_THREADS_PLAIN = 64 + 32 * PAIR_EPI_WARPS, PAIR_THREADS_RAW = PAIR_THREADS_PLAIN + 128;
+constexpr int PAIR_SMEM_BYTES = 1024 + RING_BYTES + BARRIER_BYTES + PAIR_EPI_WARPS * EPI_STAGE_FLOATS * 4;
+static_assert(PAIR_SMEM_BYTES <= 227 * 1024, "shared memory of the CTA pair");
+
 template <bool RAW>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : THREADS_PLAIN, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_RAW : PAIR_THREADS_PLAIN, 1)
     gemm_tf32x3_pair(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                      const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                      const TileArgs args) {
@@ -963,7 +974,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : 
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], 2 * EPI_WARPS);
+      mbar_init(&tmem_empty[b], 2 * PAIR_EPI_WARPS);
     }
     mbar_init(drained, 1);
     for (int s = 0; s < S; ++s) {
@@ -1075,8 +1086,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : 
       // Fires once every MMA issued above has finished (both CTAs' TMEM quiet).
       mma_commit_pair(in_cta(drained, 0));
     }
-  } else if (warp >= 2 + EPI_WARPS) { // RAW converter warps 10..13 of both CTAs
-    const int t = threadIdx.x - THREADS_PLAIN;
+  } else if (warp >= 2 + PAIR_EPI_WARPS) { // RAW converter warps (the last four) of both CTAs
+    const int t = threadIdx.x - PAIR_THREADS_PLAIN;
     const uint32_t converted0 = in_cta(converted, 0);
     int g = 0;
     for (int u = pair; u < args.units_total && !*abort_flag; u += pairs) {
@@ -1108,8 +1119,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : 
           arrive_at(converted0 + uint32_t(s) * 8u);
       }
     }
-  } else { // epilogue warps 2..9 of both CTAs: TMEM lanes 32*(warp % 4) .., column half (warp - 2) / 4
-    const int sub = warp % 4, half = (warp - 2) / 4;
+  } else { // epilogue warps of both CTAs: TMEM lanes 32*(warp % 4) .., column part (warp - 2) / 4
+    const int sub = warp % 4, part = (warp - 2) / 4;
     int j = 0;
     for (int u = pair; u < args.units_total; u += pairs, ++j) {
       int tile, kb0, kb1;
@@ -1142,7 +1153,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? THREADS_RAW : 
       const uint32_t acc = tmem + uint32_t(b) * PAIR_COLUMNS + (uint32_t(32 * sub) << 16);
       const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
 #pragma unroll 1
-      for (int col = half * (PAIR_N / 2); col < (half + 1) * (PAIR_N / 2); col += 16) {
+      for (int col = part * (PAIR_N / PAIR_PARTS); col < (part + 1) * (PAIR_N / PAIR_PARTS); col += 16) {
         float v[16];
         tmem_load_16(acc + uint32_t(col), v); // thread = row 32*sub + lane, 16 columns
         const int64_t first = col0 + col;
@@ -1374,14 +1385,14 @@ template <bool RAW> int pair_capacity(int device) {
   if (!known[device]) {
     known[device] = true;
     if (cudaFuncSetAttribute(gemm_tf32x3_pair<RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES_PERSISTENT) != cudaSuccess) {
+                             PAIR_SMEM_BYTES) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(2, 1, 1);
-    config.blockDim = dim3(RAW ? THREADS_RAW : THREADS_PLAIN, 1, 1);
-    config.dynamicSmemBytes = SMEM_BYTES_PERSISTENT;
+    config.blockDim = dim3(RAW ? PAIR_THREADS_RAW : PAIR_THREADS_PLAIN, 1, 1);
+    config.dynamicSmemBytes = PAIR_SMEM_BYTES;
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tf32x3_pair<RAW>, &config) != cudaSuccess) {
       cudaGetLastError();
@@ -1400,10 +1411,10 @@ void launch_pair(Launch &L, bool raw, const CUtensorMap (&maps)[4], TileArgs t, 
   t.split = plan.split;
   t.partials = partials;
   if (raw)
-    gemm_tf32x3_pair<true><<<uint32_t(2 * plan.ctas), THREADS_RAW, SMEM_BYTES_PERSISTENT, L.stream>>>(
+    gemm_tf32x3_pair<true><<<uint32_t(2 * plan.ctas), PAIR_THREADS_RAW, PAIR_SMEM_BYTES, L.stream>>>(
         maps[0], maps[1], maps[2], maps[3], t);
   else
-    gemm_tf32x3_pair<false><<<uint32_t(2 * plan.ctas), THREADS_PLAIN, SMEM_BYTES_PERSISTENT, L.stream>>>(
+    gemm_tf32x3_pair<false><<<uint32_t(2 * plan.ctas), PAIR_THREADS_PLAIN, PAIR_SMEM_BYTES, L.stream>>>(
         maps[0], maps[1], maps[2], maps[3], t);
   if (plan.remaining) {
     split_fixup<PAIR_N, PAIR_M><<<dim3(PAIR_M / (1024 / PAIR_N), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);

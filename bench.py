@@ -716,7 +716,8 @@ def run_ours(args, group):
 DOMINANT_ENTRY = {"chain": ("b200_matmul_prepared_f32", "paralyn_matmul_f32"), "gemm": "paralyn_matmul_f32",
                   "layernorm": "paralyn_layer_norm_f32", "affine": "array_affine_scalar", "add": "array_add",
                   "softmax": "paralyn_softmax_rows_f32", "reduce": "paralyn_reduce_rows_f32",
-                  "attention": "paralyn_batched_matmul_f32", "block": "b200_matmul_bias_activation_f32"}
+                  "attention": "paralyn_batched_matmul_f32",
+                  "block": ("b200_matmul_prepared_bias_activation_f32", "b200_matmul_bias_activation_f32")}
 
 
 def last_variant(ctx, workload):

@@ -82,3 +82,16 @@ def test_group_control_plane_over_gloo():
         assert proc.exitcode == 0
     for rank in range(2):
         assert got[rank] == (11.0, [{"rank": 0}, {"rank": 1}])
+
+
+def test_dominant_entries_name_commands_the_library_records():
+    # The roofline's bound follows the variant recorded for the workload's dominant
+    # command; a name that no command carries would silently pick the wrong bound.
+    sys.path.insert(0, str(ROOT))
+    import bench
+    # provider commands are named in the runtime, array kernels in the module builder
+    files = list((ROOT / "paralyn_b200" / "csrc" / "runtime").glob("*.cpp")) + [ROOT / "paralyn_b200" / "prk.py"]
+    sources = "".join(p.read_text() for p in files)
+    for workload, entries in bench.DOMINANT_ENTRY.items():
+        for entry in (entries,) if isinstance(entries, str) else entries:
+            assert f'"{entry}"' in sources, (workload, entry)

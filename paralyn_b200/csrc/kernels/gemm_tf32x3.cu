@@ -282,6 +282,12 @@ struct TileArgs {
   // rows, so they share B's tiles in L2); the persistent kernels and split_fixup
   // read it, the one-tile kernel uses 8.
   int group = 8;
+  // CTA-pair kernel, optional: one zeroed counter per round of whole tiles. Before a
+  // round's loads each pair's producer arrives and waits until the round's other
+  // pairs have arrived or wave_wait_ns have passed (then it goes on: the wait only
+  // keeps the pairs' k-streams of one round together, for L2 reuse).
+  int *wave_count = nullptr;
+  long long wave_wait_ns = 0;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -510,6 +516,12 @@ template <int BN, int MR = TM> struct Tile {
       (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(MR >> 4) << 24);
 };
 static_assert(Tile<256, 64>::SMEM <= 227 * 1024, "shared memory of the M = 64 form");
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
   asm volatile(
@@ -1008,6 +1020,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_R
         int tile, kb0, kb1, m0, n0, z;
         unit(u, tile, kb0, kb1);
         locate(tile, m0, n0, z);
+        if (leader && args.wave_count && u >= pairs && u < args.full_units) { // bounded, never fails
+          const int wave = u / pairs, members = min(pairs, args.full_units - wave * pairs);
+          int *count = args.wave_count + wave;
+          atomicAdd(count, 1);
+          const unsigned long long t0 = global_ns();
+          while (*reinterpret_cast<volatile int *>(count) < members &&
+                 global_ns() - t0 < static_cast<unsigned long long>(args.wave_wait_ns))
+            __nanosleep(256);
+        }
         const int a_y = z * args.a_rows + m0 + int(rank) * PAIR_HALF;
         const int b_y = z * args.b_rows + n0 + int(rank) * PAIR_HALF;
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
@@ -1438,6 +1459,16 @@ bool pair_raw_enabled() {
   static const bool enabled = env_flag("PARALYN_GEMM_PAIR_RAW");
   return enabled;
 }
+// Longest wait (ns) of the CTA pairs' round alignment: PARALYN_GEMM_WAVE_WAIT_US
+// (microseconds, at most 10000; 0 turns the alignment off), default 50.
+long long pair_wave_wait_ns() {
+  static const long long ns = [] {
+    const char *v = std::getenv("PARALYN_GEMM_WAVE_WAIT_US");
+    const long long us = v ? std::atoll(v) : 50;
+    return us > 0 && us <= 10000 ? us * 1000 : 0;
+  }();
+  return ns;
+}
 // The transposed form of a C with at most 64 columns runs 64-row tiles (M = 64 MMAs);
 // PARALYN_GEMM_NARROW=0 keeps it on 128-row tiles, half of them zero padding.
 bool narrow_enabled() {
@@ -1632,7 +1663,15 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   const size_t split_bytes = size_t(8) * size_t(k_pad) * size_t(a_rows + (prep ? 0 : batch_b * b_rows_each));
   // After the split operands and the partial tiles: the non-finite flag word (8 bytes;
   // both regions are multiples of 8 bytes).
-  const size_t bytes = split_bytes + plan.partial_bytes + (watch ? 8 : 0);
+  // Then, for the CTA pairs' round alignment, one counter per round of whole tiles.
+  // Deep products only (k >= 2048: a round then lasts ~70 us or more and reads its
+  // operands from DRAM): on the 65536 x 4096 x 4096 chain it cut the GEMM's DRAM
+  // traffic from 17.6 to 11.4 GB a launch, which under the power cap bought SM clock
+  // (227 -> 237 TFLOP/s); shallow products with short rounds (k = 128, k = 1024) lost
+  // 2-7 % to the waits.
+  const bool align_waves = pairs && pair_wave_wait_ns() && k_pad >= 2048;
+  const int64_t wave_slots = align_waves ? (plan.full_units + pairs - 1) / pairs + 1 : 0;
+  const size_t bytes = split_bytes + plan.partial_bytes + (watch || wave_slots ? 8 : 0) + size_t(wave_slots) * 4;
   if (L.dry_run)
     return true;
   auto *scratch = static_cast<float *>(L.workspace(L.workspace_owner, bytes));
@@ -1718,6 +1757,12 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   t.epoch = epoch;
   if (pairs)
     t.group = pair_group(pair_raw);
+  if (wave_slots) {
+    t.wave_count = reinterpret_cast<int *>(reinterpret_cast<char *>(scratch) + split_bytes + plan.partial_bytes + 8);
+    t.wave_wait_ns = pair_wave_wait_ns();
+    if (cudaMemsetAsync(t.wave_count, 0, size_t(wave_slots) * 4, L.stream) != cudaSuccess)
+      return false;
+  }
   ++L.kernels;
   if (pairs)
     launch_pair(L, pair_raw, maps, t, tiles_m * tiles_n * batch, plan, partials);

@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // One CTA per SM walks work units (whole tiles, then k-ranges of the tiles of a
 // short last round). The N tile width BN is 64, 128 or 256 (the narrow tiles keep
 // the tensor cores off padding when n is small); every form uses a 192 KB ring of
-// 16-deep k-slices. With RAW = RAW_A (RAW_B) the producer loads raw FP32 boxes of
+// 16-deep k-slices (200 KB for the 64-row transposed form). With RAW = RAW_A (RAW_B) the producer loads raw FP32 boxes of
 // the A (B) operand and sixteen converter warps split them into the hi/lo pair in
 // shared memory with the same conversion as split_tf32 (so the operands, and the
 // result, are bit-identical), which saves the split pass over that operand when
@@ -863,6 +863,9 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
 //    report to CTA 0's `tmem_empty` (16 arrivals: eight warps of each CTA).
 // Every wait is bounded. Before either CTA releases its shared and tensor memory,
 // CTA 0 waits for its last MMA to finish and both CTAs meet at a cluster barrier.
+// Deep products (k >= 2048) align the pairs' rounds: CTA 0's producer waits (at most
+// TileArgs::wave_wait_ns) for the round's other pairs before loading its tile, so the
+// tiles of one round stream the same k-slices of X and W at about the same time.
 constexpr int PAIR_HALF = 128, PAIR_M = 2 * PAIR_HALF, PAIR_N = 256;
 constexpr int PAIR_A_BYTES = PAIR_HALF * TK * 4, PAIR_B_BYTES = PAIR_HALF * TK * 4;
 constexpr int PAIR_STAGE = 2 * PAIR_A_BYTES + 2 * PAIR_B_BYTES; // 32 KB per CTA

@@ -433,3 +433,47 @@ def test_tma_fed_simt_kernel_ffma_contract(context, ta):
             assert np.all(np.abs(c.astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))
     finally:
         p.set_matmul_mode(context, p.MatmulMode.AUTO)
+
+
+ALIGNED_PRODUCT = """
+import hashlib, sys
+import numpy as np
+import paralyn_b200 as p
+from paralyn_b200 import synthetic
+m, n, k = 4096, 4096, 2048
+with p.Context("cuda:0") as ctx:
+    p.set_matmul_mode(ctx, p.MatmulMode.TF32X3)
+    a, b = synthetic.uniform(9700, 0, m * k), synthetic.uniform(9701, 0, k * n)
+    with p.tensor(a, shape=(m, k), context=ctx) as ta, p.tensor(b, shape=(k, n), context=ctx) as tb, \\
+            p.matmul(ta, tb) as tc:
+        c = np.asarray(tc.to_host(), np.float32)
+    rows = np.arange(0, m, 251)
+    print(hashlib.sha256(c.tobytes()).hexdigest(), ",".join(map(str, rows)))
+    np.save(sys.argv[1], c.reshape(m, n)[rows])
+"""
+
+
+def test_round_alignment_changes_no_bits(tmp_path):
+    # The CTA pairs' round alignment (products with k >= 2048: 256 tiles of 256 x 256
+    # here, three rounds and a split tail on 74 pairs) only delays producers; the same
+    # product with it off (PARALYN_GEMM_WAVE_WAIT_US=0, read once per process) and at
+    # its default gives the same bits, and sampled rows meet the FP32 contract.
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    digests = []
+    for wait in ("0", "50"):
+        env = dict(os.environ, PARALYN_GEMM_WAVE_WAIT_US=wait)
+        out = subprocess.run([sys.executable, "-c", ALIGNED_PRODUCT, str(tmp_path / f"rows{wait}.npy")], env=env,
+                             cwd=root, capture_output=True, text=True, timeout=600)
+        assert out.returncode == 0, out.stderr[-2000:]
+        digests.append(out.stdout.split()[0])
+    assert digests[0] == digests[1]
+    m, n, k = 4096, 4096, 2048
+    rows = np.arange(0, m, 251)
+    got = np.load(tmp_path / "rows50.npy")
+    a, b = synthetic.uniform(9700, 0, m * k).reshape(m, k), synthetic.uniform(9701, 0, k * n)
+    exact, magnitude = oracle.matmul_exact(a[rows].ravel(), b, len(rows), n, k)
+    assert np.all(np.abs(got.astype(np.float64) - exact) <= oracle.matmul_tolerance(magnitude, k))

@@ -288,6 +288,9 @@ struct TileArgs {
   // keeps the pairs' k-streams of one round together, for L2 reuse).
   int *wave_count = nullptr;
   long long wave_wait_ns = 0;
+  // CTA-pair kernel and its fixup: with col_group > 0 consecutive tiles walk the rows
+  // of `col_group` column tiles instead (group is then unused).
+  int col_group = 0;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -963,7 +966,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_R
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
   auto locate = [&](int tile, int &m0, int &n0, int &z) { // m0 in rows of PAIR_M tiles
     z = tile / per_batch;
-    const int id = tile % per_batch, group = args.group, per_group = group * args.tiles_n;
+    const int id = tile % per_batch;
+    if (args.col_group > 0) {
+      const int group = args.col_group, per_group = group * args.tiles_m;
+      const int first_n = (id / per_group) * group;
+      const int cols_in_group = min(group, args.tiles_n - first_n);
+      n0 = (first_n + (id % per_group) % cols_in_group) * PAIR_N;
+      m0 = ((id % per_group) / cols_in_group) * PAIR_M;
+      return;
+    }
+    const int group = args.group, per_group = group * args.tiles_n;
     const int first_m = (id / per_group) * group;
     const int rows_in_group = min(group, args.tiles_m - first_m);
     m0 = (first_m + (id % per_group) % rows_in_group) * PAIR_M;
@@ -1256,11 +1268,21 @@ template <int BN, int TMR = TM> __global__ void __launch_bounds__(256) split_fix
   const int j = 4 * (threadIdx.x % PER_ROW);                    // first of four columns
   const int tile = args.full_units + t;
   const int per_batch = args.tiles_per_batch ? args.tiles_per_batch : args.tiles_m * args.tiles_n;
-  const int z = tile / per_batch, id = tile % per_batch, group = args.group, per_group = group * args.tiles_n;
-  const int first_m = (id / per_group) * group;
-  const int rows_in_group = min(group, args.tiles_m - first_m);
-  const int64_t row = int64_t(first_m + (id % per_group) % rows_in_group) * TMR + i;
-  const int64_t col = int64_t((id % per_group) / rows_in_group) * BN + j;
+  const int z = tile / per_batch, id = tile % per_batch;
+  int64_t row, col;
+  if (args.col_group > 0) { // the CTA pair's column-group raster
+    const int group = args.col_group, per_group = group * args.tiles_m;
+    const int first_n = (id / per_group) * group;
+    const int cols_in_group = min(group, args.tiles_n - first_n);
+    col = int64_t(first_n + (id % per_group) % cols_in_group) * BN + j;
+    row = int64_t((id % per_group) / cols_in_group) * TMR + i;
+  } else {
+    const int group = args.group, per_group = group * args.tiles_n;
+    const int first_m = (id / per_group) * group;
+    const int rows_in_group = min(group, args.tiles_m - first_m);
+    row = int64_t(first_m + (id % per_group) % rows_in_group) * TMR + i;
+    col = int64_t((id % per_group) / rows_in_group) * BN + j;
+  }
   if (row >= args.m || col >= args.n)
     return;
   const float4 *p =
@@ -1461,6 +1483,19 @@ bool pair_enabled() {
 bool pair_raw_enabled() {
   static const bool enabled = env_flag("PARALYN_GEMM_PAIR_RAW");
   return enabled;
+}
+// Deep products (k >= 2048) on CTA pairs walk the rows of groups of column tiles:
+// a round of 74 pairs then covers about 9 tile-rows x 8 column tiles, against 4.6
+// tile-rows x all 16 column tiles of W for two-row groups, and the chain's GEMM read
+// 8.5 GB instead of 10.5 (rounds aligned) and ran 1 % faster under the power cap.
+// PARALYN_GEMM_COL_GROUP (1..64) overrides the 8 column tiles; 0 keeps row groups.
+int pair_col_group() {
+  static const int g = [] {
+    const char *v = std::getenv("PARALYN_GEMM_COL_GROUP");
+    const int c = v ? std::atoi(v) : 8;
+    return c >= 0 && c <= 64 ? c : 8;
+  }();
+  return g;
 }
 // Longest wait (ns) of the CTA pairs' round alignment: PARALYN_GEMM_WAVE_WAIT_US
 // (microseconds, at most 10000; 0 turns the alignment off), default 50.
@@ -1672,7 +1707,8 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // traffic from 17.6 to 11.4 GB a launch, which under the power cap bought SM clock
   // (227 -> 237 TFLOP/s); shallow products with short rounds (k = 128, k = 1024) lost
   // 2-7 % to the waits.
-  const bool align_waves = pairs && pair_wave_wait_ns() && k_pad >= 2048;
+  const bool deep = pairs && k_pad >= 2048;
+  const bool align_waves = deep && pair_wave_wait_ns();
   const int64_t wave_slots = align_waves ? (plan.full_units + pairs - 1) / pairs + 1 : 0;
   const size_t bytes = split_bytes + plan.partial_bytes + (watch || wave_slots ? 8 : 0) + size_t(wave_slots) * 4;
   if (L.dry_run)
@@ -1758,8 +1794,10 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   t.transposed = transposed;
   t.nonfinite = flag;
   t.epoch = epoch;
-  if (pairs)
+  if (pairs) {
     t.group = pair_group(pair_raw);
+    t.col_group = deep ? pair_col_group() : 0;
+  }
   if (wave_slots) {
     t.wave_count = reinterpret_cast<int *>(reinterpret_cast<char *>(scratch) + split_bytes + plan.partial_bytes + 8);
     t.wave_wait_ns = pair_wave_wait_ns();

@@ -928,18 +928,22 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
 // own conversion, so no split pass runs over A. The raw box of a stage completes on
 // the CTA's own `raw_full` barrier; the converters of both CTAs report to CTA 0's
 // `converted` barrier, which the MMA waits for besides `full` (now B's bytes only).
-// The CTA pair's epilogue warps: PAIR_EPI_WARPS / 4 per TMEM lane quarter, each taking
-// that share of the tile's columns (plus four converter warps per CTA in the RAW form).
-// Sixteen sped up the GELU epilogue of the encoder block's MLP up-projection (103 ->
-// 97 us) but slowed the store-bound score products (32 x 2048 x 2048 x 128: 141 -> 131
-// TFLOP/s), so eight stay.
-constexpr int PAIR_EPI_WARPS = 8, PAIR_PARTS = PAIR_EPI_WARPS / 4;
-constexpr int PAIR_THREADS_PLAIN = 64 + 32 * PAIR_EPI_WARPS, PAIR_THREADS_RAW = PAIR_THREADS_PLAIN + 128;
-constexpr int PAIR_SMEM_BYTES = 1024 + RING_BYTES + BARRIER_BYTES + PAIR_EPI_WARPS * EPI_STAGE_FLOATS * 4;
-static_assert(PAIR_SMEM_BYTES <= 227 * 1024, "shared memory of the CTA pair");
+// The CTA pair's epilogue warps: EW / 4 per TMEM lane quarter, each taking that share
+// of the tile's columns (plus four converter warps per CTA in the RAW form). Sixteen
+// (EW = 16) when a bias or activation is fused: they sped up the encoder block's GELU
+// up-projection from 103 to 97 us and its QKV projection from 82 to 79; without an
+// epilogue computation eight, since sixteen slowed the store-bound score products
+// (32 x 2048 x 2048 x 128: 141 -> 131 TFLOP/s).
+template <int EW> struct PairShape {
+  static_assert(EW == 8 || EW == 16, "epilogue warps");
+  static constexpr int PARTS = EW / 4;
+  static constexpr int THREADS_PLAIN = 64 + 32 * EW, THREADS_RAW = THREADS_PLAIN + 128;
+  static constexpr int SMEM = 1024 + RING_BYTES + BARRIER_BYTES + EW * EPI_STAGE_FLOATS * 4;
+  static_assert(SMEM <= 227 * 1024, "shared memory of the CTA pair");
+};
 
-template <bool RAW>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_RAW : PAIR_THREADS_PLAIN, 1)
+template <bool RAW, int EW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PairShape<EW>::THREADS_RAW : PairShape<EW>::THREADS_PLAIN, 1)
     gemm_tf32x3_pair(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                      const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                      const TileArgs args) {
@@ -1001,7 +1005,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_R
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], 2 * PAIR_EPI_WARPS);
+      mbar_init(&tmem_empty[b], 2 * EW);
     }
     mbar_init(drained, 1);
     for (int s = 0; s < S; ++s) {
@@ -1122,8 +1126,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_R
       // Fires once every MMA issued above has finished (both CTAs' TMEM quiet).
       mma_commit_pair(in_cta(drained, 0));
     }
-  } else if (warp >= 2 + PAIR_EPI_WARPS) { // RAW converter warps (the last four) of both CTAs
-    const int t = threadIdx.x - PAIR_THREADS_PLAIN;
+  } else if (warp >= 2 + EW) { // RAW converter warps (the last four) of both CTAs
+    const int t = threadIdx.x - PairShape<EW>::THREADS_PLAIN;
     const uint32_t converted0 = in_cta(converted, 0);
     int g = 0;
     for (int u = pair; u < args.units_total && !*abort_flag; u += pairs) {
@@ -1188,8 +1192,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(RAW ? PAIR_THREADS_R
       float *tile_s = epi_tiles + (warp - 2) * EPI_STAGE_FLOATS;
       const uint32_t acc = tmem + uint32_t(b) * PAIR_COLUMNS + (uint32_t(32 * sub) << 16);
       const bool vec_c = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c_base) & 15u) == 0);
+      constexpr int PART_COLUMNS = PAIR_N / PairShape<EW>::PARTS;
 #pragma unroll 1
-      for (int col = part * (PAIR_N / PAIR_PARTS); col < (part + 1) * (PAIR_N / PAIR_PARTS); col += 16) {
+      for (int col = part * PART_COLUMNS; col < (part + 1) * PART_COLUMNS; col += 16) {
         float v[16];
         tmem_load_16(acc + uint32_t(col), v); // thread = row 32*sub + lane, 16 columns
         const int64_t first = col0 + col;
@@ -1423,24 +1428,24 @@ void launch_persistent(Launch &L, const CUtensorMap (&maps)[4], TileArgs t, int6
 
 // CTA pairs the device can hold at once with the pair kernel's shared memory (the
 // persistent grid), set up once per device; 0 when the pair kernel cannot run.
-template <bool RAW> int pair_capacity(int device) {
+template <bool RAW, int EW> int pair_capacity(int device) {
   static int capacity[64] = {};
   static bool known[64] = {};
   if (device < 0 || device >= 64)
     return 0;
   if (!known[device]) {
     known[device] = true;
-    if (cudaFuncSetAttribute(gemm_tf32x3_pair<RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             PAIR_SMEM_BYTES) != cudaSuccess) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_pair<RAW, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PairShape<EW>::SMEM) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(2, 1, 1);
-    config.blockDim = dim3(RAW ? PAIR_THREADS_RAW : PAIR_THREADS_PLAIN, 1, 1);
-    config.dynamicSmemBytes = PAIR_SMEM_BYTES;
+    config.blockDim = dim3(RAW ? PairShape<EW>::THREADS_RAW : PairShape<EW>::THREADS_PLAIN, 1, 1);
+    config.dynamicSmemBytes = PairShape<EW>::SMEM;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tf32x3_pair<RAW>, &config) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tf32x3_pair<RAW, EW>, &config) != cudaSuccess) {
       cudaGetLastError();
       clusters = 0;
     }
@@ -1449,6 +1454,10 @@ template <bool RAW> int pair_capacity(int device) {
   return capacity[device];
 }
 
+// Epilogue warps per CTA of the pair: 16 when the epilogue adds a bias or applies an
+// activation, else 8.
+int pair_epilogue_warps(const TileArgs &t) { return t.bias || t.activation ? 16 : 8; }
+
 void launch_pair(Launch &L, bool raw, const CUtensorMap (&maps)[4], TileArgs t, int64_t tiles, const UnitPlan &plan,
                  float *partials) {
   t.tiles_total = int(tiles);
@@ -1456,12 +1465,20 @@ void launch_pair(Launch &L, bool raw, const CUtensorMap (&maps)[4], TileArgs t, 
   t.full_units = plan.full_units;
   t.split = plan.split;
   t.partials = partials;
-  if (raw)
-    gemm_tf32x3_pair<true><<<uint32_t(2 * plan.ctas), PAIR_THREADS_RAW, PAIR_SMEM_BYTES, L.stream>>>(
-        maps[0], maps[1], maps[2], maps[3], t);
-  else
-    gemm_tf32x3_pair<false><<<uint32_t(2 * plan.ctas), PAIR_THREADS_PLAIN, PAIR_SMEM_BYTES, L.stream>>>(
-        maps[0], maps[1], maps[2], maps[3], t);
+  const uint32_t grid = uint32_t(2 * plan.ctas);
+  if (pair_epilogue_warps(t) == 16) {
+    using P = PairShape<16>;
+    if (raw)
+      gemm_tf32x3_pair<true, 16><<<grid, P::THREADS_RAW, P::SMEM, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+    else
+      gemm_tf32x3_pair<false, 16><<<grid, P::THREADS_PLAIN, P::SMEM, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+  } else {
+    using P = PairShape<8>;
+    if (raw)
+      gemm_tf32x3_pair<true, 8><<<grid, P::THREADS_RAW, P::SMEM, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+    else
+      gemm_tf32x3_pair<false, 8><<<grid, P::THREADS_PLAIN, P::SMEM, L.stream>>>(maps[0], maps[1], maps[2], maps[3], t);
+  }
   if (plan.remaining) {
     split_fixup<PAIR_N, PAIR_M><<<dim3(PAIR_M / (1024 / PAIR_N), uint32_t(plan.remaining)), 256, 0, L.stream>>>(t);
     ++L.kernels;
@@ -1677,7 +1694,12 @@ bool launch_tf32x3(Launch &L, const float *a, const float *b, float *c, int64_t 
   // Converting A in shared memory repeats its TF32 conversions once per column tile,
   // so (as for the one-SM kernel) it pays only while few column tiles re-read A.
   const bool pair_raw = wide && form == Form::n256_raw_a && pair_raw_enabled();
-  const int pairs = !wide ? 0 : (pair_raw ? pair_capacity<true>(L.device) : pair_capacity<false>(L.device));
+  // The persistent grid: clusters the device holds at once with the launch's shared
+  // memory (the epilogue's staging grows with its warps).
+  const bool epilogue16 = bias || activation;
+  const int pairs = !wide ? 0
+                    : pair_raw ? (epilogue16 ? pair_capacity<true, 16>(L.device) : pair_capacity<true, 8>(L.device))
+                               : (epilogue16 ? pair_capacity<false, 16>(L.device) : pair_capacity<false, 8>(L.device));
   if (pairs)
     form = pair_raw ? Form::n256_raw_a : Form::n256;
   const bool a_split = !transposed && (form == Form::n64 || form == Form::n128 || form == Form::n256);

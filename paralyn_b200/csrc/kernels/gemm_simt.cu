@@ -468,12 +468,12 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_simt(const GemmArgs batch) {
   __shared__ __align__(16) float sa[2][BK][BM];
   __shared__ __align__(16) float sb[2][BK][BN];
   const int64_t tiles_m = (g.m + BM - 1) / BM, tiles_n = (g.n + BN - 1) / BN;
-  if (!GUARDED) {
+  if constexpr (!GUARDED) {
     simt_tile<MODE, TA, TB>(g, blockIdx.x, tiles_m, tiles_n, sa, sb);
-    return;
+  } else {
+    for (int64_t id = blockIdx.x; id < tiles_m * tiles_n; id += gridDim.x)
+      simt_tile<MODE, TA, TB>(g, id, tiles_m, tiles_n, sa, sb);
   }
-  for (int64_t id = blockIdx.x; id < tiles_m * tiles_n; id += gridDim.x)
-    simt_tile<MODE, TA, TB>(g, id, tiles_m, tiles_n, sa, sb);
 }
 
 // One block per tile, or (guarded launches) at most max_blocks blocks per matrix.

@@ -200,3 +200,26 @@ def test_prepared_operand_sizes(lib):
     assert b200.matmul_prepared_bytes(lib, 64, 256) == b200.matmul_prepared_bytes(lib, 32, 512)
     for k, n in ((0, 5), (5, 0), (1 << 31, 5), (5, 1 << 31)):
         assert b200.matmul_prepared_bytes(lib, k, n) == 0
+
+
+def test_integration_c_examples_compile(tmp_path):
+    # The C fragments of INTEGRATION.md, inside a function that declares what they use,
+    # compile against include/ (gcc, C11, warnings as errors).
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    text = (ROOT / "INTEGRATION.md").read_text()
+    blocks = re.findall(r"```c\n(.*?)```", text, re.S)
+    assert blocks
+    for i, body in enumerate(blocks):
+        source = tmp_path / f"example{i}.c"
+        source.write_text(
+            '#include "paralyn/native.h"\n#include "paralyn/tensor.h"\n#include "paralyn/b200.h"\n'
+            "void example(pr_context ctx, pr_queue queue, pr_module operators, pr_buffer w_buf, uint64_t m,\n"
+            "             uint64_t n, uint64_t k, pr_tensor_desc_v1 x, pr_tensor_desc_v1 y, pr_tensor_desc_v1 bias) {\n"
+            + body + "}\n")
+        out = subprocess.run([gcc, "-std=c11", "-Wall", "-Werror", "-fsyntax-only", "-I", str(ROOT / "include"),
+                              str(source)], capture_output=True, text=True)
+        assert out.returncode == 0, out.stderr

@@ -862,8 +862,9 @@ __global__ void __launch_bounds__(RAW ? THREADS_RAW_ONE : THREADS_PLAIN, 1)
 //  warp 1 (both CTAs): allocates 512 TMEM columns as a pair (two 256-column
 //    accumulators); lane 0 of CTA 0 issues the MMAs and commits stages and
 //    accumulators to the barriers of both CTAs.
-//  warps 2-9 (both CTAs): drain the CTA's own accumulator as in the one-SM kernel and
-//    report to CTA 0's `tmem_empty` (16 arrivals: eight warps of each CTA).
+//  warps 2 .. 1 + EW (both CTAs; EW = 8, or 16 when a bias or activation is fused):
+//    drain the CTA's own accumulator as in the one-SM kernel and report to CTA 0's
+//    `tmem_empty` (2 EW arrivals: the epilogue warps of both CTAs).
 // Every wait is bounded. Before either CTA releases its shared and tensor memory,
 // CTA 0 waits for its last MMA to finish and both CTAs meet at a cluster barrier.
 // Deep products (k >= 2048) align the pairs' rounds: CTA 0's producer waits (at most

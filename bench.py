@@ -17,8 +17,9 @@ benchmark configurations; one "step" is one pass of the path over one batch):
   attention  batched Q K^T: Q, K [32 heads, 2048, 128] ~ U[-1,1), seed 7, K^T as a strided view
              (replica per rank)
   block      the reference example's pre-LN encoder block at T = 2048 tokens, d = 1024, 16 heads,
-             d_ff = 4096, causal, in 11 launches (bias and GELU fused into the GEMMs); value =
-             the block's GEMM flops per second (replica per rank)
+             d_ff = 4096, causal, in 11 commands (bias and GELU fused into the GEMMs; the four
+             projection weights prepared once unless --split-w-per-step); value = the block's
+             GEMM flops per second (replica per rank)
 `value` is device time (CUDA events on the library's context stream between two
 queue markers, max over ranks); `e2e` times the same steps through the public API
 with pinned host inputs copied in and results copied out every step. Under
@@ -227,8 +228,8 @@ def describe(name, world, rank, gather=False):
     if name == "block":
         return METRICS[name], "TFLOP/s", "weak", {
             "workload": "block: pre-LN encoder block (reference examples/native/transformer_block), T=2048, d=1024, "
-                        "16 heads of 64, d_ff=4096, causal, seeded weights; 11 launches per block (bias/GELU fused "
-                        "into the GEMM epilogues)",
+                        "16 heads of 64, d_ff=4096, causal, seeded weights; 11 commands per block (bias/GELU fused "
+                        "into the GEMM epilogues; how the weights are read: the line's w_operand)",
             "tokens": 2048, "d_model": 1024, "heads": 16, "d_ff": 4096, "parallelism": f"replica{world}",
             "l2": "scores and probabilities 256 MiB each exceed L2"}
     if name == "attention":

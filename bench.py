@@ -1,7 +1,7 @@
 """Benchmark of the FP32 operator path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload chain|gemm|layernorm|affine|add]
-                    [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload chain|gemm|layernorm|affine|add|softmax|reduce|attention|block]
 
 Workloads (synthetic seeded inputs with the shapes and distributions of the
 benchmark configurations; one "step" is one pass of the path over one batch):

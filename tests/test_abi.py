@@ -223,3 +223,19 @@ def test_integration_c_examples_compile(tmp_path):
         out = subprocess.run([gcc, "-std=c11", "-Wall", "-Werror", "-fsyntax-only", "-I", str(ROOT / "include"),
                               str(source)], capture_output=True, text=True)
         assert out.returncode == 0, out.stderr
+
+
+def test_integration_binding_stubs_cover_every_b200_entry():
+    # The ctypes stubs INTEGRATION.md gives a maintainer parse as Python and name every
+    # pr_b200_* function include/paralyn/b200.h declares, and nothing else.
+    import ast
+    text = (ROOT / "INTEGRATION.md").read_text()
+    stubs = next(b for b in re.findall(r"```python\n(.*?)```", text, re.S) if "optional = {" in b)
+    tree = ast.parse(stubs)
+    names = set()
+    for node in ast.walk(tree):
+        if isinstance(node, ast.Dict):
+            names |= {k.value for k in node.keys if isinstance(k, ast.Constant) and isinstance(k.value, str)}
+    header = (ROOT / "include" / "paralyn" / "b200.h").read_text()
+    declared = set(re.findall(r"\b(pr_b200_\w+)\s*\(", header))
+    assert names == declared, (sorted(declared - names), sorted(names - declared))

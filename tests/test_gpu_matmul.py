@@ -157,12 +157,15 @@ def test_split_tail_tiles_meet_fp32_contract(context, m, n, k):
 @pytest.mark.parametrize("mode", (p.MatmulMode.REFERENCE, p.MatmulMode.FFMA, p.MatmulMode.TF32X3, p.MatmulMode.AUTO))
 @pytest.mark.parametrize("m,n,k,ta,tb", [(129, 65, 257, False, False), (300, 260, 96, True, False),
                                          (2432, 2048, 256, False, True), (64, 40, 0, False, False),
-                                         (300, 64, 96, False, False), (1000, 100, 2048, False, True)])
+                                         (300, 64, 96, False, False), (1000, 100, 2048, False, True),
+                                         (600, 300, 512, False, False)])
 def test_fused_bias_activation_equals_two_commands(context, mode, m, n, k, ta, tb):
     # One command (GEMM epilogue adds the bias and applies the activation) against
     # pr_matmul_f32 followed by pr_bias_activation_f32: identical bits, every mode,
-    # including the split tail tiles (2432 x 2048), k = 0 and narrow C computed
-    # transposed (n = 64 and n = 100, the latter with split k-ranges).
+    # including the split tail tiles (2432 x 2048), k = 0, narrow C computed
+    # transposed (n = 64 and n = 100, the latter with split k-ranges) and CTA pairs
+    # converting A in shared memory (600 x 300: two column tiles), whose fused
+    # epilogue runs on sixteen warps per CTA.
     p.set_matmul_mode(context, mode)
     res = T.operators_of(context)
     D = T.TensorDescriptor
